@@ -1,0 +1,370 @@
+"""Benchmark of the hot path on B200 (driver contract: one JSON line).
+
+Default workload (C1): W4A16 decode GEMV, x fp16
+[M, 4096] @ int4 group-128 weights [4096, 11008] with fp16 scales.  One
+"step" is one pass of the decode path over a stack of L = 32 distinct weight
+copies (like 32 layers; 745 MB in all, far larger than the 126 MB L2, so
+every GEMV streams its weights from HBM), replayed as one CUDA graph.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--m M]
+  python bench.py --impl reference ...   # the reference's CPU algorithm
+
+Multi-GPU (torchrun, one process per GPU): each rank owns its own column
+shard of weights (weak scaling, no collective in the data path); the value is
+the bytes all ranks streamed over the max-over-ranks device time.
+
+Other workloads (--workload): see WORKLOADS below.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "triton-metal_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+PEAKS_FILE = os.path.join(REPO, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# DRAM bytes per launch of the dominant kernel, from the committed ncu
+# summaries in profiles/ (None until captured for that workload).
+NCU_TRAFFIC = {
+    "w4a16_gemv": None,
+}
+
+
+def peaks():
+    if os.path.exists(PEAKS_FILE):
+        with open(PEAKS_FILE) as f:
+            p = json.load(f)
+        p["source"] = "measured"
+        return p
+    p = dict(FALLBACK_PEAKS)
+    p["source"] = "fallback"
+    return p
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+def dist_init(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------
+# clocks sampling during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip().replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# workload: W4A16 decode GEMV (C1)
+# --------------------------------------------------------------------------
+W4_N, W4_K, W4_G, W4_LAYERS = 11008, 4096, 128, 32
+
+
+def w4_gemv_bytes(M, N=W4_N, K=W4_K, G=W4_G):
+    """Algorithmic HBM bytes of one GEMV: packed weights + scales + x + out."""
+    return (K // 8) * N * 4 + (K // G) * N * 2 + M * K * 2 + M * N * 2
+
+
+class W4Gemv:
+    name = "w4a16_gemv"
+    metric = "W4A16 decode GEMV HBM throughput"
+    unit = "GB/s"
+    dtype = "fp16"
+    bound = "hbm"
+
+    def __init__(self, M, rank):
+        import b200kern as bk
+        from b200kern import _lib
+        from b200kern.synthetic import w4_inputs
+        self.bk, self.lib, self.M = bk, _lib, M
+        d = w4_inputs(M, W4_N, W4_K, W4_G, dtype=torch.float16, seed=rank)
+        dev = torch.device("cuda")
+        base_w = d["qweight"].to(dev)
+        base_s = d["scales"].to(dev)
+        self.qw = [base_w ^ ((i * 0x2545F491) & 0x7FFFFFFF) if i else base_w for i in range(W4_LAYERS)]
+        self.sc = [base_s.clone() for _ in range(W4_LAYERS)]
+        g = torch.Generator().manual_seed(1000 + rank)
+        self.x_host = torch.randn(W4_LAYERS, M, W4_K, generator=g).half().pin_memory()
+        self.x = self.x_host.to(dev)
+        self.out = torch.empty(W4_LAYERS, M, W4_N, dtype=torch.float16, device=dev)
+        self.out_host = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.step_bytes = W4_LAYERS * w4_gemv_bytes(M)
+        self.launches_per_step = W4_LAYERS
+        self.cfg = {"workload": f"w4a16_gemv M={M} K={W4_K} N={W4_N} G={W4_G}",
+                    "layers_per_step": W4_LAYERS, "weight_bytes_resident": W4_LAYERS * (W4_K // 8) * W4_N * 4,
+                    "l2": "inputs larger than L2 (32 distinct weight copies, 745 MB, streamed per step)"}
+
+    def launch(self, i, stream):
+        self.lib.call("b2_int4_matmul", self.x[i].data_ptr(), self.qw[i].data_ptr(), self.out[i].data_ptr(),
+                      self.sc[i].data_ptr(), None, self.M, W4_N, W4_K, W4_G, 0, stream)
+
+    def step(self, stream):
+        for i in range(W4_LAYERS):
+            self.launch(i, stream)
+
+    def e2e_step(self):
+        """Public API, host buffers: H2D of the step's x, 32 ops, D2H of outputs."""
+        xd = self.x_host.to("cuda", non_blocking=True)
+        for i in range(W4_LAYERS):
+            self.bk.int4_matmul(xd[i], self.qw[i], self.sc[i], group_size=W4_G, out=self.out[i])
+        self.out_host.copy_(self.out, non_blocking=True)
+        return self.x_host.numel() * 2, self.out.numel() * 2
+
+    def kernel_bytes(self):
+        return w4_gemv_bytes(self.M)
+
+    def check(self):
+        """Spot parity of layer 0 against the oracle (fp64) before timing."""
+        import numpy as np
+        from oracle import quant as oq
+        torch.cuda.synchronize()
+        q = self.bk.unpack_int4_gptq(self.qw[0].cpu()).numpy()
+        ref = oq.int4_matmul(self.x[0].double().cpu().numpy(), q, self.sc[0].double().cpu().numpy(), None, W4_G)
+        got = self.out[0].double().cpu().numpy()
+        return bool(np.allclose(got, ref, rtol=1e-2, atol=1e-2))
+
+    def cpu_baseline(self, budget_s=10.0):
+        """The reference's dequant-then-matmul (fp32 torch restatement,
+        oracle/quant.py) on the host cores, one GEMV per call."""
+        from oracle import quant as oq
+        threads = os.cpu_count()
+        torch.set_num_threads(threads)
+        q = self.bk.unpack_int4_gptq(self.qw[0].cpu()).to(torch.int32)
+        s = self.sc[0].cpu()
+        x = self.x_host[0]
+        oq.int4_matmul_fp32_torch(x, q, s, None, W4_G)  # warm
+        n, t0 = 0, time.perf_counter()
+        while True:
+            oq.int4_matmul_fp32_torch(x, q, s, None, W4_G)
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or n >= 200:
+                break
+        return {"value": n * w4_gemv_bytes(self.M) / el / 1e9, "unit": "GB/s", "cores": threads,
+                "kind": "port", "sample": f"{n} GEMVs M={self.M} K={W4_K} N={W4_N} in {el:.1f} s "
+                                          "(fp32 dequant-then-matmul, torch on all host threads)"}
+
+
+WORKLOADS = {"w4a16_gemv": W4Gemv}
+
+
+def make_workload(args, rank):
+    if args.workload == "w4a16_gemv":
+        return W4Gemv(args.m, rank)
+    raise SystemExit(f"unknown workload {args.workload}")
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
+def run_ours(args):
+    rank, world, local = dist_init(args.gpus)
+    wl = make_workload(args, rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    # eager run + parity spot check, then capture one step as a CUDA graph
+    with torch.cuda.stream(stream):
+        wl.step(stream.cuda_stream)
+    stream.synchronize()
+    parity_ok = wl.check()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        wl.step(stream.cuda_stream)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K graph replays ----
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, world)
+    value = wl.step_bytes * args.steps * world / (ms_max / 1e3) / 1e9
+
+    # ---- per-launch kernel time of the dominant kernel (events around each) ----
+    reps = max(3, min(20, args.steps // 10))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps * wl.launches_per_step)]
+    with torch.cuda.stream(stream):
+        j = 0
+        for _ in range(reps):
+            for i in range(wl.launches_per_step):
+                evs[j][0].record(stream)
+                wl.launch(i, stream.cuda_stream)
+                evs[j][1].record(stream)
+                j += 1
+    torch.cuda.synchronize()
+    k_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    pk = peaks()
+    achieved = wl.kernel_bytes() / (k_ms / 1e3) / 1e9
+    roof = {"bound": wl.bound, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": NCU_TRAFFIC.get(wl.name),
+            "peak_source": f"{pk['source']} (burst copy bandwidth)", "kernel_us": round(k_ms * 1e3, 3)}
+
+    # ---- e2e through the public API with host buffers ----
+    e2e_steps = max(3, min(args.steps, 200))
+    for _ in range(2):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        h2d, d2h = wl.e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e = {"value": round(wl.step_bytes * e2e_steps * world / (e_ms / 1e3) / 1e9, 1), "unit": wl.unit,
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps}
+
+    line = None
+    if rank == 0:
+        cpu = wl.cpu_baseline(args.cpu_budget) if world == 1 else None
+        line = {"metric": wl.metric, "value": round(value, 1), "unit": wl.unit, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+                "data": "synthetic (seeded, BASELINE distributions)", "config": wl.cfg,
+                "parity_ok": parity_ok, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": wl.launches_per_step * args.steps, "clocks": clk.summary()}
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return line
+
+
+# --------------------------------------------------------------------------
+# reference arm: the reference's algorithm on the host cores
+# --------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    from oracle import quant as oq
+    import b200kern as bk
+    from b200kern.synthetic import w4_inputs
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    d = w4_inputs(args.m, W4_N, W4_K, W4_G, dtype=torch.float16, seed=0)
+    q = d["q"]
+    for _ in range(args.warmup):
+        oq.int4_matmul_fp32_torch(d["x"], q, d["scales"], None, W4_G)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oq.int4_matmul_fp32_torch(d["x"], q, d["scales"], None, W4_G)
+    el = time.perf_counter() - t0
+    value = args.steps * w4_gemv_bytes(args.m) / el / 1e9
+    sample = (f"{args.steps} GEMVs (one per step) M={args.m} K={W4_K} N={W4_N}: the reference's "
+              "dequant-then-matmul (tests/test_emitter.py:3068-3079) restated in fp32 torch")
+    return {"metric": W4Gemv.metric, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded, BASELINE distributions)",
+            "config": {"workload": f"w4a16_gemv M={args.m} K={W4_K} N={W4_N} G={W4_G}"},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="w4a16_gemv", choices=sorted(WORKLOADS))
+    ap.add_argument("--m", type=int, default=1, help="GEMV rows (decode batch), 1..16")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        args.steps = min(args.steps, 20)
+        args.warmup = min(args.warmup, 3)
+        line = run_reference(args)
+    else:
+        line = run_ours(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

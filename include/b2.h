@@ -1,0 +1,134 @@
+/*
+ * b2.h — C ABI of the B200-native (sm_100a) hot-path kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as void*.  Nothing here allocates device memory; the caller owns
+ * every buffer, including the output (the convention of the reference's
+ * Metal templates, where the caller binds every buffer by index:
+ * triton_metal/codegen/_msl_templates.py:2705-2712 for INT4/INT8,
+ * :1625-1630 for FlashAttention, :2086-2091 for GQA decode).
+ *
+ * Return value: B2_OK (0) or a negative B2_ERR_* code.  The message of the
+ * last failure on the calling thread is returned by b2_last_error().
+ * All launches are asynchronous on the given stream; no host sync inside.
+ */
+#ifndef B2_H_
+#define B2_H_
+
+#include <stdint.h>
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define B2_API __attribute__((visibility("default")))
+#else
+#define B2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define B2_OK               0
+#define B2_ERR_INVALID    (-1)  /* bad shape / argument */
+#define B2_ERR_DTYPE      (-2)  /* unsupported dtype combination */
+#define B2_ERR_ALIGN      (-3)  /* pointer or stride alignment */
+#define B2_ERR_UNSUPPORTED (-4) /* valid but not implemented shape */
+#define B2_ERR_LAUNCH     (-5)  /* CUDA launch / runtime error */
+#define B2_ERR_TIMEOUT    (-6)  /* a bounded device wait ran out */
+
+/* dtype codes for activations / scales / outputs */
+#define B2_F16  0
+#define B2_BF16 1
+#define B2_F32  2
+
+/* int4 weight layouts */
+#define B2_LAYOUT_GPTQ 0  /* int32 [K/8, N], nibble j of a word = k%8 == j   */
+#define B2_LAYOUT_REF  1  /* uint8 [N, K/2], low nibble = even k (reference) */
+
+B2_API int         b2_version(void);
+B2_API const char* b2_last_error(void);
+
+/*
+ * W4A16 group-wise weight-only matmul: output[M,N] = input[M,K] @ W
+ * with W[k,n] = (q[k,n] - z[k/G,n]) * scales[k/G,n].
+ * Replaces the reference kernel int4_matmul
+ * (triton_metal/codegen/_msl_templates.py:2682-2745, buffer order
+ * input, weight, output, scales, zeros, M, N, K at :2705-2712).
+ *   weight  : B2_LAYOUT_GPTQ int32 [K/8, N]
+ *   scales  : dtype [K/G, N]
+ *   zeros   : NULL -> symmetric zero point 8 (the layout's default);
+ *             else dtype [K/G, N] zero points (asymmetric).
+ *   dtype   : B2_F16 or B2_BF16 for input, scales, zeros and output.
+ * Chooses the decode GEMV (M <= 16) or the tcgen05 prefill GEMM (M > 16).
+ */
+B2_API int b2_int4_matmul(const void* input, const void* weight, void* output,
+                   const void* scales, const void* zeros,
+                   int64_t M, int64_t N, int64_t K, int64_t group_size,
+                   int dtype, void* stream);
+
+/*
+ * W8A16 per-channel weight-only matmul: output[M,N] = input[M,K] @ W,
+ * W[k,n] = (w8[n,k] - zeros[n]) * scales[n].
+ * Replaces int8_matmul (triton_metal/codegen/_msl_templates.py:2630-2679,
+ * buffer order input, weight, output, scales, zeros, M, N, K at :2652-2661).
+ *   weight  : int8 [N, K] (K-major, the reference layout)
+ *   scales  : dtype [N];  zeros: NULL (symmetric) or dtype [N].
+ */
+B2_API int b2_int8_matmul(const void* input, const void* weight, void* output,
+                   const void* scales, const void* zeros,
+                   int64_t M, int64_t N, int64_t K,
+                   int dtype, void* stream);
+
+/*
+ * Exact int4 -> fp32 dequantisation W[k,n] = (q - z) * float(s), written
+ * as fp32 [K, N].  Debug/parity export of the unpack + dequant step the
+ * reference does per k inside int4_matmul (_msl_templates.py:2723-2737).
+ */
+B2_API int b2_int4_dequant(const void* weight, const void* scales, const void* zeros,
+                    float* out, int64_t N, int64_t K, int64_t group_size,
+                    int dtype, void* stream);
+
+/*
+ * Repack the reference int4 layout uint8 [N, K/2] (low nibble = even k,
+ * _msl_templates.py:2725-2732) into the GPTQ layout int32 [K/8, N].
+ */
+B2_API int b2_int4_repack_ref_to_gptq(const void* ref_weight, void* gptq_weight,
+                               int64_t N, int64_t K, void* stream);
+
+/*
+ * FlashAttention forward.  q [B, Hq, S, D], k/v [B, Hkv, S, D], o like q,
+ * each with arbitrary element strides (b, h, s; the last dim contiguous).
+ * GQA maps q head h to kv head h / (Hq/Hkv), the reference's head map
+ * (_msl_templates.py:2101-2104).  Replaces flash_attention
+ * (_msl_templates.py:1568-1767, buffers Q, K, V, O, seq_len, scale) and the
+ * strided Triton form _flash_attn_fwd (tests/test_flash_attention.py:24-104).
+ *   dtype : B2_BF16 / B2_F16 (tcgen05 path) or B2_F32 (fp32 in/out).
+ */
+B2_API int b2_flash_attn_fwd(const void* q, const void* k, const void* v, void* o,
+                      int64_t B, int64_t Hq, int64_t Hkv,
+                      int64_t Sq, int64_t Skv, int64_t D,
+                      const int64_t* q_strides, const int64_t* k_strides,
+                      const int64_t* v_strides, const int64_t* o_strides,
+                      float scale, int causal, int dtype, void* stream);
+
+/*
+ * KDA (chunked gated delta rule) forward.  No reference counterpart: the
+ * reference has no KDA code.  Layout [B, T, H, D] contiguous:
+ *   q, k, v : dtype (B2_BF16) [B,T,H,Dk|Dv];  g : fp32 [B,T,H,Dk] log-decay
+ *   beta    : dtype [B,T,H];  initial_state : fp32 [B,H,Dk,Dv] or NULL
+ *   o       : dtype [B,T,H,Dv];  final_state : fp32 [B,H,Dk,Dv] or NULL
+ *   workspace: device scratch of b2_kda_workspace_size(...) bytes.
+ */
+B2_API size_t b2_kda_workspace_size(int64_t B, int64_t T, int64_t H,
+                             int64_t Dk, int64_t Dv, int64_t chunk);
+B2_API int b2_kda_fwd(const void* q, const void* k, const void* v, const float* g,
+               const void* beta, const float* initial_state,
+               void* o, float* final_state, void* workspace,
+               int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv,
+               int64_t chunk, float scale, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2_H_ */

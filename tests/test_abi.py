@@ -1,0 +1,58 @@
+"""The C-ABI library loads and exports every entry point include/b2.h
+declares, with the status codes the Python side maps (no GPU needed)."""
+import ctypes
+import os
+import re
+
+from conftest import REPO, PKG_ROOT
+
+HEADER = os.path.join(REPO, "include", "b2.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return set(re.findall(r"^B2_API\s+[\w\s\*]+?\b(b2_\w+)\s*\(", src, flags=re.M))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert {"b2_int4_matmul", "b2_int8_matmul", "b2_flash_attn_fwd", "b2_kda_fwd"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    from b200kern import _lib
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in b2.h but not exported"
+    assert _declared() == set(_lib.SIGNATURES), "ctypes signatures out of sync with b2.h"
+
+
+def test_load_and_version():
+    from b200kern import _lib
+    lib = _lib.load()
+    assert lib.b2_version() >= 10000
+    assert isinstance(lib.b2_last_error(), bytes)
+
+
+def test_status_codes_match_header():
+    from b200kern import errors
+    src = open(HEADER).read()
+    codes = {m[0]: int(m[1]) for m in re.findall(r"#define (B2_(?:OK|ERR_\w+))\s+\(?(-?\d+)\)?", src)}
+    assert codes["B2_OK"] == errors.OK
+    for k, v in codes.items():
+        if k != "B2_OK":
+            assert getattr(errors, k[3:]) == v
+
+
+def test_host_validation_without_gpu():
+    """Shape checks run on the host before any launch (null stream, no GPU)."""
+    from b200kern import _lib, errors
+    lib = _lib.load()
+    # K not a multiple of the group size -> invalid, no device work
+    st = lib.b2_int4_matmul(1, 1, 1, 1, None, 1, 32, 200, 128, 0, None)
+    assert st == errors.ERR_INVALID
+    assert b"group_size" in lib.b2_last_error()
+    st = lib.b2_int4_matmul(1, 1, 1, 1, None, 1, 32, 128, 128, 7, None)
+    assert st == errors.ERR_DTYPE
+    st = lib.b2_int8_matmul(None, 1, 1, 1, None, 1, 32, 128, 0, None)
+    assert st == errors.ERR_INVALID

@@ -1,0 +1,64 @@
+"""ctypes binding of libb2.so (the C ABI declared in include/b2.h).
+
+The library is built in-tree by ``csrc/build.py``.  There is no fallback:
+if the library or a GPU is missing, every op raises.
+"""
+import ctypes
+import os
+
+from .errors import B2Error, raise_for_status
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libb2.so")
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+_pi64 = ctypes.POINTER(ctypes.c_int64)
+
+# name -> (restype, argtypes); must match include/b2.h exactly.
+SIGNATURES = {
+    "b2_version": (_i32, []),
+    "b2_last_error": (ctypes.c_char_p, []),
+    "b2_int4_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "b2_int8_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
+    "b2_int4_dequant": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
+    "b2_int4_repack_ref_to_gptq": (_i32, [_vp, _vp, _i64, _i64, _vp]),
+    "b2_flash_attn_fwd": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+                                 _pi64, _pi64, _pi64, _pi64, _f32, _i32, _i32, _vp]),
+    "b2_kda_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i64]),
+    "b2_kda_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                          _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
+}
+
+_lib = None
+
+
+def load():
+    """Load libb2.so once and bind every symbol of include/b2.h."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise B2Error(f"libb2.so not built at {LIB_PATH}: run csrc/build.py")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)  # AttributeError if the symbol is missing
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def call(name, *args):
+    """Invoke an int-returning entry point and raise on a non-zero status."""
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != 0:
+        raise_for_status(status, name, lib.b2_last_error().decode())
+    return status
+
+
+def strides_arg(t):
+    return (ctypes.c_int64 * 3)(*t)
