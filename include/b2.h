@@ -48,6 +48,12 @@ extern "C" {
 
 B2_API int         b2_version(void);
 B2_API const char* b2_last_error(void);
+/* Synchronise `stream`, then read and clear the device error word that the
+ * kernels' bounded waits set instead of hanging.  *code (may be NULL)
+ * receives the raw code.  Returns B2_OK or B2_ERR_TIMEOUT.  Counterpart of
+ * the reference's command-buffer status check
+ * (triton_metal/backend/driver.py:218-225). */
+B2_API int b2_device_error(void* stream, unsigned int* code);
 
 /*
  * W4A16 group-wise weight-only matmul: output[M,N] = input[M,K] @ W

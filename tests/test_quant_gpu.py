@@ -161,3 +161,12 @@ def test_errors_are_typed(cuda):
         bk.int4_matmul(d["x"].to(cuda), d["qweight"].to(cuda), d["scales"].to(cuda), group_size=96)
     with pytest.raises(bk.B2ShapeError):
         bk.int4_matmul(d["x"], d["qweight"], d["scales"])  # CPU tensors: no CPU path
+
+
+def test_no_bounded_wait_ran_out(cuda):
+    """No kernel's bounded mbarrier wait gave up during the tests above."""
+    import ctypes
+    from b200kern import _lib
+    code = ctypes.c_uint(0)
+    st = _lib.load().b2_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(code))
+    assert st == 0 and code.value == 0, hex(code.value)

@@ -6,11 +6,11 @@
 //   out[m,n] = sum_k x[m,k] * (q[k,n] - z[g,n]) * s[g,n],  g = k / G.
 //
 // Decode GEMV design (HBM-bound, 0.5 byte of weight per MAC):
-//   * CTA = 8 warps, tile of 32 output columns; the K groups are split
-//     across the 8 warps and the partials reduced in shared memory.
-//   * Lane (g = lane/4, t = lane%4) loads one 128-bit word of the packed
-//     weight: 4 adjacent columns x 8 k of GPTQ row (4*step + t).  A warp
-//     load therefore covers 4 rows x 128 contiguous bytes.
+//   * Persistent: one CTA per SM owns a slab of <= 128 output columns and
+//     streams it through a shared-memory ring with 2-D TMA copies (see
+//     w4_gemv_stream_kernel below).
+//   * In a stage, lane (g = lane/4, t = lane%4) reads packed words of GPTQ
+//     row (4*quad + t), columns g and g + 8 of a 16-column MMA tile.
 //   * Nibbles become exact small integers (q - 8) in the activation dtype
 //     with the magic-exponent trick (q | 0x6400 is 1024 + q in fp16,
 //     q | 0x4300 is 128 + q in bf16; one LOP3 + one packed SUB per pair).
@@ -22,11 +22,9 @@
 //   * Each group's MMA sum is exact-integer-weighted and is scaled in fp32
 //     by the group scale afterwards: acc += s * (C_g - (z - 8) * sum_g(x)).
 #include "b2_common.cuh"
+#include <string.h>
 
 namespace b2 {
-
-constexpr int kGemvWarps = 8;
-constexpr int kGemvCols = 32;
 
 template <int DT>
 struct Magic;
@@ -34,11 +32,15 @@ template <>
 struct Magic<B2_F16> {
   static constexpr uint32_t base = 0x64006400u;   // (1024, 1024)
   static constexpr uint32_t base8 = 0x64086408u;  // (1032, 1032)
+  static constexpr uint32_t one2 = 0x3C003C00u;   // (1.0, 1.0)
+  static constexpr float bias = 1024.f;
 };
 template <>
 struct Magic<B2_BF16> {
   static constexpr uint32_t base = 0x43004300u;   // (128, 128)
   static constexpr uint32_t base8 = 0x43084308u;  // (136, 136)
+  static constexpr uint32_t one2 = 0x3F803F80u;   // (1.0, 1.0)
+  static constexpr float bias = 128.f;
 };
 
 template <int DT>
@@ -56,169 +58,6 @@ __device__ __forceinline__ void x_pairs(const uint4& xv, uint32_t (&p)[4]) {
   p[1] = prmt(xv.x, xv.z, 0x7632);
   p[2] = prmt(xv.y, xv.w, 0x5410);
   p[3] = prmt(xv.y, xv.w, 0x7632);
-}
-
-// SPG = 128-bit steps per group (G = 32 * SPG); NT = n-tiles of 8 rows of M.
-template <int DT, int NT, int SPG, bool ZEROS>
-__global__ void __launch_bounds__(kGemvWarps * 32)
-w4_gemv_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ qw,
-               uint16_t* __restrict__ out, const uint16_t* __restrict__ scales,
-               const uint16_t* __restrict__ zeros, int M, int N, int K) {
-  using T = typename dtype_of<DT>::T;
-  __shared__ float red[kGemvWarps][NT * 8 * kGemvCols];
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int col0 = blockIdx.x * kGemvCols;
-  const int colbase = col0 + 4 * g;
-  const bool cvalid = colbase < N;
-  const int ngroups = K / (32 * SPG);
-  const int per_warp = (ngroups + kGemvWarps - 1) / kGemvWarps;
-  const int g_begin = warp * per_warp;
-  const int g_end = min(ngroups, g_begin + per_warp);
-
-  float acc[2][NT][4];
-#pragma unroll
-  for (int a = 0; a < 2; ++a)
-#pragma unroll
-    for (int b = 0; b < NT; ++b)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
-
-  const uint32_t* wp = qw + colbase;
-  uint4 wcur[SPG], wnext[SPG];
-  if (g_begin < g_end) {
-#pragma unroll
-    for (int s = 0; s < SPG; ++s) {
-      int row = g_begin * 4 * SPG + 4 * s + t;
-      wcur[s] = cvalid ? ld_stream_u4(wp + (size_t)row * N) : make_uint4(0, 0, 0, 0);
-    }
-  }
-
-  for (int grp = g_begin; grp < g_end; ++grp) {
-    // prefetch the next group's weights while this one is computed
-    if (grp + 1 < g_end) {
-#pragma unroll
-      for (int s = 0; s < SPG; ++s) {
-        int row = (grp + 1) * 4 * SPG + 4 * s + t;
-        wnext[s] = cvalid ? ld_stream_u4(wp + (size_t)row * N) : make_uint4(0, 0, 0, 0);
-      }
-    }
-    float sc[4], zc[4];
-    {
-      uint2 sv = cvalid ? __ldg(reinterpret_cast<const uint2*>(scales + (size_t)grp * N + colbase))
-                        : make_uint2(0, 0);
-      float2 a = unpack2<DT>(sv.x), b = unpack2<DT>(sv.y);
-      sc[0] = a.x; sc[1] = a.y; sc[2] = b.x; sc[3] = b.y;
-      if constexpr (ZEROS) {
-        uint2 zv = cvalid ? __ldg(reinterpret_cast<const uint2*>(zeros + (size_t)grp * N + colbase))
-                          : make_uint2(0, 0);
-        float2 c = unpack2<DT>(zv.x), d = unpack2<DT>(zv.y);
-        zc[0] = c.x - 8.f; zc[1] = c.y - 8.f; zc[2] = d.x - 8.f; zc[3] = d.y - 8.f;
-      }
-    }
-    float cg[2][NT][4];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int b = 0; b < NT; ++b)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) cg[a][b][c] = 0.f;
-    float xs[NT];
-#pragma unroll
-    for (int b = 0; b < NT; ++b) xs[b] = 0.f;
-
-#pragma unroll
-    for (int s = 0; s < SPG; ++s) {
-      const int row = grp * 4 * SPG + 4 * s + t;
-      uint32_t bp[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int m = g + 8 * nt;
-        uint4 xv = make_uint4(0, 0, 0, 0);
-        if (m < M) xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K + 8 * row));
-        x_pairs(xv, bp[nt]);
-        if constexpr (ZEROS) {
-          float2 a = unpack2<DT>(xv.x), b = unpack2<DT>(xv.y), c = unpack2<DT>(xv.z), d = unpack2<DT>(xv.w);
-          xs[nt] += (a.x + a.y) + (b.x + b.y) + (c.x + c.y) + (d.x + d.y);
-        }
-      }
-      const uint32_t wv[4] = {wcur[s].x, wcur[s].y, wcur[s].z, wcur[s].w};
-      uint32_t dq[4][4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          dq[c][j] = sub2<DT>(and_or(wv[c] >> (4 * j), 0x000F000Fu, Magic<DT>::base), Magic<DT>::base8);
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const uint32_t a0[4] = {dq[2 * mt][0], dq[2 * mt + 1][0], dq[2 * mt][1], dq[2 * mt + 1][1]};
-        const uint32_t a1[4] = {dq[2 * mt][2], dq[2 * mt + 1][2], dq[2 * mt][3], dq[2 * mt + 1][3]};
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const uint32_t b0[2] = {bp[nt][0], bp[nt][1]};
-          const uint32_t b1[2] = {bp[nt][2], bp[nt][3]};
-          mma_16816<DT>(cg[mt][nt], a0, b0);
-          mma_16816<DT>(cg[mt][nt], a1, b1);
-        }
-      }
-    }
-    // fold the group into the fp32 accumulator with its scale (and zero)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      float x0 = 0.f, x1 = 0.f;
-      if constexpr (ZEROS) {
-        float tot = xs[nt];
-        tot += __shfl_xor_sync(0xffffffffu, tot, 1);
-        tot += __shfl_xor_sync(0xffffffffu, tot, 2);
-        // tot = sum_g x[8nt + g]; C columns of this lane are m = 8nt+2t, +1
-        x0 = __shfl_sync(0xffffffffu, tot, (2 * t) << 2);
-        x1 = __shfl_sync(0xffffffffu, tot, (2 * t + 1) << 2);
-      }
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const float s0 = sc[2 * mt], s1 = sc[2 * mt + 1];
-        if constexpr (ZEROS) {
-          const float z0 = zc[2 * mt], z1 = zc[2 * mt + 1];
-          acc[mt][nt][0] += s0 * (cg[mt][nt][0] - z0 * x0);
-          acc[mt][nt][1] += s0 * (cg[mt][nt][1] - z0 * x1);
-          acc[mt][nt][2] += s1 * (cg[mt][nt][2] - z1 * x0);
-          acc[mt][nt][3] += s1 * (cg[mt][nt][3] - z1 * x1);
-        } else {
-          acc[mt][nt][0] += s0 * cg[mt][nt][0];
-          acc[mt][nt][1] += s0 * cg[mt][nt][1];
-          acc[mt][nt][2] += s1 * cg[mt][nt][2];
-          acc[mt][nt][3] += s1 * cg[mt][nt][3];
-        }
-      }
-    }
-#pragma unroll
-    for (int s = 0; s < SPG; ++s) wcur[s] = wnext[s];
-  }
-
-  // per-warp partials -> shared memory -> sum over warps
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      const int m = nt * 8 + 2 * t;
-      const int c = 4 * g + 2 * mt;
-      red[warp][m * kGemvCols + c] = acc[mt][nt][0];
-      red[warp][(m + 1) * kGemvCols + c] = acc[mt][nt][1];
-      red[warp][m * kGemvCols + c + 1] = acc[mt][nt][2];
-      red[warp][(m + 1) * kGemvCols + c + 1] = acc[mt][nt][3];
-    }
-  __syncthreads();
-  for (int i = threadIdx.x; i < NT * 8 * kGemvCols; i += blockDim.x) {
-    const int m = i / kGemvCols, c = i % kGemvCols;
-    float sum = 0.f;
-#pragma unroll
-    for (int w = 0; w < kGemvWarps; ++w) sum += red[w][i];
-    if (m < M && col0 + c < N) {
-      T r = from_f32<T>(sum);
-      out[(size_t)m * N + col0 + c] = *reinterpret_cast<uint16_t*>(&r);
-    }
-  }
 }
 
 // Generic kernel: one thread per output, any M/N/K/G, GPTQ layout.  Used for
@@ -279,45 +118,383 @@ __global__ void w4_repack_kernel(const uint8_t* __restrict__ ref, uint32_t* __re
   gptq[idx] = lo;
 }
 
-template <int DT, int NT, int SPG>
-static void launch_gemv(const void* x, const void* w, void* out, const void* s, const void* z,
-                        int M, int N, int K, cudaStream_t st) {
-  dim3 grid((N + kGemvCols - 1) / kGemvCols);
-  if (z)
-    w4_gemv_kernel<DT, NT, SPG, true><<<grid, kGemvWarps * 32, 0, st>>>(
-        (const uint16_t*)x, (const uint32_t*)w, (uint16_t*)out, (const uint16_t*)s, (const uint16_t*)z, M, N, K);
-  else
-    w4_gemv_kernel<DT, NT, SPG, false><<<grid, kGemvWarps * 32, 0, st>>>(
-        (const uint16_t*)x, (const uint32_t*)w, (uint16_t*)out, (const uint16_t*)s, nullptr, M, N, K);
-}
+// Persistent streaming GEMV.  One CTA per SM owns a slab of columns
+// [c0, c0 + w) (w <= 128, a multiple of 8).  The last warp (one elected
+// lane) streams the slab through a ring of shared-memory stages with 2-D TMA
+// tensor copies: one box of [G/8 rows x w columns] per quantisation group,
+// plus one box holding the slab's whole [K/G x w] scale (and zero) block.
+// Consumer warp w takes stage lane w % 8 (stages w%8, w%8 + 8, ...) and
+// column half w / 8 (NCH = 2 halves for M <= 8, 1 for M <= 16): more warps
+// per SM to issue the dequant + MMA work, which is what bounds this kernel
+// once the copy engine keeps the weight stream in flight.
+//
+// Dequant is 7 integer ops per 32-bit word: each nibble pair becomes the
+// exact fp16/bf16 value (bias + q) (bias = 1024 / 128) with one LOP3; the
+// MMA then computes sum x*(bias+q) and the bias (and zero point) is removed
+// per group with one extra MMA against a ones matrix, sum_k x:
+//   sum_k x (q - z) = sum_k x (bias + q) - (bias + z) sum_k x.
+// Both MMA products are exact and accumulate in fp32.
+//
+// Column mapping: in a 16-column MMA tile, A row g is smem column 2g and
+// row g + 8 is column 2g + 1, so a lane fetches both words with one 64-bit
+// shared load and both scales with one 32-bit load.
+constexpr int kStageLanes = 8;
+constexpr int kMaxColTiles = 16;  // 8-column tiles per CTA -> <= 128 columns
+constexpr int kMaxMt = kMaxColTiles / 2;
+
+struct GemvMaps {
+  CUtensorMap w[2], s[2], z[2];  // [0]: CTAs with the wider slab, [1]: the rest
+};
 
 template <int DT>
-static int gemv_dispatch(const void* x, const void* w, void* out, const void* s, const void* z,
-                         int M, int N, int K, int G, cudaStream_t st) {
-  const int spg = G / 32;
-#define B2_SPG_CASE(S)                                      \
-  case S:                                                   \
-    if (M <= 8) launch_gemv<DT, 1, S>(x, w, out, s, z, M, N, K, st); \
-    else launch_gemv<DT, 2, S>(x, w, out, s, z, M, N, K, st);        \
-    break;
-  switch (spg) {
-    B2_SPG_CASE(1)
-    B2_SPG_CASE(2)
-    B2_SPG_CASE(4)
-    B2_SPG_CASE(8)
-    default: return B2_ERR_UNSUPPORTED;
+__device__ __forceinline__ void biased_pairs(uint32_t w, uint32_t (&d)[4]) {
+  d[0] = and_or(w, 0x000F000Fu, Magic<DT>::base);
+  d[1] = and_or(w >> 4, 0x000F000Fu, Magic<DT>::base);
+  d[2] = and_or(w >> 8, 0x000F000Fu, Magic<DT>::base);
+  d[3] = and_or(w >> 12, 0x000F000Fu, Magic<DT>::base);
+}
+
+template <int NCH>
+constexpr int gemv_threads() { return (kStageLanes * NCH + 1) * 32; }
+
+// Two CTAs per SM when M <= 8, so that the CTAs of the next launch in a
+// stream (programmatic dependent launch) can start streaming their weights
+// while this launch's CTAs finish.
+template <int NT>
+constexpr int gemv_min_blocks() { return NT == 1 ? 2 : 1; }
+
+// RQ = row quads per stage (G / 32); NT = 8-row tiles of M; NCH = column halves.
+template <int DT, int NT, int RQ, int NCH, bool ZEROS>
+__global__ void __launch_bounds__(gemv_threads<NCH>(), gemv_min_blocks<NT>())
+w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __restrict__ x,
+                      uint16_t* __restrict__ out, int M, int N, int K, int tiles_base, int tiles_rem,
+                      int stages, unsigned* err) {
+  using T = typename dtype_of<DT>::T;
+  using T2 = typename dtype_of<DT>::T2;
+  constexpr int R = 4 * RQ;                // weight rows (of 8 k) per stage
+  constexpr int NCONS = kStageLanes * NCH;  // consumer warps
+  constexpr int MPW = kMaxMt / NCH;         // m-tiles per consumer warp (max)
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x;
+  const int wide = b < tiles_rem ? 0 : 1;
+  const int tile0 = b * tiles_base + min(b, tiles_rem);
+  const int sw = (tiles_base + (wide == 0 ? 1 : 0)) * 8;  // slab width == smem row stride
+  const int c0 = tile0 * 8;
+  const int ncols = min(sw, N - c0);
+  const int ngroups = K / (8 * R);
+  const int max_sw = (tiles_base + (tiles_rem ? 1 : 0)) * 8;
+  const int sblk = ((ngroups * max_sw * 2) + 127) / 128 * 128;  // scale block bytes
+  const int slot_bytes = R * max_sw * 4;
+  uint8_t* ring = smem + sblk * (ZEROS ? 2 : 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)stages * slot_bytes);
+  uint64_t* empty = full + stages;
+  uint64_t* sbar = empty + stages;
+  // Let the next launch in the stream start as soon as SM resources allow;
+  // it only streams weights until its own griddepcontrol.wait.
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (ncols <= 0) return;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NCH);
+    }
+    mbar_init(sbar, 1);
+    fence_mbar_init();
   }
-#undef B2_SPG_CASE
+  __syncthreads();
+
+  if (warp == NCONS) {
+    // ---------------- producer (one lane) ----------------
+    if (lane != 0) return;
+    const uint64_t pol = policy_evict_first();
+    mbar_arrive_expect_tx(sbar, ngroups * sw * 2 * (ZEROS ? 2 : 1));
+    tma_load_2d(smem, &maps.s[wide], c0, 0, sbar);
+    if constexpr (ZEROS) tma_load_2d(smem + sblk, &maps.z[wide], c0, 0, sbar);
+    for (int s = 0; s < ngroups; ++s) {
+      const int slot = s % stages;
+      if (s >= stages && !mbar_wait(&empty[slot], ((s / stages) - 1) & 1, err, 0xB2000001u)) return;
+      mbar_arrive_expect_tx(&full[slot], R * sw * 4);
+      tma_load_2d_hint(ring + (size_t)slot * slot_bytes, &maps.w[wide], c0, s * R, &full[slot], pol);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, t = lane & 3;
+  const int sid = warp % kStageLanes, ch = warp / kStageLanes;
+  const int nmt = (ncols + 15) / 16;
+  const uint32_t ones[4] = {Magic<DT>::one2, Magic<DT>::one2, Magic<DT>::one2, Magic<DT>::one2};
+  float acc[MPW][NT][4];
+#pragma unroll
+  for (int a = 0; a < MPW; ++a)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][n][c] = 0.f;
+
+  // x (and the output we overwrite) may be produced / still read by the
+  // previous kernel in the stream: wait for it before touching either.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  bool alive = mbar_wait(sbar, 0, err, 0xB2000003u);
+  for (int s = sid; s < ngroups && alive; s += kStageLanes) {
+    const int slot = s % stages;
+    // x fragments of this group (L2 hits), loaded before the stage wait
+    uint32_t bp[RQ][NT][4];
+#pragma unroll
+    for (int rq = 0; rq < RQ; ++rq) {
+      const int row = s * R + 4 * rq + t;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int m = g + 8 * n;
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (m < M) xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K + 8 * row));
+        x_pairs(xv, bp[rq][n]);
+      }
+    }
+    // ds[n][.] = sum over the group's k of x[m], m = 8n + 2t (+1), via MMA
+    float ds[NT][2][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ds[n][j][c] = 0.f;
+#pragma unroll
+    for (int rq = 0; rq < RQ; ++rq)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint32_t b0[2] = {bp[rq][n][0], bp[rq][n][1]};
+        const uint32_t b1[2] = {bp[rq][n][2], bp[rq][n][3]};
+        mma_16816<DT>(ds[n][0], ones, b0);
+        mma_16816<DT>(ds[n][1], ones, b1);
+      }
+    if (!mbar_wait(&full[slot], (s / stages) & 1, err, 0xB2000002u)) {
+      alive = false;
+      break;
+    }
+    const uint32_t* wsm = reinterpret_cast<const uint32_t*>(ring + (size_t)slot * slot_bytes);
+    const T* ssm = reinterpret_cast<const T*>(smem) + (size_t)s * sw;
+    const T* zsm = reinterpret_cast<const T*>(smem + sblk) + (size_t)s * sw;
+#pragma unroll
+    for (int ip = 0; ip < MPW; ip += 2) {
+      if (ch + NCH * ip < nmt) {
+        // two m-tiles x two k-steps -> 4*NT independent MMA chains
+        float cg[2][2][NT][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) cg[i][j][n][c] = 0.f;
+        uint2 wv[2][RQ];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int col = 16 * (ch + NCH * (ip + i)) + 2 * g;
+#pragma unroll
+          for (int rq = 0; rq < RQ; ++rq)
+            wv[i][rq] = col < ncols ? *reinterpret_cast<const uint2*>(wsm + (4 * rq + t) * sw + col)
+                                    : make_uint2(0, 0);
+        }
+#pragma unroll
+        for (int rq = 0; rq < RQ; ++rq) {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            uint32_t da[4], db[4];
+            biased_pairs<DT>(wv[i][rq].x, da);
+            biased_pairs<DT>(wv[i][rq].y, db);
+            const uint32_t a0[4] = {da[0], db[0], da[1], db[1]};
+            const uint32_t a1[4] = {da[2], db[2], da[3], db[3]};
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+              const uint32_t b0[2] = {bp[rq][n][0], bp[rq][n][1]};
+              const uint32_t b1[2] = {bp[rq][n][2], bp[rq][n][3]};
+              mma_16816<DT>(cg[i][0][n], a0, b0);
+              mma_16816<DT>(cg[i][1][n], a1, b1);
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int col = 16 * (ch + NCH * (ip + i)) + 2 * g;
+          const bool v = col < ncols;
+          float2 sc = make_float2(0.f, 0.f), bz = make_float2(Magic<DT>::bias + 8.f, Magic<DT>::bias + 8.f);
+          if (v) {
+            T2 sv = *reinterpret_cast<const T2*>(ssm + col);
+            sc = make_float2(to_f32<T>(sv.x), to_f32<T>(sv.y));
+            if constexpr (ZEROS) {
+              T2 zv = *reinterpret_cast<const T2*>(zsm + col);
+              bz = make_float2(Magic<DT>::bias + to_f32<T>(zv.x), Magic<DT>::bias + to_f32<T>(zv.y));
+            }
+          }
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            const float d0 = ds[n][0][0] + ds[n][1][0], d1 = ds[n][0][1] + ds[n][1][1];
+            float* ac = acc[ip + i][n];
+            ac[0] += sc.x * ((cg[i][0][n][0] + cg[i][1][n][0]) - bz.x * d0);
+            ac[1] += sc.x * ((cg[i][0][n][1] + cg[i][1][n][1]) - bz.x * d1);
+            ac[2] += sc.y * ((cg[i][0][n][2] + cg[i][1][n][2]) - bz.y * d0);
+            ac[3] += sc.y * ((cg[i][0][n][3] + cg[i][1][n][3]) - bz.y * d1);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+
+  // every stage (and the scale block) was waited for -> smem is free again
+  asm volatile("bar.sync 1, %0;" ::"n"(NCONS * 32));
+  constexpr int CW = kMaxColTiles * 8;           // max slab width
+  float* red = reinterpret_cast<float*>(smem);  // [stage lane][NT*8][CW]
+  constexpr int RS = NT * 8 * CW;
+#pragma unroll
+  for (int i = 0; i < MPW; ++i) {
+    const int col = 16 * (ch + NCH * i) + 2 * g;
+    if (col < CW) {
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int m = 8 * n + 2 * t;
+        float* r = red + sid * RS;
+        r[m * CW + col] = acc[i][n][0];
+        r[(m + 1) * CW + col] = acc[i][n][1];
+        r[m * CW + col + 1] = acc[i][n][2];
+        r[(m + 1) * CW + col + 1] = acc[i][n][3];
+      }
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(NCONS * 32));
+  for (int i = threadIdx.x; i < NT * 8 * CW; i += NCONS * 32) {
+    const int m = i / CW, c = i % CW;
+    if (m >= M || c >= ncols) continue;
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kStageLanes; ++w) sum += red[w * RS + i];
+    T r = from_f32<T>(sum);
+    out[(size_t)m * N + c0 + c] = *reinterpret_cast<uint16_t*>(&r);
+  }
+}
+
+constexpr int kSmemBudgetNT1 = 110 * 1024;  // two CTAs per SM (PDL overlap)
+constexpr int kSmemBudgetNT2 = 227 * 1024;
+constexpr int kMaxStages = 64;
+
+struct GemvPlan {
+  int grid, base, rem, stages;
+  size_t smem;
+};
+
+// Column-slab split over the SMs and shared-memory ring size for one shape.
+static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p) {
+  const int budget = nt == 1 ? kSmemBudgetNT1 : kSmemBudgetNT2;
+  // one CTA per SM; each owns a slab of <= 128 columns (8-column granules)
+  const int tiles8 = N / 8;
+  int ctas = num_sms();
+  if (tiles8 < ctas) ctas = tiles8;
+  int base = tiles8 / ctas, rem = tiles8 % ctas;
+  if (base + (rem ? 1 : 0) > kMaxColTiles) {  // very wide N: more CTAs than SMs
+    ctas = (tiles8 + kMaxColTiles - 1) / kMaxColTiles;
+    base = tiles8 / ctas;
+    rem = tiles8 % ctas;
+  }
+  const int max_sw = (base + (rem ? 1 : 0)) * 8;
+  const int rows = G / 8, ngroups = K / G;
+  if (ngroups > 256) return false;  // TMA box dimension limit of the scale block
+  const size_t sblk = ((size_t)ngroups * max_sw * 2 + 127) / 128 * 128;
+  const size_t slot = (size_t)rows * max_sw * 4;
+  const size_t fixed = sblk * (zeros ? 2 : 1);
+  int stages = (int)((budget - fixed - 256) / (slot + 16));
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages > ngroups) stages = ngroups;
+  if (stages < 1) return false;
+  size_t total = fixed + (size_t)stages * (slot + 16) + 16;
+  const size_t red = (size_t)kStageLanes * nt * 8 * kMaxColTiles * 8 * 4;
+  if (total < red) total = red;
+  p->grid = ctas;
+  p->base = base;
+  p->rem = rem;
+  p->stages = stages;
+  p->smem = total;
+  return total <= (size_t)budget;
+}
+
+template <int DT, int NT, int RQ, int NCH, bool ZEROS>
+static int launch_stream(const void* x, const void* w, void* out, const void* s, const void* z, int M, int N, int K,
+                         int G, cudaStream_t st) {
+  GemvPlan p;
+  if (!gemv_plan(N, K, G, ZEROS, NT, &p)) return B2_ERR_UNSUPPORTED;
+  unsigned* err = device_error_word();
+  if (!err) {
+    set_error("w4_gemv: cannot resolve the device error word");
+    return B2_ERR_LAUNCH;
+  }
+  const int ngroups = K / G, rows = G / 8;
+  const CUtensorMapDataType sdt = DT == B2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  GemvMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  const int widths[2] = {(p.base + 1) * 8, p.base * 8};
+  for (int i = 0; i < 2; ++i) {
+    const int wdt = widths[i];
+    if (wdt == 0 || (i == 0 && p.rem == 0)) continue;
+    if (!make_tmap_2d(&maps.w[i], w, CU_TENSOR_MAP_DATA_TYPE_UINT32, N, K / 8, (uint64_t)N * 4, wdt, rows) ||
+        !make_tmap_2d(&maps.s[i], s, sdt, N, ngroups, (uint64_t)N * 2, wdt, ngroups) ||
+        (ZEROS && !make_tmap_2d(&maps.z[i], z, sdt, N, ngroups, (uint64_t)N * 2, wdt, ngroups)))
+      return B2_ERR_INVALID;
+  }
+  auto kern = w4_gemv_stream_kernel<DT, NT, RQ, NCH, ZEROS>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  // Programmatic dependent launch: may overlap the previous kernel of the
+  // stream; the kernel itself orders every dependent access after
+  // griddepcontrol.wait (a no-op when the previous kernel did not trigger).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(gemv_threads<NCH>());
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, maps, (const uint16_t*)x, (uint16_t*)out, M, N, K, p.base, p.rem, p.stages, err);
   return launch_status("w4_gemv");
 }
 
-// Returns true when the decode GEMV's layout constraints hold.
-static bool gemv_ok(const void* x, const void* w, const void* s, const void* z,
-                    int64_t M, int64_t N, int64_t K, int64_t G) {
-  return M >= 1 && M <= 16 && N % 4 == 0 && K % G == 0 && G % 32 == 0 && G / 32 <= 8 &&
-         (G / 32 & (G / 32 - 1)) == 0 && aligned(x, 16) && aligned(w, 16) && aligned(s, 8) &&
-         (!z || aligned(z, 8));
+template <int DT, int RQ>
+static int gemv_nt(const void* x, const void* w, void* out, const void* s, const void* z, int M, int N, int K, int G,
+                   cudaStream_t st) {
+  if (M <= 8)
+    return z ? launch_stream<DT, 1, RQ, 1, true>(x, w, out, s, z, M, N, K, G, st)
+             : launch_stream<DT, 1, RQ, 1, false>(x, w, out, s, z, M, N, K, G, st);
+  return z ? launch_stream<DT, 2, RQ, 1, true>(x, w, out, s, z, M, N, K, G, st)
+           : launch_stream<DT, 2, RQ, 1, false>(x, w, out, s, z, M, N, K, G, st);
 }
+
+template <int DT>
+static int gemv_dispatch(const void* x, const void* w, void* out, const void* s, const void* z, int M, int N, int K,
+                         int G, cudaStream_t st) {
+  switch (G / 32) {
+    case 1: return gemv_nt<DT, 1>(x, w, out, s, z, M, N, K, G, st);
+    case 2: return gemv_nt<DT, 2>(x, w, out, s, z, M, N, K, G, st);
+    case 4: return gemv_nt<DT, 4>(x, w, out, s, z, M, N, K, G, st);
+    case 8: return gemv_nt<DT, 8>(x, w, out, s, z, M, N, K, G, st);
+    default: return B2_ERR_UNSUPPORTED;
+  }
+}
+
+// Layout constraints of the streaming GEMV (TMA: 16-byte aligned rows/boxes).
+static bool gemv_ok(const void* x, const void* w, const void* s, const void* z, int64_t M, int64_t N, int64_t K,
+                    int64_t G) {
+  const int64_t spg = G / 32;
+  return M >= 1 && M <= 16 && N % 8 == 0 && K % G == 0 && G % 32 == 0 &&
+         (spg == 1 || spg == 2 || spg == 4 || spg == 8) && K / G <= 256 && aligned(x, 16) && aligned(w, 16) &&
+         aligned(s, 16) && (!z || aligned(z, 16));
+}
+
 
 }  // namespace b2
 
