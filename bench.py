@@ -160,6 +160,9 @@ class W4Gemv:
         self.out = torch.empty(W4_LAYERS, M, W4_N, dtype=torch.float16, device=dev)
         self.out_host = torch.empty_like(self.out, device="cpu").pin_memory()
         self.step_bytes = W4_LAYERS * w4_gemv_bytes(M)
+        self.step_work = self.step_bytes          # algorithmic bytes per step
+        self.value_scale = 1e9                    # -> GB/s
+        self.peak_key, self.peak_unit = "hbm_gbs", "GB/s"
         self.launches_per_step = W4_LAYERS
         self.cfg = {"workload": f"w4a16_gemv M={M} K={W4_K} N={W4_N} G={W4_G}",
                     "layers_per_step": W4_LAYERS, "weight_bytes_resident": W4_LAYERS * (W4_K // 8) * W4_N * 4,
@@ -181,7 +184,7 @@ class W4Gemv:
         self.out_host.copy_(self.out, non_blocking=True)
         return self.x_host.numel() * 2, self.out.numel() * 2
 
-    def kernel_bytes(self):
+    def kernel_work(self):
         return w4_gemv_bytes(self.M)
 
     def check(self):
@@ -216,12 +219,134 @@ class W4Gemv:
                                           "(fp32 dequant-then-matmul, torch on all host threads)"}
 
 
-WORKLOADS = {"w4a16_gemv": W4Gemv}
+# --------------------------------------------------------------------------
+# workloads: prefill GEMMs (C2 / C2'): x bf16 [4096, 4096] @ W [4096, 14336]
+# --------------------------------------------------------------------------
+G_M, G_K, G_N, G_G = 4096, 4096, 14336, 128
+
+
+class Gemm:
+    """One step = one GEMM on the C2 shape; x, packed W, scales and the 117 MB
+    output together exceed the 126 MB L2 (no flush needed)."""
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    bound = "tensor"
+
+    def __init__(self, kind, rank, M=G_M, N=G_N, K=G_K):
+        import b200kern as bk
+        from b200kern import _lib
+        from b200kern.synthetic import w4_inputs, w8_inputs
+        self.bk, self.lib, self.kind = bk, _lib, kind
+        self.M, self.N, self.K = M, N, K
+        dev = torch.device("cuda")
+        self.name = kind
+        self.metric = {"w4a16_gemm": "W4A16 prefill GEMM tensor throughput",
+                       "w8a16_gemm": "W8A16 prefill GEMM tensor throughput",
+                       "gemm_bf16": "bf16 GEMM tensor throughput"}[kind]
+        if kind == "w4a16_gemm":
+            d = w4_inputs(M, N, K, G_G, dtype=torch.bfloat16, seed=rank)
+            self.q = d["q"]
+            self.w, self.s = d["qweight"].to(dev), d["scales"].to(dev)
+        elif kind == "w8a16_gemm":
+            d = w8_inputs(M, N, K, dtype=torch.bfloat16, seed=rank)
+            self.w, self.s = d["w"].to(dev), d["scales"].to(dev)
+        else:
+            g = torch.Generator().manual_seed(rank)
+            d = {"x": torch.randn(M, K, generator=g).bfloat16()}
+            self.w = (torch.randn(N, K, generator=g) / K ** 0.5).bfloat16().to(dev)
+            self.s = None
+        self.x_host = d["x"].pin_memory()
+        self.x = self.x_host.to(dev)
+        self.out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        self.out_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.step_work = 2.0 * M * N * K
+        self.value_scale = 1e12
+        self.peak_key, self.peak_unit = "bf16_tflops_sustained", "TFLOP/s"
+        self.launches_per_step = 1
+        self.cfg = {"workload": f"{kind} M={M} K={K} N={N}" + (f" G={G_G}" if kind == "w4a16_gemm" else ""),
+                    "l2": "inputs+output 178+ MB > 126 MB L2 (no flush needed)"}
+
+    def launch(self, i, stream):
+        if self.kind == "w4a16_gemm":
+            self.lib.call("b2_int4_matmul", self.x.data_ptr(), self.w.data_ptr(), self.out.data_ptr(),
+                          self.s.data_ptr(), None, self.M, self.N, self.K, G_G, 1, stream)
+        elif self.kind == "w8a16_gemm":
+            self.lib.call("b2_int8_matmul", self.x.data_ptr(), self.w.data_ptr(), self.out.data_ptr(),
+                          self.s.data_ptr(), None, self.M, self.N, self.K, 1, stream)
+        else:
+            self.lib.call("b2_gemm_bf16", self.x.data_ptr(), self.w.data_ptr(), self.out.data_ptr(),
+                          self.M, self.N, self.K, stream)
+
+    def step(self, stream):
+        self.launch(0, stream)
+
+    def e2e_step(self):
+        xd = self.x_host.to("cuda", non_blocking=True)
+        if self.kind == "w4a16_gemm":
+            self.bk.int4_matmul(xd, self.w, self.s, group_size=G_G, out=self.out)
+        elif self.kind == "w8a16_gemm":
+            self.bk.int8_matmul(xd, self.w, self.s, out=self.out)
+        else:
+            self.bk.gemm_bf16(xd, self.w, out=self.out)
+        self.out_host.copy_(self.out, non_blocking=True)
+        return self.x_host.numel() * 2, self.out.numel() * 2
+
+    def kernel_work(self):
+        return self.step_work
+
+    def check(self):
+        """Sampled rows vs the float64 oracle (max-normalised 1e-2)."""
+        import numpy as np
+        from oracle import quant as oq
+        torch.cuda.synchronize()
+        rows = torch.arange(0, self.M, max(1, self.M // 8))[:8]
+        xr = self.x[rows].double().cpu().numpy()
+        if self.kind == "w4a16_gemm":
+            ref = oq.int4_matmul(xr, self.q.numpy(), self.s.double().cpu().numpy(), None, G_G)
+        elif self.kind == "w8a16_gemm":
+            ref = oq.int8_matmul(xr, self.w.cpu().numpy(), self.s.double().cpu().numpy())
+        else:
+            ref = xr @ self.w.double().cpu().numpy().T
+        got = self.out[rows].double().cpu().numpy()
+        return bool(np.abs(got - ref).max() <= 1e-2 * np.abs(ref).max())
+
+    def cpu_baseline(self, budget_s=10.0):
+        """Reference algorithm (fp32 dequant-then-matmul, oracle/quant.py) on a
+        bounded sample of rows, on all host threads."""
+        from oracle import quant as oq
+        threads = os.cpu_count()
+        torch.set_num_threads(threads)
+        rows = 256
+        x = self.x_host[:rows]
+        if self.kind == "w4a16_gemm":
+            q, s = self.q.to(torch.int32), self.s.cpu()
+            fn = lambda: oq.int4_matmul_fp32_torch(x, q, s, None, G_G)
+        elif self.kind == "w8a16_gemm":
+            w, s = self.w.cpu(), self.s.cpu()
+            fn = lambda: x.float() @ (w.float() * s.float()[:, None]).t()
+        else:
+            w = self.w.cpu()
+            fn = lambda: x.float() @ w.float().t()
+        fn()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or n >= 50:
+                break
+        return {"value": n * 2.0 * rows * self.N * self.K / el / 1e12, "unit": "TFLOP/s", "cores": threads,
+                "kind": "port", "sample": f"{n} x [{rows} rows of M] x K={self.K} x N={self.N} in {el:.1f} s"}
+
+
+WORKLOADS = {"w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
 
 
 def make_workload(args, rank):
     if args.workload == "w4a16_gemv":
         return W4Gemv(args.m, rank)
+    if args.workload in ("w4a16_gemm", "w8a16_gemm", "gemm_bf16"):
+        return Gemm(args.workload, rank)
     raise SystemExit(f"unknown workload {args.workload}")
 
 
@@ -259,7 +384,7 @@ def run_ours(args):
     barrier(world)
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, world)
-    value = wl.step_bytes * args.steps * world / (ms_max / 1e3) / 1e9
+    value = wl.step_work * args.steps * world / (ms_max / 1e3) / wl.value_scale
 
     # ---- average device time per launch of the dominant kernel ----
     # The timed graph holds only this kernel (launches_per_step of them back
@@ -267,10 +392,11 @@ def run_ours(args):
     # includes the short inter-kernel gaps inside the graph (conservative).
     k_ms = ms / args.steps / wl.launches_per_step
     pk = peaks()
-    achieved = wl.kernel_bytes() / (k_ms / 1e3) / 1e9
-    roof = {"bound": wl.bound, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": NCU_TRAFFIC.get(wl.name),
-            "peak_source": f"{pk['source']} (burst copy bandwidth)", "kernel_us": round(k_ms * 1e3, 3)}
+    achieved = wl.kernel_work() / (k_ms / 1e3) / wl.value_scale
+    peak = pk[wl.peak_key]
+    roof = {"bound": wl.bound, "achieved": round(achieved, 1), "peak": peak, "unit": wl.peak_unit,
+            "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC.get(wl.name),
+            "peak_source": f"{pk['source']} {wl.peak_key}", "kernel_us": round(k_ms * 1e3, 3)}
 
     # ---- e2e through the public API with host buffers ----
     e2e_steps = max(3, min(args.steps, 200))
@@ -285,7 +411,7 @@ def run_ours(args):
     e1.record()
     torch.cuda.synchronize()
     e_ms = max_over_ranks(e0.elapsed_time(e1), world)
-    e2e = {"value": round(wl.step_bytes * e2e_steps * world / (e_ms / 1e3) / 1e9, 1), "unit": wl.unit,
+    e2e = {"value": round(wl.step_work * e2e_steps * world / (e_ms / 1e3) / wl.value_scale, 1), "unit": wl.unit,
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps}
 
     line = None

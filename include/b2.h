@@ -87,6 +87,16 @@ B2_API int b2_int8_matmul(const void* input, const void* weight, void* output,
                    int dtype, void* stream);
 
 /*
+ * Plain bf16 GEMM on tcgen05: out[M,N] = x[M,K] @ w[N,K]^T (w K-major, the
+ * nn.Linear layout), fp32 accumulate, bf16 out.  The dequantised-weight
+ * path of the reference's matmuls (x @ dequant(W), _msl_templates.py:2663,
+ * :2716) when W is already bf16.  Needs M % 128 == 0, N % 256 == 0,
+ * K % 64 == 0 and 16-byte aligned pointers.
+ */
+B2_API int b2_gemm_bf16(const void* x, const void* w, void* out,
+                        int64_t M, int64_t N, int64_t K, void* stream);
+
+/*
  * Exact int4 -> fp32 dequantisation W[k,n] = (q - z) * float(s), written
  * as fp32 [K, N].  Debug/parity export of the unpack + dequant step the
  * reference does per k inside int4_matmul (_msl_templates.py:2723-2737).

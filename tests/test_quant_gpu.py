@@ -77,7 +77,7 @@ def test_w4_gemv_group_sizes_and_zeros(cuda, G):
     _check(out, ref)
 
 
-@pytest.mark.parametrize("M,N,K,G", [(3, 20, 24, 8), (17, 64, 256, 128), (40, 36, 128, 64)])
+@pytest.mark.parametrize("M,N,K,G", [(3, 20, 24, 8), (17, 64, 256, 128), (40, 36, 128, 64), (20, 256, 256, 128)])
 def test_w4_generic_shapes(cuda, M, N, K, G):
     """Shapes outside the GEMV fast path (tiny K/G, odd N, M > 16)."""
     import b200kern as bk

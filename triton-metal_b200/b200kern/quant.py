@@ -177,3 +177,19 @@ def int8_matmul(input, weight, scales, zeros=None, out=None):
         out.copy_(res)
         return out
     return res
+
+
+def gemm_bf16(x, w, out=None):
+    """out[M, N] = x[M, K] @ w[N, K]^T on tcgen05 (bf16 in/out, fp32 accumulate).
+
+    Needs M % 128 == 0, N % 256 == 0, K % 64 == 0."""
+    _check_cuda(x, w)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or x.dim() != 2 or w.dim() != 2:
+        raise B2DtypeError("gemm_bf16 takes bf16 x [M, K] and w [N, K]")
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise B2ShapeError("K mismatch")
+    res = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    _lib.call("b2_gemm_bf16", _ptr(x.contiguous()), _ptr(w.contiguous()), _ptr(res), M, N, K, _stream())
+    return res
