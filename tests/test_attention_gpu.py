@@ -1,0 +1,122 @@
+"""Parity of the FlashAttention kernels (through the C ABI) with the oracle.
+
+Tolerances: the reference's own fp32 tests use max abs error < 0.01
+(tests/test_flash_attention.py:155, :188); bf16/fp16 paths are checked
+against an fp32 reference of the same rounded inputs with
+|out - ref| <= 1e-2 + 1e-2 |ref| (the north-star rtol/atol)."""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, golden
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+MANIFEST = json.load(open(os.path.join(GOLDEN, "manifest.json")))
+REF_TESTS = {r["test"]: r for r in MANIFEST["reference_tests"]}
+
+
+def _close(out, ref, tol=1e-2):
+    out, ref = out.float(), ref.float()
+    err = (out - ref).abs()
+    bound = tol + tol * ref.abs()
+    assert bool((err <= bound).all()), f"max err {err.max().item():.4g}, ratio {(err / bound).max().item():.3g}"
+
+
+@pytest.mark.parametrize("rec", MANIFEST["triton_fa"], ids=lambda r: r["name"])
+def test_triton_fa_golden(cuda, rec):
+    """The reference's strided Triton test cases (seed 42, fp32) vs _ref_attention."""
+    import b200kern as bk
+    g = golden(rec["name"])
+    q, k, v = (torch.tensor(g[n], device=cuda) for n in "qkv")
+    out = bk.flash_attention(q, k, v, causal=rec["causal"])
+    assert (out.cpu() - torch.tensor(g["out"])).abs().max().item() < 0.01
+
+
+@pytest.mark.parametrize("name", ["test_flash_attention_single_head", "test_flash_attention_multi_block",
+                                  "test_flash_attention_causal", "test_flash_attention_gpu",
+                                  "test_causal_attention_gpu"])
+def test_template_golden(cuda, name):
+    import b200kern as bk
+    g, rec = golden("ref_" + name), REF_TESTS[name]
+    Q, K, V = (torch.tensor(g[n], device=cuda) for n in "qkv")
+    out = bk.flash_attention_template(Q, K, V, rec["seq_len"], rec["scale"], rec["head_dim"], causal=rec["causal"])
+    ref = g["expected"] if "expected" in g else g["out"]
+    assert np.abs(out.reshape(-1).cpu().numpy() - ref.reshape(-1)).max() < 1e-3
+
+
+@pytest.mark.parametrize("name", ["test_gqa_attention", "test_gqa_attention_gpu"])
+def test_gqa_decode_golden(cuda, name):
+    import b200kern as bk
+    g, rec = golden("ref_" + name), REF_TESTS[name]
+    out = bk.gqa_attention(torch.tensor(g["q"], device=cuda), torch.tensor(g["k"], device=cuda),
+                           torch.tensor(g["v"], device=cuda), rec["seq_len"], rec["scale"], rec["n_q_per_kv"])
+    ref = g["expected"] if "expected" in g else g["out"]
+    assert np.abs(out.reshape(-1).cpu().numpy() - ref.reshape(-1)).max() < 1e-3
+
+
+def _ref_torch(q, k, v, causal, scale=None):
+    """fp32 reference on the GPU, per (b, h) to bound memory."""
+    B, Hq, S, D = q.shape
+    rep = Hq // k.shape[1]
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    out = torch.empty(B, Hq, S, D, device=q.device, dtype=torch.float32)
+    for b in range(B):
+        for h in range(Hq):
+            s = (q[b, h].float() * scale) @ k[b, h // rep].float().t()
+            if causal:
+                s = s.masked_fill(torch.ones(S, k.shape[2], device=q.device, dtype=torch.bool).triu(1), float("-inf"))
+            out[b, h] = torch.softmax(s, -1).nan_to_num(0.0) @ v[b, h // rep].float()
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,Hq,Hkv,S,causal", [(1, 1, 1, 128, False), (1, 2, 2, 256, True), (2, 4, 2, 384, True),
+                                               (1, 4, 1, 200, False), (1, 2, 1, 1000, True), (1, 8, 2, 2048, True)])
+def test_fa_tcgen05(cuda, dtype, B, Hq, Hkv, S, causal):
+    import b200kern as bk
+    g = torch.Generator().manual_seed(S + Hq)
+    q = (torch.randn(B, Hq, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
+    k = (torch.randn(B, Hkv, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
+    v = (torch.randn(B, Hkv, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
+    out = bk.flash_attention(q, k, v, causal=causal)
+    _close(out, _ref_torch(q, k, v, causal))
+
+
+def test_fa_tcgen05_strided_and_large_logits(cuda):
+    """[B, S, H, D] storage viewed as [B, H, S, D]; large logits exercise the
+    lazy O rescale (running max growing by > 2^8 across blocks)."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(3)
+    base = torch.randn(2, 512, 4, 128, generator=g)
+    base[:, 300:] *= 6.0
+    q = base.bfloat16().to(cuda).transpose(1, 2)
+    k = (torch.randn(2, 512, 4, 128, generator=g) * 2).bfloat16().to(cuda).transpose(1, 2)
+    v = torch.randn(2, 512, 4, 128, generator=g).bfloat16().to(cuda).transpose(1, 2)
+    for causal in (False, True):
+        out = bk.flash_attention(q, k, v, causal=causal)
+        _close(out, _ref_torch(q, k, v, causal))
+
+
+def test_fa_oracle_small_bf16(cuda):
+    """tcgen05 path vs the float64 numpy oracle on one small GQA case."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(11)
+    q = (torch.randn(1, 4, 256, 128, generator=g) * 0.5).bfloat16()
+    k = (torch.randn(1, 2, 256, 128, generator=g) * 0.5).bfloat16()
+    v = (torch.randn(1, 2, 256, 128, generator=g) * 0.5).bfloat16()
+    out = bk.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=True).float().cpu()
+    ref = oatt.attention(q.double().numpy(), k.double().numpy(), v.double().numpy(), causal=True)
+    _close(out, torch.from_numpy(ref))
+
+
+def test_fa_no_bounded_wait_ran_out(cuda):
+    import ctypes
+    from b200kern import _lib
+    code = ctypes.c_uint(0)
+    st = _lib.load().b2_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(code))
+    assert st == 0 and code.value == 0, hex(code.value)

@@ -1,9 +1,541 @@
-// FlashAttention forward (sm_100a).
-#include "b2_common.cuh"
+// FlashAttention forward (sm_100a): O = softmax(scale * Q K^T [+ causal]) V
+//
+// Reference: flash_attention template (triton_metal/codegen/_msl_templates.py
+// :1568-1767; online softmax m/l/O update at :1697-1753, causal mask
+// kv_pos <= q_pos at :1610-1619, final O /= l skipped when l == 0), the
+// strided Triton kernel _flash_attn_fwd (tests/test_flash_attention.py:24-104)
+// and the GQA head map kv_head = q_head / n_q_per_kv (_msl_templates.py:2101).
+//
+// Fast path (D = 128, bf16/fp16): one CTA per (128-row Q tile, b, h).
+//   warp 0     TMA: Q tile once; K tiles (3-stage ring) and V tiles (2-stage)
+//   warp 1     TMEM owner + MMA issuer: S_j = Q K_j^T into one of two TMEM S
+//              buffers (M=N=128, K=16 x 8), then O += P_{j-1} V_{j-1} into the
+//              TMEM O accumulator (V is the MN-major B operand).  S_{j} is
+//              issued before PV_{j-1} so it overlaps softmax_{j-1}.
+//   warps 4-7  softmax, one query row per thread (TMEM lane = row): row max in
+//              the log2 domain, p = exp2(s - m), row sum, P as bf16 into a
+//              128B-swizzled K-major smem tile; O is rescaled in TMEM only
+//              when the running max grows by more than 8 (2^8 headroom in P),
+//              so most blocks never touch O.  Final O / l -> global.
+// Generic path (any D <= 256, fp32/bf16/fp16, any strides): one warp per
+// query row with the same online softmax in fp32.
+#include "tc_common.cuh"
+#include <string.h>
 
-extern "C" int b2_flash_attn_fwd(const void*, const void*, const void*, void*, int64_t, int64_t, int64_t,
-                                 int64_t, int64_t, int64_t, const int64_t*, const int64_t*, const int64_t*,
-                                 const int64_t*, float, int, int, void*) {
-  b2::set_error("flash_attn_fwd: not built yet");
-  return B2_ERR_UNSUPPORTED;
+namespace b2 {
+namespace fa {
+
+constexpr int BQ = 128, BKV = 128, HD = 128;
+constexpr int kTile = BQ * HD * 2;   // 32 KB: a 128 x 128 bf16 tile (two 64-col swizzle atoms)
+constexpr int kAtom = kTile / 2;     // 16 KB
+constexpr int kKStages = 3, kVStages = 2;
+constexpr int kThreads = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+struct Params {
+  int B, Hq, Hkv, Sq, Skv, causal, q_tiles;
+  float scale_log2;
+  __nv_bfloat16* o;
+  int64_t os_b, os_h, os_s;
+  unsigned* err;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code,
+                                           volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitNs) break;
+    }
+  }
+  atomicCAS(err, 0u, code);
+  *abort_flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 4-D tensor map coordinates: (d, s, h, b)
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int d, int s, int h, int b,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(d), "r"(s), "r"(h), "r"(b), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
+fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+              const __grid_constant__ CUtensorMap tmV, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTile;
+  uint8_t* sV = sK + kKStages * kTile;
+  uint8_t* sP = sV + kVStages * kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTile);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + kKStages;
+  uint64_t* v_full = k_empty + kKStages;
+  uint64_t* v_empty = v_full + kVStages;
+  uint64_t* s_full = v_empty + kVStages;  // [2]
+  uint64_t* s_free = s_full + 2;          // [2]
+  uint64_t* p_ready = s_free + 2;
+  uint64_t* pv_done = p_ready + 1;
+  uint64_t* drain = pv_done + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // longest (causal) tiles first: reverse the q-tile order
+  const int qt = p.q_tiles - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int q0 = qt * BQ;
+  int nkv = (p.Skv + BKV - 1) / BKV;
+  if (p.causal) nkv = min(nkv, (q0 + BQ - 1) / BKV + 1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kKStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kVStages; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_ready, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_holder, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t tO = tmem, tS0 = tmem + 128;  // S buffers at columns 128 and 256
+
+  if (warp == 0) {
+    // ---------------------------------- TMA ----------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_4d(sQ, &tmQ, 0, q0, h, b, q_full);
+      tma_load_4d(sQ + kAtom, &tmQ, 64, q0, h, b, q_full);
+      int kst = 0, vst = 0;
+      uint32_t kph = 0, vph = 0;
+      for (int j = 0; j < nkv; ++j) {
+        if (!wait_abort(&k_empty[kst], kph ^ 1, p.err, 0xB2200001u, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[kst], kTile);
+        tma_load_4d(sK + kst * kTile, &tmK, 0, j * BKV, hk, b, &k_full[kst]);
+        tma_load_4d(sK + kst * kTile + kAtom, &tmK, 64, j * BKV, hk, b, &k_full[kst]);
+        if (!wait_abort(&v_empty[vst], vph ^ 1, p.err, 0xB2200002u, abort_flag)) break;
+        mbar_arrive_expect_tx(&v_full[vst], kTile);
+        tma_load_4d(sV + vst * kTile, &tmV, 0, j * BKV, hk, b, &v_full[vst]);
+        tma_load_4d(sV + vst * kTile + kAtom, &tmV, 64, j * BKV, hk, b, &v_full[vst]);
+        if (++kst == kKStages) { kst = 0; kph ^= 1; }
+        if (++vst == kVStages) { vst = 0; vph ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------- MMA ----------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idS = tc::idesc_f16(BQ, BKV, !F16);
+      constexpr uint32_t idPV = tc::idesc_f16(BQ, HD, !F16, false, true);
+      bool ok = wait_abort(q_full, 0, p.err, 0xB2200003u, abort_flag);
+      int kst = 0, vst = 0;
+      uint32_t kph = 0, vph = 0;
+      auto issue_pv = [&](int jj) -> bool {
+        if (!wait_abort(p_ready, jj & 1, p.err, 0xB2200005u, abort_flag)) return false;
+        if (!wait_abort(&v_full[vst], vph, p.err, 0xB2200006u, abort_flag)) return false;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t da = tc::smem_desc(sP + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024, tc::kSwizzle128B);
+          const uint64_t db = tc::smem_desc(sV + vst * kTile + kk * 16 * 128, kAtom, 1024, tc::kSwizzle128B);
+          tc::mma_f16_ss(tO, da, db, idPV, (jj | kk) != 0);
+        }
+        tc::commit(pv_done);
+        tc::commit(&v_empty[vst]);
+        if (++vst == kVStages) { vst = 0; vph ^= 1; }
+        return true;
+      };
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int sb = j & 1;
+        // S buffer sb was last read by softmax_{j-2}
+        if (!wait_abort(&s_free[sb], ((j >> 1) & 1) ^ 1, p.err, 0xB2200004u, abort_flag) ||
+            !wait_abort(&k_full[kst], kph, p.err, 0xB2200007u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t da = tc::desc_kmajor_sw128(sQ + (kk >> 2) * kAtom + (kk & 3) * 32);
+          const uint64_t db = tc::desc_kmajor_sw128(sK + kst * kTile + (kk >> 2) * kAtom + (kk & 3) * 32);
+          tc::mma_f16_ss(tS0 + sb * 128, da, db, idS, kk != 0);
+        }
+        tc::commit(&s_full[sb]);
+        tc::commit(&k_empty[kst]);
+        if (++kst == kKStages) { kst = 0; kph ^= 1; }
+        if (j >= 1 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && nkv > 0) ok = issue_pv(nkv - 1);
+      if (!ok) {
+        tc::commit(drain);
+        mbar_wait(drain, 0, p.err, 0xB2200008u);
+      }
+    }
+  } else if (warp >= 4) {
+    // -------------------------------- softmax --------------------------------
+    const int qw = warp & 3;
+    const int r = qw * 32 + lane;  // row within the tile == TMEM lane
+    const int qpos = q0 + r;
+    const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int sb = j & 1;
+      if (!wait_abort(&s_full[sb], (j >> 1) & 1, p.err, 0xB2200009u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      uint32_t s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t (&part)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]);
+        tc::tmem_ld_32x32b_x32(tS0 + sb * 128 + lane_off + 32 * c, part);
+      }
+      tc::tmem_ld_wait();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      // scale into the log2 domain and mask
+      const int kv0 = j * BKV;
+      const bool need_mask = (p.causal && kv0 + BKV - 1 > q0) || kv0 + BKV > p.Skv;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float v = __uint_as_float(s[c]) * p.scale_log2;
+        if (need_mask) {
+          const int kv = kv0 + c;
+          if (kv >= p.Skv || (p.causal && kv > qpos)) v = -INFINITY;
+        }
+        s[c] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      // PV_{j-1} must be done before O is rescaled or P is overwritten
+      if (j >= 1 && !wait_abort(pv_done, (j - 1) & 1, p.err, 0xB220000Au, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      // Lazy rescale.  tcgen05.ld/st are warp-collective, so the decision to
+      // touch O is taken per warp; each lane applies its own factor.
+      const bool need = mx > m_used + kRescaleThreshold;
+      const float alpha = need ? ((m_used == -INFINITY) ? 0.f : ex2(m_used - mx)) : 1.f;
+      if (need) {
+        l *= alpha;
+        m_used = mx;
+      }
+      if (__any_sync(0xffffffffu, need) && j >= 1) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tc::tmem_ld_32x32b_x32(tO + lane_off + 32 * c, o);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + lane_off + 32 * c, o);
+        }
+        tmem_st_wait();
+      }
+      // p = exp2(s - m), row sum, bf16 P into the swizzled K-major tile
+      const float mref = (m_used == -INFINITY) ? 0.f : m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2(__uint_as_float(s[8 * c + 2 * e]) - mref);
+          const float p1 = ex2(__uint_as_float(s[8 * c + 2 * e + 1]) - mref);
+          rs += p0 + p1;
+          if constexpr (F16) {
+            __half2 hv = __floats2half2_rn(p0, p1);
+            pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+          } else {
+            __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
+            pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+          }
+        }
+        uint8_t* dst = sP + (c >> 3) * kAtom + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      l += rs;
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+    }
+    // epilogue: O / l -> global (rows beyond Sq are not stored)
+    if (ok && nkv > 0 && wait_abort(pv_done, (nkv - 1) & 1, p.err, 0xB220000Bu, abort_flag)) {
+      tc::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + b * p.os_b + h * p.os_h + (int64_t)qpos * p.os_s;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tc::tmem_ld_32x32b_x32(tO + lane_off + 32 * c, o);
+        tc::tmem_ld_wait();
+        if (qpos < p.Sq) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float a = __uint_as_float(o[2 * e]) * inv, bb = __uint_as_float(o[2 * e + 1]) * inv;
+            if constexpr (F16) {
+              __half2 hv = __floats2half2_rn(a, bb);
+              pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+            } else {
+              __nv_bfloat162 hv = __floats2bfloat162_rn(a, bb);
+              pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+        }
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+constexpr size_t kSmem = (size_t)kTile * (2 + kKStages + kVStages) + 1024 + 256;
+
+// ---------------------------------------------------------------------------
+// Generic path: one warp per query row, fp32 online softmax (same update as
+// the reference template, _msl_templates.py:1712-1743).  Any D <= 256.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p) {
+  if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float*>(p);
+  else return to_f32<T>(*p);
+}
+template <typename T>
+__device__ __forceinline__ void stf(T* p, float v) {
+  if constexpr (sizeof(T) == 4) *reinterpret_cast<float*>(p) = v;
+  else *p = from_f32<T>(v);
+}
+
+struct GenParams {
+  const void *q, *k, *v;
+  void* o;
+  int B, Hq, Hkv, Sq, Skv, D, causal;
+  float scale;
+  int64_t qs[3], ks[3], vs[3], os[3];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(128) fa_generic_kernel(const GenParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+  if (row >= (int64_t)p.B * p.Hq * p.Sq) return;
+  const int s = row % p.Sq;
+  const int h = (row / p.Sq) % p.Hq;
+  const int b = row / ((int64_t)p.Sq * p.Hq);
+  const int hk = h / (p.Hq / p.Hkv);
+  const T* q = (const T*)p.q + b * p.qs[0] + h * p.qs[1] + (int64_t)s * p.qs[2];
+  const T* kb = (const T*)p.k + b * p.ks[0] + hk * p.ks[1];
+  const T* vb = (const T*)p.v + b * p.vs[0] + hk * p.vs[1];
+  constexpr int MAXE = 8;
+  float qv[MAXE], acc[MAXE];
+#pragma unroll
+  for (int e = 0; e < MAXE; ++e) {
+    const int d = lane + 32 * e;
+    qv[e] = d < p.D ? ldf(q + d) * p.scale : 0.f;
+    acc[e] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  const int kend = p.causal ? min(p.Skv, s + 1) : p.Skv;
+  for (int j = 0; j < kend; ++j) {
+    const T* kr = kb + (int64_t)j * p.ks[2];
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < MAXE; ++e) {
+      const int d = lane + 32 * e;
+      if (d < p.D) dot += qv[e] * ldf(kr + d);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mn = fmaxf(m, dot);
+    const float alpha = __expf(m - mn), pj = __expf(dot - mn);
+    l = l * alpha + pj;
+    const T* vr = vb + (int64_t)j * p.vs[2];
+#pragma unroll
+    for (int e = 0; e < MAXE; ++e) {
+      const int d = lane + 32 * e;
+      acc[e] = acc[e] * alpha + (d < p.D ? pj * ldf(vr + d) : 0.f);
+    }
+    m = mn;
+  }
+  T* o = (T*)p.o + b * p.os[0] + h * p.os[1] + (int64_t)s * p.os[2];
+  const float inv = l > 0.f ? 1.f / l : 0.f;  // all-masked row -> 0 (reference nan_to_num)
+#pragma unroll
+  for (int e = 0; e < MAXE; ++e) {
+    const int d = lane + 32 * e;
+    if (d < p.D) stf(o + d, acc[e] * inv);
+  }
+}
+
+}  // namespace fa
+
+static bool make_tmap_4d(CUtensorMap* map, const void* base, bool f16, int64_t D, int64_t S, int64_t H, int64_t B,
+                         const int64_t* strides_elems) {
+  // dims (d, s, h, b); strides in bytes for s, h, b
+  typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    fn = reinterpret_cast<EncodeFn>(p);
+  }
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)strides_elems[2] * 2, (cuuint64_t)strides_elems[1] * 2,
+                                 (cuuint64_t)strides_elems[0] * 2};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool strides_ok16(const int64_t* s) { return s[0] % 8 == 0 && s[1] % 8 == 0 && s[2] % 8 == 0; }
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" int b2_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq,
+                                 int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, const int64_t* qs,
+                                 const int64_t* ks, const int64_t* vs, const int64_t* os, float scale, int causal,
+                                 int dtype, void* stream) {
+  B2_CHECK_ARG(q && k && v && o && qs && ks && vs && os, B2_ERR_INVALID, "flash_attn_fwd: null pointer");
+  B2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && Sq >= 0 && Skv >= 0 && D > 0, B2_ERR_INVALID,
+               "flash_attn_fwd: bad shape");
+  B2_CHECK_ARG(Hq % Hkv == 0, B2_ERR_INVALID, "flash_attn_fwd: Hq=%lld not a multiple of Hkv=%lld", (long long)Hq,
+               (long long)Hkv);
+  B2_CHECK_ARG(!causal || Sq == Skv, B2_ERR_INVALID, "flash_attn_fwd: causal needs Sq == Skv (square tril mask)");
+  B2_CHECK_ARG(dtype == B2_F16 || dtype == B2_BF16 || dtype == B2_F32, B2_ERR_DTYPE, "flash_attn_fwd: dtype %d",
+               dtype);
+  B2_CHECK_ARG(D <= 256, B2_ERR_UNSUPPORTED, "flash_attn_fwd: D=%lld > 256", (long long)D);
+  if (Sq == 0) return B2_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool fast = D == fa::HD && dtype != B2_F32 && Skv > 0 && strides_ok16(qs) && strides_ok16(ks) &&
+                    strides_ok16(vs) && strides_ok16(os) && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) &&
+                    aligned(o, 16) && B <= 65535 && Hq <= 65535;
+  if (fast) {
+    unsigned* err = device_error_word();
+    CUtensorMap tq, tk, tv;
+    const bool f16 = dtype == B2_F16;
+    if (err && make_tmap_4d(&tq, q, f16, D, Sq, Hq, B, qs) && make_tmap_4d(&tk, k, f16, D, Skv, Hkv, B, ks) &&
+        make_tmap_4d(&tv, v, f16, D, Skv, Hkv, B, vs)) {
+      fa::Params p;
+      p.B = (int)B;
+      p.Hq = (int)Hq;
+      p.Hkv = (int)Hkv;
+      p.Sq = (int)Sq;
+      p.Skv = (int)Skv;
+      p.causal = causal;
+      p.q_tiles = (int)((Sq + fa::BQ - 1) / fa::BQ);
+      p.scale_log2 = scale * fa::kLog2e;
+      p.o = (__nv_bfloat16*)o;
+      p.os_b = os[0];
+      p.os_h = os[1];
+      p.os_s = os[2];
+      p.err = err;
+      dim3 grid(p.q_tiles, (unsigned)Hq, (unsigned)B);
+      if (f16) {
+        cudaFuncSetAttribute(fa::fa_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa::kSmem);
+        fa::fa_fwd_kernel<true><<<grid, fa::kThreads, fa::kSmem, st>>>(tq, tk, tv, p);
+      } else {
+        cudaFuncSetAttribute(fa::fa_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa::kSmem);
+        fa::fa_fwd_kernel<false><<<grid, fa::kThreads, fa::kSmem, st>>>(tq, tk, tv, p);
+      }
+      return launch_status("fa_fwd");
+    }
+  }
+  fa::GenParams g;
+  g.q = q;
+  g.k = k;
+  g.v = v;
+  g.o = o;
+  g.B = (int)B;
+  g.Hq = (int)Hq;
+  g.Hkv = (int)Hkv;
+  g.Sq = (int)Sq;
+  g.Skv = (int)Skv;
+  g.D = (int)D;
+  g.causal = causal;
+  g.scale = scale;
+  for (int i = 0; i < 3; ++i) {
+    g.qs[i] = qs[i];
+    g.ks[i] = ks[i];
+    g.vs[i] = vs[i];
+    g.os[i] = os[i];
+  }
+  const int64_t rows = B * Hq * Sq;
+  const unsigned blocks = (unsigned)((rows + 3) / 4);
+  if (dtype == B2_F32) fa::fa_generic_kernel<float><<<blocks, 128, 0, st>>>(g);
+  else if (dtype == B2_BF16) fa::fa_generic_kernel<__nv_bfloat16><<<blocks, 128, 0, st>>>(g);
+  else fa::fa_generic_kernel<__half><<<blocks, 128, 0, st>>>(g);
+  return launch_status("fa_generic");
 }
