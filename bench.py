@@ -339,7 +339,103 @@ class Gemm:
                 "kind": "port", "sample": f"{n} x [{rows} rows of M] x K={self.K} x N={self.N} in {el:.1f} s"}
 
 
-WORKLOADS = {"w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
+# --------------------------------------------------------------------------
+# workload: FlashAttention GQA prefill (C3)
+# --------------------------------------------------------------------------
+class FlashAttn:
+    """B=4, Hq=32, Hkv=8, S=8192, D=128, causal, bf16; q/k/v = 0.5 N(0,1).
+    One step = one forward over the whole batch (q/k/v/o 671 MB > L2)."""
+    name = "fa_gqa"
+    metric = "FlashAttention GQA prefill throughput"
+    unit = "tokens/s"
+    dtype = "bf16"
+    bound = "tensor"
+
+    def __init__(self, rank, B=4, Hq=32, Hkv=8, S=8192, D=128, causal=True):
+        import b200kern as bk
+        self.bk = bk
+        self.B, self.Hq, self.Hkv, self.S, self.D, self.causal = B, Hq, Hkv, S, D, causal
+        g = torch.Generator().manual_seed(rank)
+        self.q_host = (torch.randn(B, Hq, S, D, generator=g) * 0.5).bfloat16().pin_memory()
+        self.k_host = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).bfloat16().pin_memory()
+        self.v_host = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).bfloat16().pin_memory()
+        self.q, self.k, self.v = (t.cuda() for t in (self.q_host, self.k_host, self.v_host))
+        self.o = torch.empty_like(self.q)
+        self.o_host = torch.empty_like(self.q_host).pin_memory()
+        self.flops = 4.0 * B * Hq * S * S * D / (2 if causal else 1)
+        self.step_work = B * S          # tokens per step
+        self.value_scale = 1.0
+        self.roof_scale = 1e12
+        self.peak_key, self.peak_unit = "bf16_tflops_sustained", "TFLOP/s"
+        self.launches_per_step = 1
+        self.cfg = {"workload": f"fa_gqa B={B} Hq={Hq} Hkv={Hkv} S={S} D={D} causal={causal}",
+                    "flop_convention": "4*B*Hq*S^2*D/2 (causal half)",
+                    "l2": "q/k/v/o 671 MB > 126 MB L2 (no flush needed)"}
+
+    def step(self, stream):
+        self.bk.flash_attention(self.q, self.k, self.v, causal=self.causal, out=self.o)
+
+    def launch(self, i, stream):
+        self.step(stream)
+
+    def e2e_step(self):
+        q, k, v = (h.to("cuda", non_blocking=True) for h in (self.q_host, self.k_host, self.v_host))
+        self.bk.flash_attention(q, k, v, causal=self.causal, out=self.o)
+        self.o_host.copy_(self.o, non_blocking=True)
+        return sum(t.numel() * 2 for t in (self.q_host, self.k_host, self.v_host)), self.o.numel() * 2
+
+    def kernel_work(self):
+        return self.flops
+
+    def _ref_rows(self, b, h, rows):
+        """float64 reference for some query rows of one (b, h) (causal offsets kept)."""
+        rep = self.Hq // self.Hkv
+        q = self.q_host[b, h, rows].double()
+        k = self.k_host[b, h // rep].double()
+        v = self.v_host[b, h // rep].double()
+        s = (q / self.D ** 0.5) @ k.t()
+        if self.causal:
+            kpos = torch.arange(self.S)[None, :]
+            s = s.masked_fill(kpos > rows[:, None], float("-inf"))
+        return torch.softmax(s, -1) @ v
+
+    def check(self):
+        torch.cuda.synchronize()
+        rows = torch.cat([torch.arange(0, 64), torch.arange(self.S - 64, self.S)])
+        ok = True
+        for (b, h) in ((0, 0), (self.B - 1, self.Hq - 1)):
+            ref = self._ref_rows(b, h, rows)
+            got = self.o[b, h, rows].double().cpu()
+            ok &= bool(((got - ref).abs() <= 1e-2 + 1e-2 * ref.abs()).all())
+        return ok
+
+    def cpu_baseline(self, budget_s=10.0):
+        """The reference's _ref_attention (tests/test_flash_attention.py:107-118)
+        restated in fp32 torch on all host threads, on a sample of (b, h)
+        slices with the GQA expansion, scaled to the B*Hq slices of a step."""
+        threads = os.cpu_count()
+        torch.set_num_threads(threads)
+        rep = self.Hq // self.Hkv
+        n, t0 = 0, time.perf_counter()
+        while True:
+            b, h = divmod(n % (self.B * self.Hq), self.Hq)
+            q = self.q_host[b, h].float()
+            k = self.k_host[b, h // rep].float()
+            v = self.v_host[b, h // rep].float()
+            s = (q * (1.0 / self.D ** 0.5)) @ k.t()
+            if self.causal:
+                s = s.masked_fill(torch.ones(self.S, self.S, dtype=torch.bool).triu(1), float("-inf"))
+            torch.softmax(s, -1).nan_to_num(0.0) @ v
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or n >= 8:
+                break
+        step_s = el / n * self.B * self.Hq
+        return {"value": self.B * self.S / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"{n} (b, h) slices of {self.B * self.Hq} in {el:.1f} s, scaled linearly"}
+
+
+WORKLOADS = {"fa_gqa": FlashAttn, "w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
 
 
 def make_workload(args, rank):
@@ -347,6 +443,8 @@ def make_workload(args, rank):
         return W4Gemv(args.m, rank)
     if args.workload in ("w4a16_gemm", "w8a16_gemm", "gemm_bf16"):
         return Gemm(args.workload, rank)
+    if args.workload == "fa_gqa":
+        return FlashAttn(rank)
     raise SystemExit(f"unknown workload {args.workload}")
 
 
@@ -392,7 +490,8 @@ def run_ours(args):
     # includes the short inter-kernel gaps inside the graph (conservative).
     k_ms = ms / args.steps / wl.launches_per_step
     pk = peaks()
-    achieved = wl.kernel_work() / (k_ms / 1e3) / wl.value_scale
+    roof_scale = getattr(wl, "roof_scale", wl.value_scale)
+    achieved = wl.kernel_work() / (k_ms / 1e3) / roof_scale
     peak = pk[wl.peak_key]
     roof = {"bound": wl.bound, "achieved": round(achieved, 1), "peak": peak, "unit": wl.peak_unit,
             "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC.get(wl.name),
