@@ -283,8 +283,40 @@ def main():
             _save(name, {"q": q.numpy(), "k": k.numpy(), "v": v.numpy(), "out": ref.numpy()})
             manifest["triton_fa"].append({"name": name, "causal": causal, "shape": [Z, H, N, D],
                                           "cite": "tests/test_flash_attention.py:107-118"})
+    manifest["kda"] = kda_goldens()
     with open(os.path.join(HERE, "manifest.json"), "w") as f:
         json.dump(manifest, f, indent=1)
+
+
+KDA_CASES = [  # (name, B, T, H, D, with_initial_state, seed)
+    ("kda_b1_t128_h1", 1, 128, 1, 128, False, 1),
+    ("kda_b2_t64_h2_init", 2, 64, 2, 128, True, 2),
+]
+
+
+def kda_goldens():
+    """KDA has no reference code (triton-metal ships none).  Golden vectors
+    come from flash-linear-attention 0.5.1, fla.ops.kda.naive
+    (naive_recurrent_kda), on inputs drawn as in oracle/kda.py.make_inputs."""
+    import torch
+    from fla.ops.kda.naive import naive_recurrent_kda
+    from oracle import kda as okda
+    out = []
+    for name, B, T, H, D, init, seed in KDA_CASES:
+        q, k, v, g, beta = okda.make_inputs(B, T, H, D, seed=seed)
+        s0 = np.random.default_rng(seed + 100).standard_normal((B, H, D, D)) * 0.1 if init else None
+        tt = lambda a: torch.tensor(a, dtype=torch.float32)
+        o, S = naive_recurrent_kda(tt(q), tt(k), tt(v), tt(g), tt(beta), scale=None,
+                                   initial_state=None if s0 is None else tt(s0), output_final_state=True)
+        arrays = {"q": q.astype(np.float32), "k": k.astype(np.float32), "v": v.astype(np.float32),
+                  "g": g.astype(np.float32), "beta": beta.astype(np.float32),
+                  "o": o.numpy(), "S": S.numpy()}
+        if s0 is not None:
+            arrays["s0"] = s0.astype(np.float32)
+        _save(name, arrays)
+        out.append({"name": name, "B": B, "T": T, "H": H, "D": D, "initial_state": init,
+                    "source": "fla 0.5.1 fla.ops.kda.naive.naive_recurrent_kda"})
+    return out
 
 
 if __name__ == "__main__":

@@ -91,3 +91,14 @@ def test_asymmetric_zero_matches_loop():
             exp[i, j] = sum(x[i, k] * (q[j, k] - z[j, k // G]) * s[j, k // G] for k in range(K))
     out = oq.int4_matmul_ref_layout(x, oq.pack_int4_ref(q), s, z, G)
     np.testing.assert_allclose(out, exp, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("rec", MANIFEST["kda"], ids=lambda r: r["name"])
+def test_kda_oracle_matches_fla(rec):
+    """KDA oracle vs flash-linear-attention 0.5.1's naive recurrence (the
+    reference has no KDA; fla is the operator's defining library)."""
+    from oracle import kda as okda
+    g = golden(rec["name"])
+    o, S = okda.recurrent(g["q"], g["k"], g["v"], g["g"], g["beta"], initial_state=g.get("s0"))
+    np.testing.assert_allclose(o, g["o"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(S, g["S"], rtol=1e-4, atol=1e-4)
