@@ -435,7 +435,98 @@ class FlashAttn:
                 "sample": f"{n} (b, h) slices of {self.B * self.Hq} in {el:.1f} s, scaled linearly"}
 
 
-WORKLOADS = {"fa_gqa": FlashAttn, "w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
+# --------------------------------------------------------------------------
+# workload: KDA chunked forward (C4)
+# --------------------------------------------------------------------------
+class KDA:
+    """B=1, H=32, T=16384, Dk=Dv=128, chunk 64; q,k L2-normalised bf16, v bf16,
+    g = -softplus(N(0,1)) fp32, beta = sigmoid(N(0,1)) bf16, zero fp32 state.
+    One step = one forward over all heads (inputs 810 MB > L2)."""
+    name = "kda"
+    metric = "KDA chunked forward throughput"
+    unit = "tokens/s"
+    dtype = "bf16 (fp32 state)"
+    bound = "hbm"
+
+    def __init__(self, rank, B=1, T=16384, H=32, D=128):
+        import b200kern as bk
+        from b200kern.kda import workspace_size
+        self.bk, self.B, self.T, self.H, self.D = bk, B, T, H, D
+        gen = torch.Generator().manual_seed(rank)
+        F = torch.nn.functional
+        self.q_host = F.normalize(torch.randn(B, T, H, D, generator=gen), dim=-1).bfloat16().pin_memory()
+        self.k_host = F.normalize(torch.randn(B, T, H, D, generator=gen), dim=-1).bfloat16().pin_memory()
+        self.v_host = torch.randn(B, T, H, D, generator=gen).bfloat16().pin_memory()
+        self.g_host = (-F.softplus(torch.randn(B, T, H, D, generator=gen))).pin_memory()
+        self.b_host = torch.sigmoid(torch.randn(B, T, H, generator=gen)).bfloat16().pin_memory()
+        self.q, self.k, self.v, self.g, self.beta = (t.cuda() for t in (self.q_host, self.k_host, self.v_host,
+                                                                        self.g_host, self.b_host))
+        self.o = torch.empty_like(self.v)
+        self.o_host = torch.empty_like(self.v_host).pin_memory()
+        self.ws = torch.empty(workspace_size(B, T, H), dtype=torch.uint8, device="cuda")
+        # algorithmic bytes: q,k,v bf16 + g fp32 + beta + o bf16 + S0 and S_T fp32
+        self.bytes = (3 * B * T * H * D * 2 + B * T * H * D * 4 + B * T * H * 2 + B * T * H * D * 2
+                      + 2 * B * H * D * D * 4)
+        self.step_work = B * T
+        self.value_scale = 1.0
+        self.roof_scale = 1e9
+        self.peak_key, self.peak_unit = "hbm_gbs", "GB/s"
+        self.launches_per_step = 1
+        self.kernels_per_launch = 2  # intra-chunk kernel + state pass
+        self.cfg = {"workload": f"kda B={B} T={T} H={H} Dk=Dv={D} chunk=64",
+                    "algorithmic_bytes": self.bytes, "l2": "inputs 810 MB > 126 MB L2",
+                    "kernels_per_step": 2}
+
+    def step(self, stream):
+        self.bk.kda_chunk_fwd(self.q, self.k, self.v, self.g, self.beta, out=self.o, workspace=self.ws)
+
+    def launch(self, i, stream):
+        self.step(stream)
+
+    def e2e_step(self):
+        q, k, v, g, b = (h.to("cuda", non_blocking=True) for h in (self.q_host, self.k_host, self.v_host,
+                                                                   self.g_host, self.b_host))
+        self.bk.kda_chunk_fwd(q, k, v, g, b, out=self.o, workspace=self.ws)
+        self.o_host.copy_(self.o, non_blocking=True)
+        h2d = sum(t.numel() * t.element_size() for t in (self.q_host, self.k_host, self.v_host, self.g_host,
+                                                         self.b_host))
+        return h2d, self.o.numel() * 2
+
+    def kernel_work(self):
+        return self.bytes
+
+    def check(self):
+        """Heads 0 and H-1 over the first 512 steps vs the float64 oracle."""
+        import numpy as np
+        from oracle import kda as okda
+        n, heads = 512, [0, self.H - 1]
+        o2, _ = self.bk.kda_chunk_fwd(self.q[:, :n].contiguous(), self.k[:, :n].contiguous(),
+                                      self.v[:, :n].contiguous(), self.g[:, :n].contiguous(),
+                                      self.beta[:, :n].contiguous())
+        d = lambda t: t[:, :n, heads].double().numpy()
+        oref, _ = okda.recurrent(d(self.q_host), d(self.k_host), d(self.v_host), d(self.g_host),
+                                 self.b_host[:, :n, heads].double().numpy())
+        got = o2[:, :, heads].double().cpu().numpy()
+        return bool((np.abs(got - oref) <= 2e-2 + 2e-2 * np.abs(oref)).all())
+
+    def cpu_baseline(self, budget_s=10.0):
+        """No reference CPU path exists for KDA: the float64 recurrence oracle
+        (oracle/kda.py, not the reference's code) on a sample of steps and heads,
+        scaled linearly to T and H."""
+        from oracle import kda as okda
+        heads, n = 2, 256
+        d = lambda t: t[:, :n, :heads].double().numpy()
+        t0 = time.perf_counter()
+        okda.recurrent(d(self.q_host), d(self.k_host), d(self.v_host), d(self.g_host),
+                       self.b_host[:, :n, :heads].double().numpy())
+        el = time.perf_counter() - t0
+        step_s = el * (self.T / n) * (self.H / heads)
+        return {"value": self.B * self.T / step_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+                "sample": f"{n} steps x {heads} heads in {el:.2f} s (numpy float64 recurrence, not reference code), "
+                          "scaled linearly"}
+
+
+WORKLOADS = {"kda": KDA, "fa_gqa": FlashAttn, "w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
 
 
 def make_workload(args, rank):
@@ -445,6 +536,8 @@ def make_workload(args, rank):
         return Gemm(args.workload, rank)
     if args.workload == "fa_gqa":
         return FlashAttn(rank)
+    if args.workload == "kda":
+        return KDA(rank)
     raise SystemExit(f"unknown workload {args.workload}")
 
 
@@ -521,7 +614,7 @@ def run_ours(args):
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
                 "data": "synthetic (seeded, BASELINE distributions)", "config": wl.cfg,
                 "parity_ok": parity_ok, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": wl.launches_per_step * args.steps, "clocks": clk.summary()}
+                "gpu_launches": getattr(wl, "kernels_per_launch", 1) * wl.launches_per_step * args.steps, "clocks": clk.summary()}
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
