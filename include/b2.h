@@ -144,6 +144,23 @@ B2_API int b2_kda_fwd(const void* q, const void* k, const void* v, const float* 
                int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv,
                int64_t chunk, float scale, int dtype, void* stream);
 
+/*
+ * b2_kda_fwd without a workspace argument, for callers that cannot allocate
+ * device memory when they run KDA (e.g. inside a custom allocator or memory
+ * pool that must not be re-entered, or a plugin host that only provides the
+ * input and output buffers).  No counterpart in the reference (which has no
+ * KDA at all).  The workspace is a fixed 64 MiB device array inside the
+ * library that every GPU loading it keeps until exit; shapes needing more
+ * (B*H*(T/64) > 453) are rejected with B2_ERR_INVALID.  The first call on a
+ * device looks up the array's address (do it before any stream capture).
+ * All calls share the array: calls overlapping on the GPU race.
+ */
+B2_API int b2_kda_fwd_noalloc(const void* q, const void* k, const void* v, const float* g,
+                              const void* beta, const float* initial_state,
+                              void* o, float* final_state,
+                              int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv,
+                              int64_t chunk, float scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -353,3 +353,73 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
 #undef B2_KDA_LAUNCH
   return launch_status("kda_fwd");
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot allocate device memory at the point where they run
+// KDA: code that executes while a custom allocator or memory pool must not be
+// re-entered, plugin hosts that hand out only input/output buffers, or
+// runtimes that forbid cudaMalloc on their hot path.  For them the workspace
+// lives in a fixed file-scope device array of kNoAllocScratchBytes that every
+// GPU loading this library holds until the process exits.
+//
+// * The first call on a device resolves the array's device address with
+//   cudaGetSymbolAddress (with that device current) and caches it; make that
+//   first call before any stream capture.
+// * Problems whose workspace exceeds kNoAllocScratchBytes are rejected with
+//   B2_ERR_INVALID (use b2_kda_fwd with a caller-provided workspace instead).
+// * Every call shares the one array, which keeps the previous call's
+//   contents.  Nothing in it needs clearing: each call writes every workspace
+//   element it reads before reading it.  Calls whose kernels overlap on the
+//   GPU (other streams, other threads) race on the array.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace b2 {
+namespace kda {
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static void* noalloc_scratch_ptr(int* status) {
+  static std::mutex mu;
+  static void* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = B2_ERR_LAUNCH;
+    set_error("kda_fwd_noalloc: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *status = B2_ERR_LAUNCH;
+      set_error("kda_fwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    cache[dev] = p;
+  }
+  return cache[dev];
+}
+}  // namespace kda
+}  // namespace b2
+
+extern "C" int b2_kda_fwd_noalloc(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                                  const float* initial_state, void* o, float* final_state, int64_t B, int64_t T,
+                                  int64_t H, int64_t Dk, int64_t Dv, int64_t chunk, float scale, int dtype,
+                                  void* stream) {
+  const size_t need = b2_kda_workspace_size(B, T, H, Dk, Dv, chunk);
+  B2_CHECK_ARG(need > 0, B2_ERR_INVALID, "kda_fwd_noalloc: unsupported shape B=%lld T=%lld H=%lld chunk=%lld",
+               (long long)B, (long long)T, (long long)H, (long long)chunk);
+  B2_CHECK_ARG(need <= kda::kNoAllocScratchBytes, B2_ERR_INVALID,
+               "kda_fwd_noalloc: workspace of %zu bytes exceeds the fixed %zu-byte device array "
+               "(B*H*(T/64) <= %zu chunk-heads); call b2_kda_fwd with your own workspace",
+               need, kda::kNoAllocScratchBytes, kda::kNoAllocScratchBytes / (kda::kWsBlock * sizeof(float)));
+  int status = B2_OK;
+  void* ws = kda::noalloc_scratch_ptr(&status);
+  if (!ws) return status;
+  return b2_kda_fwd(q, k, v, g, beta, initial_state, o, final_state, ws, B, T, H, Dk, Dv, chunk, scale, dtype,
+                    stream);
+}
