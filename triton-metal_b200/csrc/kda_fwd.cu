@@ -34,7 +34,9 @@ constexpr int C = 64, DK = 128, DV = 128;
 constexpr int kAThreads = 256;
 constexpr int VB = 16;  // state columns per CTA in kernel B
 constexpr int kBThreads = 256;
-constexpr int LDA = C + 1;  // padded row stride of the 64 x 64 matrices
+constexpr int LDA = C + 1;   // padded row stride of the 64 x 64 matrices
+constexpr int LDK = DK + 1;  // padded row stride of the 64 x 128 tiles (kernel A)
+constexpr int LDS = DK + 4;  // padded, 16-byte aligned row stride (kernel B)
 
 // Workspace block per (b, h, chunk), floats
 constexpr size_t kWsW = 0;
@@ -53,14 +55,14 @@ __device__ __forceinline__ float ld(const T* p) {
 
 // smem layout of kernel A (floats)
 constexpr int kAK = 0;
-constexpr int kAQ = kAK + C * DK;
-constexpr int kAG = kAQ + C * DK;
-constexpr int kAV = kAG + C * DK;
-constexpr int kAAkk = kAV + C * DV;
+constexpr int kAQ = kAK + C * LDK;
+constexpr int kAG = kAQ + C * LDK;
+constexpr int kAV = kAG + C * LDK;
+constexpr int kAAkk = kAV + C * LDK;
 constexpr int kAAqk = kAAkk + C * LDA;
 constexpr int kAT = kAAqk + C * LDA;
 constexpr int kAKg = kAT + C * LDA;
-constexpr int kABeta = kAKg + C * DK;
+constexpr int kABeta = kAKg + C * LDK;
 constexpr int kAFloats = kABeta + C;
 constexpr size_t kASmem = (size_t)kAFloats * 4;
 
@@ -87,13 +89,13 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
   for (int e = tid; e < C * DK; e += kAThreads) {
     const int t = e / DK, d = e % DK;
     const int64_t off = (row0 + (int64_t)t * H) * DK + d;
-    sK[e] = ld(k + off);
-    sQ[e] = ld(q + off) * scale;
-    sG[e] = g[off];
+    sK[t * LDK + d] = ld(k + off);
+    sQ[t * LDK + d] = ld(q + off) * scale;
+    sG[t * LDK + d] = g[off];
   }
   for (int e = tid; e < C * DV; e += kAThreads) {
     const int t = e / DV, d = e % DV;
-    sV[e] = ld(v + (row0 + (int64_t)t * H) * DV + d);
+    sV[t * LDK + d] = ld(v + (row0 + (int64_t)t * H) * DV + d);
   }
   if (tid < C) sBeta[tid] = ld(beta + row0 + (int64_t)tid * H);
   __syncthreads();
@@ -101,8 +103,8 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
   if (tid < DK) {
     float acc = 0.f;
     for (int t = 0; t < C; ++t) {
-      acc += sG[t * DK + tid];
-      sG[t * DK + tid] = acc;
+      acc += sG[t * LDK + tid];
+      sG[t * LDK + tid] = acc;
     }
   }
   __syncthreads();
@@ -122,16 +124,16 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
 #pragma unroll
       for (int c = 0; c < 4; ++c) akk[a][c] = aqk[a][c] = 0.f;
     for (int d = 0; d < DK; ++d) {
-      const float gr = sG[r * DK + d];
+      const float gr = sG[r * LDK + d];
       float ki[4], qi[4], kj[4];
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
         const int i = 4 * bi + a, j = 4 * bj + a;
-        const float ei = __expf(sG[i * DK + d] - gr);
-        const float ej = __expf(gr - sG[j * DK + d]);
-        ki[a] = sK[i * DK + d] * ei;
-        qi[a] = sQ[i * DK + d] * ei;
-        kj[a] = sK[j * DK + d] * ej;
+        const float ei = __expf(sG[i * LDK + d] - gr);
+        const float ej = __expf(gr - sG[j * LDK + d]);
+        ki[a] = sK[i * LDK + d] * ei;
+        qi[a] = sQ[i * LDK + d] * ei;
+        kj[a] = sK[j * LDK + d] * ej;
       }
 #pragma unroll
       for (int a = 0; a < 4; ++a)
@@ -173,13 +175,17 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
       __syncthreads();
     }
   }
-  for (int e = tid; e < C * DK; e += kAThreads) sKg[e] = sK[e] * __expf(sG[e]);
+  for (int e = tid; e < C * DK; e += kAThreads) {
+    const int t = e / DK, d = e % DK;
+    sKg[t * LDK + d] = sK[t * LDK + d] * __expf(sG[t * LDK + d]);
+  }
   __syncthreads();
   // ---- W = T diag(beta) (K o e^G), U = T diag(beta) V, and the per-row products ----
   float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
   {
-    // thread -> (row i = tid / 4, 32 columns starting at 32 * (tid % 4))
-    const int i = tid >> 2, c0 = (tid & 3) * 32;
+    // thread -> (row i = tid / 4, columns d = tid % 4 + 4 c): interleaved so
+    // the 4 column groups of a row fall in different banks
+    const int i = tid >> 2, cg = tid & 3;
     float w[32], u[32];
 #pragma unroll
     for (int c = 0; c < 32; ++c) w[c] = u[c] = 0.f;
@@ -187,32 +193,33 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
       const float tb = sT[i * LDA + m] * sBeta[m];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const int d = c0 + c;
-        w[c] += tb * sKg[m * DK + d];
-        u[c] += tb * sV[m * DV + d];
+        const int d = cg + 4 * c;
+        w[c] += tb * sKg[m * LDK + d];
+        u[c] += tb * sV[m * LDK + d];
       }
     }
-    const float* gl = sG + (C - 1) * DK;
+    const float* gl = sG + (C - 1) * LDK;
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
-      const int d = c0 + c;
-      const float gi = sG[i * DK + d];
+      const int d = cg + 4 * c;
+      const float gi = sG[i * LDK + d];
       blk[kWsW + i * DK + d] = w[c];
       blk[kWsU + i * DV + d] = u[c];
-      blk[kWsQg + i * DK + d] = sQ[i * DK + d] * __expf(gi);
-      blk[kWsKr + i * DK + d] = sK[i * DK + d] * __expf(gl[d] - gi);
+      blk[kWsQg + i * DK + d] = sQ[i * LDK + d] * __expf(gi);
+      blk[kWsKr + i * DK + d] = sK[i * LDK + d] * __expf(gl[d] - gi);
     }
   }
   for (int e = tid; e < C * C; e += kAThreads) blk[kWsAq + e] = sAq[(e / C) * LDA + (e % C)];
-  if (tid < DK) blk[kWsGl + tid] = __expf(sG[(C - 1) * DK + tid]);
+  if (tid < DK) blk[kWsGl + tid] = __expf(sG[(C - 1) * LDK + tid]);
 }
 
 // smem layout of kernel B (floats)
 constexpr int kBW = 0;
-constexpr int kBQg = kBW + C * DK;
-constexpr int kBKr = kBQg + C * DK;
-constexpr int kBAq = kBKr + C * DK;
-constexpr int kBU = kBAq + C * C;
+constexpr int LDQ = C + 4;  // padded, 16-byte aligned row stride of A_qk (kernel B)
+constexpr int kBQg = kBW + C * LDS;
+constexpr int kBKr = kBQg + C * LDS;
+constexpr int kBAq = kBKr + C * LDS;
+constexpr int kBU = kBAq + C * LDQ;
 constexpr int kBVp = kBU + C * VB;
 constexpr int kBS = kBVp + C * VB;
 constexpr int kBGl = kBS + DK * VB;
@@ -245,12 +252,15 @@ kda_state_kernel(const float* __restrict__ ws, const float* __restrict__ s0, T* 
     const float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
     __syncthreads();
     for (int e = tid; e < C * DK / 4; e += kBThreads) {
-      reinterpret_cast<float4*>(sW)[e] = reinterpret_cast<const float4*>(blk + kWsW)[e];
-      reinterpret_cast<float4*>(sQg)[e] = reinterpret_cast<const float4*>(blk + kWsQg)[e];
-      reinterpret_cast<float4*>(sKr)[e] = reinterpret_cast<const float4*>(blk + kWsKr)[e];
+      const int r = e / (DK / 4), c4 = e % (DK / 4);
+      reinterpret_cast<float4*>(sW + r * LDS)[c4] = reinterpret_cast<const float4*>(blk + kWsW)[e];
+      reinterpret_cast<float4*>(sQg + r * LDS)[c4] = reinterpret_cast<const float4*>(blk + kWsQg)[e];
+      reinterpret_cast<float4*>(sKr + r * LDS)[c4] = reinterpret_cast<const float4*>(blk + kWsKr)[e];
     }
-    for (int e = tid; e < C * C / 4; e += kBThreads)
-      reinterpret_cast<float4*>(sAq)[e] = reinterpret_cast<const float4*>(blk + kWsAq)[e];
+    for (int e = tid; e < C * C / 4; e += kBThreads) {
+      const int r = e / (C / 4), c4 = e % (C / 4);
+      reinterpret_cast<float4*>(sAq + r * LDQ)[c4] = reinterpret_cast<const float4*>(blk + kWsAq)[e];
+    }
     for (int e = tid; e < C * VB; e += kBThreads) sU[e] = blk[kWsU + (e / VB) * DV + v0 + (e % VB)];
     if (tid < DK) sGl[tid] = blk[kWsGl + tid];
     __syncthreads();
@@ -259,7 +269,7 @@ kda_state_kernel(const float* __restrict__ ws, const float* __restrict__ s0, T* 
       const int i = tid >> 2, c0 = (tid & 3) * 4;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       for (int kk = 0; kk < DK; ++kk) {
-        const float w = sW[i * DK + kk];
+        const float w = sW[i * LDS + kk];
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[c] += w * sS[kk * VB + c0 + c];
       }
@@ -272,12 +282,12 @@ kda_state_kernel(const float* __restrict__ ws, const float* __restrict__ s0, T* 
       const int i = tid >> 2, c0 = (tid & 3) * 4;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       for (int kk = 0; kk < DK; ++kk) {
-        const float qg = sQg[i * DK + kk];
+        const float qg = sQg[i * LDS + kk];
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[c] += qg * sS[kk * VB + c0 + c];
       }
       for (int j = 0; j <= i; ++j) {
-        const float a = sAq[i * C + j];
+        const float a = sAq[i * LDQ + j];
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[c] += a * sVp[j * VB + c0 + c];
       }
@@ -294,7 +304,7 @@ kda_state_kernel(const float* __restrict__ ws, const float* __restrict__ s0, T* 
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc[c] = gl * sS[kk * VB + c0 + c];
       for (int i = 0; i < C; ++i) {
-        const float kr = sKr[i * DK + kk];
+        const float kr = sKr[i * LDS + kk];
 #pragma unroll
         for (int c = 0; c < 8; ++c) acc[c] += kr * sVp[i * VB + c0 + c];
       }
