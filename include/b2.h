@@ -151,7 +151,7 @@ B2_API int b2_kda_fwd(const void* q, const void* k, const void* v, const float* 
  * input and output buffers).  No counterpart in the reference (which has no
  * KDA at all).  The workspace is a fixed 64 MiB device array inside the
  * library that every GPU loading it keeps until exit; shapes needing more
- * (B*H*(T/64) > 453) are rejected with B2_ERR_INVALID.  The first call on a
+ * (B*H*(T/64) > 272) are rejected with B2_ERR_INVALID.  The first call on a
  * device looks up the array's address (do it before any stream capture).
  * All calls share the array: calls overlapping on the GPU race.
  */

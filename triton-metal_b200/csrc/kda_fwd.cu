@@ -22,9 +22,10 @@
 // exp(G_i - G_j) is split at r = the last row of the j block, so both
 // exp(G_i - G_r) and exp(G_r - G_j) are <= 1 off the diagonal (and the
 // diagonal blocks span at most 3 steps).
-// Kernel B (one CTA per (b, h, 16 columns of Dv)) carries the fp32 state
-// through the chunks in order.  Columns of the state are independent: the
-// transition acts on the Dk side only.
+// Kernel B (one CTA per (b, h, 32 columns of Dv)) carries the fp32 state
+// through the chunks in order on tf32 tensor cores (columns of the state are
+// independent: the transition acts on the Dk side only), storing V' and each
+// chunk's entering state; kernel C (parallel over chunks) forms the outputs.
 #include "b2_common.cuh"
 
 namespace b2 {
@@ -45,7 +46,9 @@ constexpr size_t kWsQg = kWsU + (size_t)C * DV;
 constexpr size_t kWsKr = kWsQg + (size_t)C * DK;
 constexpr size_t kWsAq = kWsKr + (size_t)C * DK;
 constexpr size_t kWsGl = kWsAq + (size_t)C * C;
-constexpr size_t kWsBlock = kWsGl + DK;
+constexpr size_t kWsVp = kWsGl + DK;                  // V' = U - W S (state pass -> output)
+constexpr size_t kWsS = kWsVp + (size_t)C * DV;       // state entering the chunk
+constexpr size_t kWsBlock = kWsS + (size_t)DK * DV;
 
 template <typename T>
 __device__ __forceinline__ float ld(const T* p) {
@@ -213,114 +216,283 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
   if (tid < DK) blk[kWsGl + tid] = __expf(sG[(C - 1) * LDK + tid]);
 }
 
-// smem layout of kernel B (floats)
-constexpr int kBW = 0;
-constexpr int LDQ = C + 4;  // padded, 16-byte aligned row stride of A_qk (kernel B)
-constexpr int kBQg = kBW + C * LDS;
-constexpr int kBKr = kBQg + C * LDS;
-constexpr int kBAq = kBKr + C * LDS;
-constexpr int kBU = kBAq + C * LDQ;
-constexpr int kBVp = kBU + C * VB;
-constexpr int kBS = kBVp + C * VB;
-constexpr int kBGl = kBS + DK * VB;
-constexpr int kBFloats = kBGl + DK;
-constexpr size_t kBSmem = (size_t)kBFloats * 4;
+// ---- tf32 warp MMA (m16n8k8), fp32 accumulate -------------------------------
+__device__ __forceinline__ uint32_t tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <typename T>
-__global__ void __launch_bounds__(kBThreads, 1)
-kda_state_kernel(const float* __restrict__ ws, const float* __restrict__ s0, T* __restrict__ o,
-                 float* __restrict__ s_out, int B, int Tlen, int H) {
-  extern __shared__ float sm[];
-  float* sW = sm + kBW;
-  float* sQg = sm + kBQg;
-  float* sKr = sm + kBKr;
-  float* sAq = sm + kBAq;
-  float* sU = sm + kBU;
-  float* sVp = sm + kBVp;
-  float* sS = sm + kBS;
-  float* sGl = sm + kBGl;
-  const int nc = Tlen / C;
-  const int vb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int v0 = vb * VB;
-  const int tid = threadIdx.x;
-  // state slice S[:, v0:v0+VB]
-  for (int e = tid; e < DK * VB; e += kBThreads) {
-    const int kk = e / VB, c = e % VB;
-    sS[e] = s0 ? s0[(((size_t)b * H + h) * DK + kk) * DV + v0 + c] : 0.f;
+// ---------------------------------------------------------------------------
+// Kernel B: sequential state pass, one CTA per (b, h, 32 state columns).
+// Per chunk (tf32 tensor-core MMAs, fp32 state in registers):
+//   V' = U - W S          (64 x 32, K = 128)
+//   S  = e^{G_last} o S + Kr^T V'   (128 x 32, K = 64)
+// and stores V' and the state entering the chunk for kernel C.  The next
+// chunk's W, Kr and U slice stream in with cp.async while this one computes.
+// ---------------------------------------------------------------------------
+constexpr int SV = 32;        // state columns per CTA
+constexpr int kB2Threads = 128;
+constexpr int LW = DK + 4;    // sW row stride: A-fragment reads (row g, col t) conflict-free
+constexpr int LKR = DK + 8;   // sKr row stride: transposed A reads (row t, col g) conflict-free
+constexpr int LB = SV + 8;    // B-operand tiles (row t, col g) conflict-free
+constexpr int kB2Stage = C * LW + C * LKR + C * LB;  // floats per stage
+constexpr int kB2S = 2 * kB2Stage;
+constexpr int kB2Vp = kB2S + DK * LB;
+constexpr int kB2Floats = kB2Vp + C * LB;
+constexpr size_t kB2Smem = (size_t)kB2Floats * 4;
+
+__device__ __forceinline__ void b2_load_stage(float* st, const float* blk, int v0, int tid) {
+  float* sW = st;
+  float* sKr = sW + C * LW;
+  float* sU = sKr + C * LKR;
+  for (int e = tid; e < C * DK / 4; e += kB2Threads) {
+    const int r = e / (DK / 4), c4 = e % (DK / 4);
+    cp_async16(sW + r * LW + 4 * c4, blk + kWsW + r * DK + 4 * c4);
+    cp_async16(sKr + r * LKR + 4 * c4, blk + kWsKr + r * DK + 4 * c4);
   }
-  for (int chunk = 0; chunk < nc; ++chunk) {
-    const float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
-    __syncthreads();
-    for (int e = tid; e < C * DK / 4; e += kBThreads) {
-      const int r = e / (DK / 4), c4 = e % (DK / 4);
-      reinterpret_cast<float4*>(sW + r * LDS)[c4] = reinterpret_cast<const float4*>(blk + kWsW)[e];
-      reinterpret_cast<float4*>(sQg + r * LDS)[c4] = reinterpret_cast<const float4*>(blk + kWsQg)[e];
-      reinterpret_cast<float4*>(sKr + r * LDS)[c4] = reinterpret_cast<const float4*>(blk + kWsKr)[e];
-    }
-    for (int e = tid; e < C * C / 4; e += kBThreads) {
-      const int r = e / (C / 4), c4 = e % (C / 4);
-      reinterpret_cast<float4*>(sAq + r * LDQ)[c4] = reinterpret_cast<const float4*>(blk + kWsAq)[e];
-    }
-    for (int e = tid; e < C * VB; e += kBThreads) sU[e] = blk[kWsU + (e / VB) * DV + v0 + (e % VB)];
-    if (tid < DK) sGl[tid] = blk[kWsGl + tid];
-    __syncthreads();
-    // V' = U - W S   (64 x VB): 4 outputs per thread
-    {
-      const int i = tid >> 2, c0 = (tid & 3) * 4;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kk = 0; kk < DK; ++kk) {
-        const float w = sW[i * LDS + kk];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[c] += w * sS[kk * VB + c0 + c];
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) sVp[i * VB + c0 + c] = sU[i * VB + c0 + c] - acc[c];
-    }
-    __syncthreads();
-    // O = Qg S + Aq V'   (64 x VB)
-    {
-      const int i = tid >> 2, c0 = (tid & 3) * 4;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kk = 0; kk < DK; ++kk) {
-        const float qg = sQg[i * LDS + kk];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[c] += qg * sS[kk * VB + c0 + c];
-      }
-      for (int j = 0; j <= i; ++j) {
-        const float a = sAq[i * LDQ + j];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[c] += a * sVp[j * VB + c0 + c];
-      }
-      T* orow = o + (((int64_t)b * Tlen + (int64_t)chunk * C + i) * H + h) * DV + v0 + c0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) orow[c] = from_f32<T>(acc[c]);
-    }
-    __syncthreads();
-    // S <- Gl o S + Kr^T V'   (DK x VB): 8 outputs per thread
-    {
-      const int kk = tid >> 1, c0 = (tid & 1) * 8;
-      float acc[8];
-      const float gl = sGl[kk];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = gl * sS[kk * VB + c0 + c];
-      for (int i = 0; i < C; ++i) {
-        const float kr = sKr[i * LDS + kk];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[c] += kr * sVp[i * VB + c0 + c];
-      }
-      __syncthreads();  // every thread finished reading the old S
-#pragma unroll
-      for (int c = 0; c < 8; ++c) sS[kk * VB + c0 + c] = acc[c];
-    }
+  for (int e = tid; e < C * SV / 4; e += kB2Threads) {
+    const int r = e / (SV / 4), c4 = e % (SV / 4);
+    cp_async16(sU + r * LB + 4 * c4, blk + kWsU + r * DV + v0 + 4 * c4);
   }
-  __syncthreads();
-  if (s_out)
-    for (int e = tid; e < DK * VB; e += kBThreads) {
-      const int kk = e / VB, c = e % VB;
-      s_out[(((size_t)b * H + h) * DK + kk) * DV + v0 + c] = sS[e];
-    }
 }
 
+__global__ void __launch_bounds__(kB2Threads, 1)
+kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ s_out, int B, int Tlen,
+                 int H) {
+  extern __shared__ __align__(16) float sm[];
+  float* sS = sm + kB2S;
+  float* sVp = sm + kB2Vp;
+  const int nc = Tlen / C;
+  const int v0 = blockIdx.x * SV, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  float* head = ws + ((size_t)b * H + h) * nc * kWsBlock;
+
+  b2_load_stage(sm, head, v0, tid);
+  cp_async_commit();
+
+  // state rows of this warp: m-tiles 2w, 2w+1 (dk rows 32w .. 32w+31), all 32 columns
+  float acc[2][4][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
+        const float v = s0 ? s0[(((size_t)b * H + h) * DK + row) * DV + v0 + col] : 0.f;
+        acc[mt][nt][e] = v;
+        sS[row * LB + col] = v;
+      }
+
+  for (int c = 0; c < nc; ++c) {
+    float* blk = head + (size_t)c * kWsBlock;
+    float* st = sm + (c & 1) * kB2Stage;
+    if (c + 1 < nc) {
+      b2_load_stage(sm + ((c + 1) & 1) * kB2Stage, blk + kWsBlock, v0, tid);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // stage c and sS visible to all
+    const float* sW = st;
+    const float* sKr = sW + C * LW;
+    const float* sU = sKr + C * LKR;
+
+    // state entering this chunk -> workspace (read by kernel C)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = v0 + 8 * nt + 2 * t;
+          *reinterpret_cast<float2*>(blk + kWsS + row * DV + col) = make_float2(acc[mt][nt][e], acc[mt][nt][e + 1]);
+        }
+
+    // V' = U - W S: warp w owns chunk rows 16w .. 16w+15
+    {
+      float p[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p[nt][e] = 0.f;
+      const int r0 = 16 * warp;
+#pragma unroll 4
+      for (int ks = 0; ks < DK / 8; ++ks) {
+        const int k0 = 8 * ks;
+        const uint32_t a0 = tf32(sW[(r0 + g) * LW + k0 + t]), a1 = tf32(sW[(r0 + g + 8) * LW + k0 + t]);
+        const uint32_t a2 = tf32(sW[(r0 + g) * LW + k0 + t + 4]), a3 = tf32(sW[(r0 + g + 8) * LW + k0 + t + 4]);
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const uint32_t b0 = tf32(sS[(k0 + t) * LB + 8 * nt + g]), b1 = tf32(sS[(k0 + t + 4) * LB + 8 * nt + g]);
+          mma_tf32(p[nt], a0, a1, a2, a3, b0, b1);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int row = r0 + g + 8 * (e >> 1), col = 8 * nt + 2 * t;
+          const float v0f = sU[row * LB + col] - p[nt][e], v1f = sU[row * LB + col + 1] - p[nt][e + 1];
+          sVp[row * LB + col] = v0f;
+          sVp[row * LB + col + 1] = v1f;
+          *reinterpret_cast<float2*>(blk + kWsVp + row * DV + v0 + col) = make_float2(v0f, v1f);
+        }
+    }
+    __syncthreads();  // V' complete; every warp finished reading sS
+
+    // S = e^{G_last} o S + Kr^T V'
+    {
+      const float* glp = blk + kWsGl;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const float gl0 = glp[32 * warp + 16 * mt + g], gl1 = glp[32 * warp + 16 * mt + g + 8];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          acc[mt][nt][0] *= gl0;
+          acc[mt][nt][1] *= gl0;
+          acc[mt][nt][2] *= gl1;
+          acc[mt][nt][3] *= gl1;
+        }
+      }
+#pragma unroll 2
+      for (int ks = 0; ks < C / 8; ++ks) {
+        const int k0 = 8 * ks;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          const int m0 = 32 * warp + 16 * mt;  // dk rows; A[m][k] = Kr[k][m]
+          const uint32_t a0 = tf32(sKr[(k0 + t) * LKR + m0 + g]), a1 = tf32(sKr[(k0 + t) * LKR + m0 + g + 8]);
+          const uint32_t a2 = tf32(sKr[(k0 + t + 4) * LKR + m0 + g]), a3 = tf32(sKr[(k0 + t + 4) * LKR + m0 + g + 8]);
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            const uint32_t b0 = tf32(sVp[(k0 + t) * LB + 8 * nt + g]), b1 = tf32(sVp[(k0 + t + 4) * LB + 8 * nt + g]);
+            mma_tf32(acc[mt][nt], a0, a1, a2, a3, b0, b1);
+          }
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
+            sS[row * LB + col] = acc[mt][nt][e];
+          }
+    }
+    __syncthreads();  // new S visible; stage c may be overwritten by the next prefetch
+  }
+  if (s_out) {
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
+          s_out[(((size_t)b * H + h) * DK + row) * DV + v0 + col] = acc[mt][nt][e];
+        }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel C: outputs, one CTA per (b, h, chunk), fully parallel:
+//   O = (scale Q o e^G) S_c + A_qk V'     (64 x 128; tf32 MMAs)
+// ---------------------------------------------------------------------------
+constexpr int kCThreads = 128;
+constexpr int LQ = DK + 4;   // A reads (row g, col t)
+constexpr int LAQ = C + 4;
+constexpr int LBS = DV + 8;  // B reads (row t, col g)
+constexpr int kCQ = 0;
+constexpr int kCA = kCQ + C * LQ;
+constexpr int kCS = kCA + C * LAQ;
+constexpr int kCV = kCS + DK * LBS;
+constexpr int kCFloats = kCV + C * LBS;
+constexpr size_t kCSmem = (size_t)kCFloats * 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kCThreads, 1)
+kda_output_kernel(const float* __restrict__ ws, T* __restrict__ o, int B, int Tlen, int H) {
+  extern __shared__ __align__(16) float sm[];
+  float* sQ = sm + kCQ;
+  float* sA = sm + kCA;
+  float* sS = sm + kCS;
+  float* sV = sm + kCV;
+  const int nc = Tlen / C;
+  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
+  for (int e = tid; e < C * DK / 4; e += kCThreads) {
+    const int r = e / (DK / 4), c4 = e % (DK / 4);
+    cp_async16(sQ + r * LQ + 4 * c4, blk + kWsQg + r * DK + 4 * c4);
+    cp_async16(sV + r * LBS + 4 * c4, blk + kWsVp + r * DV + 4 * c4);
+  }
+  for (int e = tid; e < DK * DV / 4; e += kCThreads) {
+    const int r = e / (DV / 4), c4 = e % (DV / 4);
+    cp_async16(sS + r * LBS + 4 * c4, blk + kWsS + r * DV + 4 * c4);
+  }
+  for (int e = tid; e < C * C / 4; e += kCThreads) {
+    const int r = e / (C / 4), c4 = e % (C / 4);
+    cp_async16(sA + r * LAQ + 4 * c4, blk + kWsAq + r * C + 4 * c4);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  // warp w: chunk rows 16w .. 16w+15, all 128 output columns (16 n-tiles)
+  const int r0 = 16 * warp;
+  float acc[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+#pragma unroll 2
+  for (int ks = 0; ks < DK / 8; ++ks) {
+    const int k0 = 8 * ks;
+    const uint32_t a0 = tf32(sQ[(r0 + g) * LQ + k0 + t]), a1 = tf32(sQ[(r0 + g + 8) * LQ + k0 + t]);
+    const uint32_t a2 = tf32(sQ[(r0 + g) * LQ + k0 + t + 4]), a3 = tf32(sQ[(r0 + g + 8) * LQ + k0 + t + 4]);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+      mma_tf32(acc[nt], a0, a1, a2, a3, tf32(sS[(k0 + t) * LBS + 8 * nt + g]),
+               tf32(sS[(k0 + t + 4) * LBS + 8 * nt + g]));
+  }
+  // A_qk is lower triangular: k-steps beyond this warp's last row contribute 0
+  const int ksteps = (r0 + 16) / 8;
+  for (int ks = 0; ks < ksteps; ++ks) {
+    const int k0 = 8 * ks;
+    const uint32_t a0 = tf32(sA[(r0 + g) * LAQ + k0 + t]), a1 = tf32(sA[(r0 + g + 8) * LAQ + k0 + t]);
+    const uint32_t a2 = tf32(sA[(r0 + g) * LAQ + k0 + t + 4]), a3 = tf32(sA[(r0 + g + 8) * LAQ + k0 + t + 4]);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+      mma_tf32(acc[nt], a0, a1, a2, a3, tf32(sV[(k0 + t) * LBS + 8 * nt + g]),
+               tf32(sV[(k0 + t + 4) * LBS + 8 * nt + g]));
+  }
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int row = r0 + g + 8 * (e >> 1), col = 8 * nt + 2 * t;
+      T* dst = o + (((int64_t)b * Tlen + (int64_t)chunk * C + row) * H + h) * DV + col;
+      dst[0] = from_f32<T>(acc[nt][e]);
+      dst[1] = from_f32<T>(acc[nt][e + 1]);
+    }
+}
 }  // namespace kda
 }  // namespace b2
 
@@ -347,15 +519,18 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
   cudaStream_t st = (cudaStream_t)stream;
   float* ws = (float*)workspace;
   const dim3 ga((unsigned)(T / chunk), (unsigned)H, (unsigned)B);
-  const dim3 gb(kda::DV / kda::VB, (unsigned)H, (unsigned)B);
+  const dim3 gb(kda::DV / kda::SV, (unsigned)H, (unsigned)B);
+  cudaFuncSetAttribute(kda::kda_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kB2Smem);
 #define B2_KDA_LAUNCH(TY)                                                                                         \
   do {                                                                                                            \
     cudaFuncSetAttribute(kda::kda_intra_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kASmem); \
-    cudaFuncSetAttribute(kda::kda_state_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kBSmem); \
+    cudaFuncSetAttribute(kda::kda_output_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                         (int)kda::kCSmem);                                                                       \
     kda::kda_intra_kernel<TY><<<ga, kda::kAThreads, kda::kASmem, st>>>(                                         \
         (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale);        \
-    kda::kda_state_kernel<TY><<<gb, kda::kBThreads, kda::kBSmem, st>>>(ws, initial_state, (TY*)o, final_state, \
-                                                                      (int)B, (int)T, (int)H);                  \
+    kda::kda_state_kernel<<<gb, kda::kB2Threads, kda::kB2Smem, st>>>(ws, initial_state, final_state, (int)B,     \
+                                                                     (int)T, (int)H);                           \
+    kda::kda_output_kernel<TY><<<ga, kda::kCThreads, kda::kCSmem, st>>>(ws, (TY*)o, (int)B, (int)T, (int)H);     \
   } while (0)
   if (dtype == B2_BF16) B2_KDA_LAUNCH(__nv_bfloat16);
   else if (dtype == B2_F16) B2_KDA_LAUNCH(__half);
