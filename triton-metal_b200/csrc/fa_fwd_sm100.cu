@@ -6,17 +6,19 @@
 // strided Triton kernel _flash_attn_fwd (tests/test_flash_attention.py:24-104)
 // and the GQA head map kv_head = q_head / n_q_per_kv (_msl_templates.py:2101).
 //
-// Fast path (D = 128, bf16/fp16): one CTA per (128-row Q tile, b, h).
-//   warp 0     TMA: Q tile once; K tiles (3-stage ring) and V tiles (2-stage)
-//   warp 1     TMEM owner + MMA issuer: S_j = Q K_j^T into one of two TMEM S
-//              buffers (M=N=128, K=16 x 8), then O += P_{j-1} V_{j-1} into the
-//              TMEM O accumulator (V is the MN-major B operand).  S_{j} is
-//              issued before PV_{j-1} so it overlaps softmax_{j-1}.
-//   warps 4-7  softmax, one query row per thread (TMEM lane = row): row max in
-//              the log2 domain, p = exp2(s - m), row sum, P as bf16 into a
-//              128B-swizzled K-major smem tile; O is rescaled in TMEM only
-//              when the running max grows by more than 8 (2^8 headroom in P),
-//              so most blocks never touch O.  Final O / l -> global.
+// Fast path (D = 128, bf16/fp16): one CTA per pair of 128-row Q tiles of one
+// (b, h), longest causal pairs first.
+//   warp 0      TMA: both Q tiles once; K tiles (3-stage ring) and V tiles
+//               (2-stage) shared by the two Q tiles
+//   warp 1      TMEM owner + MMA issuer: S_u = Q_u K^T (M=N=128, K=16 x 8)
+//               and O_u += P_u V (P from TMEM, V the MN-major smem B operand)
+//               for the two tiles in ping-pong order
+//   warps 4-11  two softmax warpgroups (one per Q tile), one query row per
+//               thread (TMEM lane = row): row max in the log2 domain,
+//               p = exp2(s - m), row sum, P as bf16 written back into TMEM
+//               over its S columns; O is rescaled in TMEM only when the
+//               running max grows by more than 8 (2^8 headroom in P).
+//               Final O / l -> global.
 // Generic path (any D <= 256, fp32/bf16/fp16, any strides): one warp per
 // query row with the same online softmax in fp32.
 #include "tc_common.cuh"
@@ -29,7 +31,6 @@ constexpr int BQ = 128, BKV = 128, HD = 128;
 constexpr int kTile = BQ * HD * 2;   // 32 KB: a 128 x 128 bf16 tile (two 64-col swizzle atoms)
 constexpr int kAtom = kTile / 2;     // 16 KB
 constexpr int kKStages = 3, kVStages = 2;
-constexpr int kThreads = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
@@ -86,38 +87,75 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Fast path v2: two Q tiles per CTA (ping-pong), P kept in TMEM.
+//   TMEM (512 columns): tile u in {0, 1}: S_u / P_u at columns 256u, O_u at
+//   256u + 128.  P_u (bf16, two per 32-bit column) overwrites the first 64
+//   columns of S_u and is read by the TMEM-A form of tcgen05.mma.
+//   MMA issue order per KV block j:  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1),
+//   so the tensor core works on one tile while the other tile's softmax
+//   warpgroup runs.  MMAs from the single issuing thread execute in order,
+//   which orders S_u(j+1) after PV_u(j) (both use the S/P columns) and makes
+//   O_u quiescent whenever S_u(j) is complete.
+//   warps: 0 TMA, 1 TMEM owner + MMA issuer, 4-7 softmax tile 0,
+//          8-11 softmax tile 1 (warp w reads TMEM lanes 32 (w % 4) ..).
+// ---------------------------------------------------------------------------
+constexpr int kThreads2 = 384;
+constexpr size_t kSmem2 = (size_t)kTile * (2 + kKStages + kVStages) + 1024 + 256;
+
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 template <bool F16>
-__global__ void __launch_bounds__(kThreads, 1)
-fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-              const __grid_constant__ CUtensorMap tmV, const Params p) {
+__global__ void __launch_bounds__(kThreads2, 1)
+fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTile;
+  uint8_t* sQ = smem;                      // 2 tiles
+  uint8_t* sK = sQ + 2 * kTile;
   uint8_t* sV = sK + kKStages * kTile;
-  uint8_t* sP = sV + kVStages * kTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTile);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * kTile);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
   uint64_t* k_empty = k_full + kKStages;
   uint64_t* v_full = k_empty + kKStages;
   uint64_t* v_empty = v_full + kVStages;
-  uint64_t* s_full = v_empty + kVStages;  // [2]
-  uint64_t* s_free = s_full + 2;          // [2]
-  uint64_t* p_ready = s_free + 2;
-  uint64_t* pv_done = p_ready + 1;
-  uint64_t* drain = pv_done + 1;
+  uint64_t* s_full = v_empty + kVStages;  // [2] per tile
+  uint64_t* p_ready = s_full + 2;         // [2]
+  uint64_t* o_done = p_ready + 2;         // [2]
+  uint64_t* drain = o_done + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // longest (causal) tiles first: reverse the q-tile order
-  const int qt = p.q_tiles - 1 - (int)blockIdx.x;
+  const int npairs = (p.q_tiles + 1) / 2;
+  const int pi = npairs - 1 - (int)blockIdx.x;  // longest causal pairs first
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hkv);
-  const int q0 = qt * BQ;
-  int nkv = (p.Skv + BKV - 1) / BKV;
-  if (p.causal) nkv = min(nkv, (q0 + BQ - 1) / BKV + 1);
+  const int nkv_all = (p.Skv + BKV - 1) / BKV;
+  int q0[2], nkv[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    q0[u] = (2 * pi + u) * BQ;
+    nkv[u] = (2 * pi + u < p.q_tiles) ? (p.causal ? min(nkv_all, (q0[u] + BQ - 1) / BKV + 1) : nkv_all) : 0;
+  }
+  const int nkv_max = max(nkv[0], nkv[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -129,12 +167,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
+    for (int u = 0; u < 2; ++u) {
+      mbar_init(&s_full[u], 1);
+      mbar_init(&p_ready[u], 4);
+      mbar_init(&o_done[u], 1);
     }
-    mbar_init(p_ready, 4);
-    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -147,22 +184,24 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t tO = tmem, tS0 = tmem + 128;  // S buffers at columns 128 and 256
 
   if (warp == 0) {
     // ---------------------------------- TMA ----------------------------------
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kTile);
-      tma_load_4d(sQ, &tmQ, 0, q0, h, b, q_full);
-      tma_load_4d(sQ + kAtom, &tmQ, 64, q0, h, b, q_full);
+      const int ntiles = nkv[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, ntiles * kTile);
+      for (int u = 0; u < ntiles; ++u) {
+        tma_load_4d(sQ + u * kTile, &tmQ, 0, q0[u], h, b, q_full);
+        tma_load_4d(sQ + u * kTile + kAtom, &tmQ, 64, q0[u], h, b, q_full);
+      }
       int kst = 0, vst = 0;
       uint32_t kph = 0, vph = 0;
-      for (int j = 0; j < nkv; ++j) {
-        if (!wait_abort(&k_empty[kst], kph ^ 1, p.err, 0xB2200001u, abort_flag)) break;
+      for (int j = 0; j < nkv_max; ++j) {
+        if (!wait_abort(&k_empty[kst], kph ^ 1, p.err, 0xB2300001u, abort_flag)) break;
         mbar_arrive_expect_tx(&k_full[kst], kTile);
         tma_load_4d(sK + kst * kTile, &tmK, 0, j * BKV, hk, b, &k_full[kst]);
         tma_load_4d(sK + kst * kTile + kAtom, &tmK, 64, j * BKV, hk, b, &k_full[kst]);
-        if (!wait_abort(&v_empty[vst], vph ^ 1, p.err, 0xB2200002u, abort_flag)) break;
+        if (!wait_abort(&v_empty[vst], vph ^ 1, p.err, 0xB2300002u, abort_flag)) break;
         mbar_arrive_expect_tx(&v_full[vst], kTile);
         tma_load_4d(sV + vst * kTile, &tmV, 0, j * BKV, hk, b, &v_full[vst]);
         tma_load_4d(sV + vst * kTile + kAtom, &tmV, 64, j * BKV, hk, b, &v_full[vst]);
@@ -175,100 +214,110 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     if (lane == 0) {
       constexpr uint32_t idS = tc::idesc_f16(BQ, BKV, !F16);
       constexpr uint32_t idPV = tc::idesc_f16(BQ, HD, !F16, false, true);
-      bool ok = wait_abort(q_full, 0, p.err, 0xB2200003u, abort_flag);
+      bool ok = wait_abort(q_full, 0, p.err, 0xB2300003u, abort_flag);
       int kst = 0, vst = 0;
       uint32_t kph = 0, vph = 0;
-      auto issue_pv = [&](int jj) -> bool {
-        if (!wait_abort(p_ready, jj & 1, p.err, 0xB2200005u, abort_flag)) return false;
-        if (!wait_abort(&v_full[vst], vph, p.err, 0xB2200006u, abort_flag)) return false;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t da = tc::smem_desc(sP + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024, tc::kSwizzle128B);
-          const uint64_t db = tc::smem_desc(sV + vst * kTile + kk * 16 * 128, kAtom, 1024, tc::kSwizzle128B);
-          tc::mma_f16_ss(tO, da, db, idPV, (jj | kk) != 0);
-        }
-        tc::commit(pv_done);
-        tc::commit(&v_empty[vst]);
-        if (++vst == kVStages) { vst = 0; vph ^= 1; }
-        return true;
-      };
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int sb = j & 1;
-        // S buffer sb was last read by softmax_{j-2}
-        if (!wait_abort(&s_free[sb], ((j >> 1) & 1) ^ 1, p.err, 0xB2200004u, abort_flag) ||
-            !wait_abort(&k_full[kst], kph, p.err, 0xB2200007u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
+      auto issue_s = [&](int u) {
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t da = tc::desc_kmajor_sw128(sQ + (kk >> 2) * kAtom + (kk & 3) * 32);
+          const uint64_t da = tc::desc_kmajor_sw128(sQ + u * kTile + (kk >> 2) * kAtom + (kk & 3) * 32);
           const uint64_t db = tc::desc_kmajor_sw128(sK + kst * kTile + (kk >> 2) * kAtom + (kk & 3) * 32);
-          tc::mma_f16_ss(tS0 + sb * 128, da, db, idS, kk != 0);
+          tc::mma_f16_ss(tmem + 256 * u, da, db, idS, kk != 0);
         }
-        tc::commit(&s_full[sb]);
-        tc::commit(&k_empty[kst]);
-        if (++kst == kKStages) { kst = 0; kph ^= 1; }
-        if (j >= 1 && !issue_pv(j - 1)) {
+        tc::commit(&s_full[u]);
+      };
+      // prologue: S_u(0)
+      if (ok && nkv_max > 0) {
+        ok = wait_abort(&k_full[kst], kph, p.err, 0xB2300004u, abort_flag);
+        if (ok) {
+          tc::fence_after_sync();
+          for (int u = 0; u < 2; ++u)
+            if (nkv[u] > 0) issue_s(u);
+          tc::commit(&k_empty[kst]);
+          if (++kst == kKStages) { kst = 0; kph ^= 1; }
+        }
+      }
+      for (int j = 0; j < nkv_max && ok; ++j) {
+        if (!wait_abort(&v_full[vst], vph, p.err, 0xB2300005u, abort_flag)) {
           ok = false;
           break;
         }
+        const bool next_k = (j + 1 < nkv[0]) || (j + 1 < nkv[1]);
+        bool k_waited = false;
+        for (int u = 0; u < 2 && ok; ++u) {
+          if (j >= nkv[u]) continue;
+          if (!wait_abort(&p_ready[u], j & 1, p.err, 0xB2300006u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            const uint64_t db = tc::smem_desc(sV + vst * kTile + kk * 16 * 128, kAtom, 1024, tc::kSwizzle128B);
+            mma_f16_ts(tmem + 256 * u + 128, tmem + 256 * u + kk * 8, db, idPV, (j | kk) != 0);
+          }
+          if (j == nkv[u] - 1) tc::commit(&o_done[u]);
+          if (j + 1 < nkv[u]) {
+            if (!k_waited) {
+              if (!wait_abort(&k_full[kst], kph, p.err, 0xB2300007u, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc::fence_after_sync();
+              k_waited = true;
+            }
+            issue_s(u);
+          }
+        }
+        if (!ok) break;
+        tc::commit(&v_empty[vst]);
+        if (++vst == kVStages) { vst = 0; vph ^= 1; }
+        if (next_k) {
+          tc::commit(&k_empty[kst]);
+          if (++kst == kKStages) { kst = 0; kph ^= 1; }
+        }
       }
-      if (ok && nkv > 0) ok = issue_pv(nkv - 1);
       if (!ok) {
         tc::commit(drain);
-        mbar_wait(drain, 0, p.err, 0xB2200008u);
+        mbar_wait(drain, 0, p.err, 0xB2300008u);
       }
     }
   } else if (warp >= 4) {
     // -------------------------------- softmax --------------------------------
+    const int u = (warp - 4) >> 2;
     const int qw = warp & 3;
-    const int r = qw * 32 + lane;  // row within the tile == TMEM lane
-    const int qpos = q0 + r;
+    const int r = qw * 32 + lane;
+    const int qpos = q0[u] + r;
     const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+    const uint32_t tS = tmem + 256 * u + lane_off, tO = tS + 128;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int sb = j & 1;
-      if (!wait_abort(&s_full[sb], (j >> 1) & 1, p.err, 0xB2200009u, abort_flag)) {
+    for (int j = 0; j < nkv[u] && ok; ++j) {
+      if (!wait_abort(&s_full[u], j & 1, p.err, 0xB2300009u, abort_flag)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
-      uint32_t s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t (&part)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]);
-        tc::tmem_ld_32x32b_x32(tS0 + sb * 128 + lane_off + 32 * c, part);
-      }
-      tc::tmem_ld_wait();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
-      // scale into the log2 domain and mask
       const int kv0 = j * BKV;
-      const bool need_mask = (p.causal && kv0 + BKV - 1 > q0) || kv0 + BKV > p.Skv;
+      const bool need_mask = (p.causal && kv0 + BKV - 1 > q0[u]) || kv0 + BKV > p.Skv;
+      // pass 1: row max (scaled, masked)
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32];
+        tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
+        tc::tmem_ld_wait();
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = __uint_as_float(s[c]) * p.scale_log2;
-        if (need_mask) {
-          const int kv = kv0 + c;
-          if (kv >= p.Skv || (p.causal && kv > qpos)) v = -INFINITY;
+        for (int e = 0; e < 32; ++e) {
+          float v = __uint_as_float(sv[e]) * p.scale_log2;
+          if (need_mask) {
+            const int kv = kv0 + 32 * c + e;
+            if (kv >= p.Skv || (p.causal && kv > qpos)) v = -INFINITY;
+          }
+          mx = fmaxf(mx, v);
         }
-        s[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
       }
-      // PV_{j-1} must be done before O is rescaled or P is overwritten
-      if (j >= 1 && !wait_abort(pv_done, (j - 1) & 1, p.err, 0xB220000Au, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      // Lazy rescale.  tcgen05.ld/st are warp-collective, so the decision to
-      // touch O is taken per warp; each lane applies its own factor.
+      // lazy, warp-uniform rescale of O (O_u is quiescent: PV_u(j-1) finished)
       const bool need = mx > m_used + kRescaleThreshold;
       const float alpha = need ? ((m_used == -INFINITY) ? 0.f : ex2(m_used - mx)) : 1.f;
       if (need) {
@@ -279,24 +328,31 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tc::tmem_ld_32x32b_x32(tO + lane_off + 32 * c, o);
+          tc::tmem_ld_32x32b_x32(tO + 32 * c, o);
           tc::tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st_32x32b_x32(tO + lane_off + 32 * c, o);
+          tmem_st_32x32b_x32(tO + 32 * c, o);
         }
-        tmem_st_wait();
       }
-      // p = exp2(s - m), row sum, bf16 P into the swizzled K-major tile
+      // pass 2: p = exp2(s - m) -> bf16 pairs over the S columns already read
       const float mref = (m_used == -INFINITY) ? 0.f : m_used;
       float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32];
+        tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
+        tc::tmem_ld_wait();
+        uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2(__uint_as_float(s[8 * c + 2 * e]) - mref);
-          const float p1 = ex2(__uint_as_float(s[8 * c + 2 * e + 1]) - mref);
+        for (int e = 0; e < 16; ++e) {
+          float v0 = __uint_as_float(sv[2 * e]) * p.scale_log2, v1 = __uint_as_float(sv[2 * e + 1]) * p.scale_log2;
+          if (need_mask) {
+            const int kv = kv0 + 32 * c + 2 * e;
+            if (kv >= p.Skv || (p.causal && kv > qpos)) v0 = -INFINITY;
+            if (kv + 1 >= p.Skv || (p.causal && kv + 1 > qpos)) v1 = -INFINITY;
+          }
+          const float p0 = ex2(v0 - mref), p1 = ex2(v1 - mref);
           rs += p0 + p1;
           if constexpr (F16) {
             __half2 hv = __floats2half2_rn(p0, p1);
@@ -306,24 +362,23 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             pk[e] = *reinterpret_cast<uint32_t*>(&hv);
           }
         }
-        uint8_t* dst = sP + (c >> 3) * kAtom + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st_32x32b_x16(tS + 16 * c, pk);
       }
       l += rs;
-      tc::fence_proxy_async_smem();
+      tmem_st_wait();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
+      if (lane == 0) mbar_arrive(&p_ready[u]);
     }
-    // epilogue: O / l -> global (rows beyond Sq are not stored)
-    if (ok && nkv > 0 && wait_abort(pv_done, (nkv - 1) & 1, p.err, 0xB220000Bu, abort_flag)) {
+    // epilogue: O_u / l -> global (rows beyond Sq are not stored)
+    if (ok && nkv[u] > 0 && wait_abort(&o_done[u], 0, p.err, 0xB230000Au, abort_flag)) {
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.o + b * p.os_b + h * p.os_h + (int64_t)qpos * p.os_s;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        tc::tmem_ld_32x32b_x32(tO + lane_off + 32 * c, o);
+        tc::tmem_ld_32x32b_x32(tO + 32 * c, o);
         tc::tmem_ld_wait();
         if (qpos < p.Sq) {
           uint32_t pk[16];
@@ -354,7 +409,6 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   }
 }
 
-constexpr size_t kSmem = (size_t)kTile * (2 + kKStages + kVStages) + 1024 + 256;
 
 // ---------------------------------------------------------------------------
 // Generic path: one warp per query row, fp32 online softmax (same update as
@@ -502,13 +556,14 @@ extern "C" int b2_flash_attn_fwd(const void* q, const void* k, const void* v, vo
       p.os_h = os[1];
       p.os_s = os[2];
       p.err = err;
-      dim3 grid(p.q_tiles, (unsigned)Hq, (unsigned)B);
+      dim3 grid((p.q_tiles + 1) / 2, (unsigned)Hq, (unsigned)B);
       if (f16) {
-        cudaFuncSetAttribute(fa::fa_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa::kSmem);
-        fa::fa_fwd_kernel<true><<<grid, fa::kThreads, fa::kSmem, st>>>(tq, tk, tv, p);
+        cudaFuncSetAttribute(fa::fa_fwd2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa::kSmem2);
+        fa::fa_fwd2_kernel<true><<<grid, fa::kThreads2, fa::kSmem2, st>>>(tq, tk, tv, p);
       } else {
-        cudaFuncSetAttribute(fa::fa_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa::kSmem);
-        fa::fa_fwd_kernel<false><<<grid, fa::kThreads, fa::kSmem, st>>>(tq, tk, tv, p);
+        cudaFuncSetAttribute(fa::fa_fwd2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)fa::kSmem2);
+        fa::fa_fwd2_kernel<false><<<grid, fa::kThreads2, fa::kSmem2, st>>>(tq, tk, tv, p);
       }
       return launch_status("fa_fwd");
     }
