@@ -121,6 +121,64 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Row max of the raw S row (this thread's TMEM lane), masked keys -> -inf.
+template <bool MASK, bool F16>
+__device__ __forceinline__ float row_max(uint32_t tS, int kv0, int qpos, const Params& p) {
+  float mx = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t sv[32];
+    tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      float v = __uint_as_float(sv[e]);
+      if constexpr (MASK) {
+        const int kv = kv0 + 32 * c + e;
+        if (kv >= p.Skv || (p.causal && kv > qpos)) v = -INFINITY;
+      }
+      mx = fmaxf(mx, v);
+    }
+  }
+  return mx;
+}
+
+// p = exp2(s * scale_log2 - m) written as 16-bit pairs over the S columns
+// (P for the TMEM-A MMA); returns the row sum of p.
+template <bool MASK, bool F16>
+__device__ __forceinline__ float exp_to_p(uint32_t tS, int kv0, int qpos, float mref, const Params& p) {
+  float rs0 = 0.f, rs1 = 0.f;
+  const float sc = p.scale_log2;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t sv[32];
+    tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
+    tc::tmem_ld_wait();
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float p0 = ex2(fmaf(__uint_as_float(sv[2 * e]), sc, -mref));
+      float p1 = ex2(fmaf(__uint_as_float(sv[2 * e + 1]), sc, -mref));
+      if constexpr (MASK) {
+        const int kv = kv0 + 32 * c + 2 * e;
+        if (kv >= p.Skv || (p.causal && kv > qpos)) p0 = 0.f;
+        if (kv + 1 >= p.Skv || (p.causal && kv + 1 > qpos)) p1 = 0.f;
+      }
+      rs0 += p0;
+      rs1 += p1;
+      if constexpr (F16) {
+        __half2 hv = __floats2half2_rn(p0, p1);
+        pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+      } else {
+        __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
+        pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+      }
+    }
+    tmem_st_32x32b_x16(tS + 16 * c, pk);
+  }
+  return rs0 + rs1;
+}
+
 template <bool F16>
 __global__ void __launch_bounds__(kThreads2, 1)
 fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -300,23 +358,9 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       tc::fence_after_sync();
       const int kv0 = j * BKV;
       const bool need_mask = (p.causal && kv0 + BKV - 1 > q0[u]) || kv0 + BKV > p.Skv;
-      // pass 1: row max (scaled, masked)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float v = __uint_as_float(sv[e]) * p.scale_log2;
-          if (need_mask) {
-            const int kv = kv0 + 32 * c + e;
-            if (kv >= p.Skv || (p.causal && kv > qpos)) v = -INFINITY;
-          }
-          mx = fmaxf(mx, v);
-        }
-      }
+      // pass 1: row max of the raw scores (scale > 0 commutes with max)
+      float mx = need_mask ? row_max<true, F16>(tS, kv0, qpos, p) : row_max<false, F16>(tS, kv0, qpos, p);
+      mx *= p.scale_log2;
       // lazy, warp-uniform rescale of O (O_u is quiescent: PV_u(j-1) finished)
       const bool need = mx > m_used + kRescaleThreshold;
       const float alpha = need ? ((m_used == -INFINITY) ? 0.f : ex2(m_used - mx)) : 1.f;
@@ -335,35 +379,10 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           tmem_st_32x32b_x32(tO + 32 * c, o);
         }
       }
-      // pass 2: p = exp2(s - m) -> bf16 pairs over the S columns already read
+      // pass 2: p = exp2(s * scale - m) -> bf16 pairs over the S columns already read
       const float mref = (m_used == -INFINITY) ? 0.f : m_used;
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
-        tc::tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float v0 = __uint_as_float(sv[2 * e]) * p.scale_log2, v1 = __uint_as_float(sv[2 * e + 1]) * p.scale_log2;
-          if (need_mask) {
-            const int kv = kv0 + 32 * c + 2 * e;
-            if (kv >= p.Skv || (p.causal && kv > qpos)) v0 = -INFINITY;
-            if (kv + 1 >= p.Skv || (p.causal && kv + 1 > qpos)) v1 = -INFINITY;
-          }
-          const float p0 = ex2(v0 - mref), p1 = ex2(v1 - mref);
-          rs += p0 + p1;
-          if constexpr (F16) {
-            __half2 hv = __floats2half2_rn(p0, p1);
-            pk[e] = *reinterpret_cast<uint32_t*>(&hv);
-          } else {
-            __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
-            pk[e] = *reinterpret_cast<uint32_t*>(&hv);
-          }
-        }
-        tmem_st_32x32b_x16(tS + 16 * c, pk);
-      }
+      const float rs = need_mask ? exp_to_p<true, F16>(tS, kv0, qpos, mref, p)
+                                 : exp_to_p<false, F16>(tS, kv0, qpos, mref, p);
       l += rs;
       tmem_st_wait();
       tc::fence_before_sync();
