@@ -32,11 +32,8 @@ namespace b2 {
 namespace kda {
 
 constexpr int C = 64, DK = 128, DV = 128;
-constexpr int kAThreads = 256;
 constexpr int VB = 16;  // state columns per CTA in kernel B
 constexpr int kBThreads = 256;
-constexpr int LDA = C + 1;   // padded row stride of the 64 x 64 matrices
-constexpr int LDK = DK + 1;  // padded row stride of the 64 x 128 tiles (kernel A)
 constexpr int LDS = DK + 4;  // padded, 16-byte aligned row stride (kernel B)
 
 // Workspace block per (b, h, chunk), floats
@@ -54,166 +51,6 @@ template <typename T>
 __device__ __forceinline__ float ld(const T* p) {
   if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float*>(p);
   else return to_f32<T>(*p);
-}
-
-// smem layout of kernel A (floats)
-constexpr int kAK = 0;
-constexpr int kAQ = kAK + C * LDK;
-constexpr int kAG = kAQ + C * LDK;
-constexpr int kAV = kAG + C * LDK;
-constexpr int kAAkk = kAV + C * LDK;
-constexpr int kAAqk = kAAkk + C * LDA;
-constexpr int kAT = kAAqk + C * LDA;
-constexpr int kAKg = kAT + C * LDA;
-constexpr int kABeta = kAKg + C * LDK;
-constexpr int kAFloats = kABeta + C;
-constexpr size_t kASmem = (size_t)kAFloats * 4;
-
-template <typename T>
-__global__ void __launch_bounds__(kAThreads, 1)
-kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                 const float* __restrict__ g, const T* __restrict__ beta, float* __restrict__ ws, int B, int Tlen,
-                 int H, float scale) {
-  extern __shared__ float sm[];
-  float* sK = sm + kAK;
-  float* sQ = sm + kAQ;
-  float* sG = sm + kAG;
-  float* sV = sm + kAV;
-  float* sA = sm + kAAkk;
-  float* sAq = sm + kAAqk;
-  float* sT = sm + kAT;
-  float* sKg = sm + kAKg;
-  float* sBeta = sm + kABeta;
-  const int nc = Tlen / C;
-  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x;
-  const int64_t row0 = ((int64_t)b * Tlen + (int64_t)chunk * C) * H + h;  // (b, t0, h)
-  // ---- load the chunk ----
-  for (int e = tid; e < C * DK; e += kAThreads) {
-    const int t = e / DK, d = e % DK;
-    const int64_t off = (row0 + (int64_t)t * H) * DK + d;
-    sK[t * LDK + d] = ld(k + off);
-    sQ[t * LDK + d] = ld(q + off) * scale;
-    sG[t * LDK + d] = g[off];
-  }
-  for (int e = tid; e < C * DV; e += kAThreads) {
-    const int t = e / DV, d = e % DV;
-    sV[t * LDK + d] = ld(v + (row0 + (int64_t)t * H) * DV + d);
-  }
-  if (tid < C) sBeta[tid] = ld(beta + row0 + (int64_t)tid * H);
-  __syncthreads();
-  // ---- cumulative decay G (per channel) ----
-  if (tid < DK) {
-    float acc = 0.f;
-    for (int t = 0; t < C; ++t) {
-      acc += sG[t * LDK + tid];
-      sG[t * LDK + tid] = acc;
-    }
-  }
-  __syncthreads();
-  // ---- A_kk (j < i) and A_qk (j <= i), 4 x 4 blocks, bounded exponents ----
-  if (tid < 136) {
-    // map tid -> (bi, bj) with bj <= bi among 16 x 16 blocks
-    int bi = 0, rem = tid;
-    while (rem > bi) {
-      rem -= bi + 1;
-      ++bi;
-    }
-    const int bj = rem;
-    const int r = 4 * bj + 3;  // reference row: last row of the j block
-    float akk[4][4], aqk[4][4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) akk[a][c] = aqk[a][c] = 0.f;
-    for (int d = 0; d < DK; ++d) {
-      const float gr = sG[r * LDK + d];
-      float ki[4], qi[4], kj[4];
-#pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        const int i = 4 * bi + a, j = 4 * bj + a;
-        const float ei = __expf(sG[i * LDK + d] - gr);
-        const float ej = __expf(gr - sG[j * LDK + d]);
-        ki[a] = sK[i * LDK + d] * ei;
-        qi[a] = sQ[i * LDK + d] * ei;
-        kj[a] = sK[j * LDK + d] * ej;
-      }
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          akk[a][c] += ki[a] * kj[c];
-          aqk[a][c] += qi[a] * kj[c];
-        }
-    }
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int i = 4 * bi + a, j = 4 * bj + c;
-        sA[i * LDA + j] = j < i ? akk[a][c] * sBeta[i] : 0.f;
-        sAq[i * LDA + j] = j <= i ? aqk[a][c] : 0.f;
-      }
-  }
-  // zero the upper blocks
-  for (int e = tid; e < C * C; e += kAThreads) {
-    const int i = e / C, j = e % C;
-    if ((j >> 2) > (i >> 2)) {
-      sA[i * LDA + j] = 0.f;
-      sAq[i * LDA + j] = 0.f;
-    }
-  }
-  __syncthreads();
-  // ---- T = (I + A)^-1, unit lower triangular, forward substitution ----
-  // thread (j, part): column j, terms m = j+1+part, +4, ... ; 4 lanes combine
-  {
-    const int j = tid >> 2, part = tid & 3;
-    for (int i = 0; i < C; ++i) {
-      float s = 0.f;
-      if (j < i)
-        for (int m = j + 1 + part; m < i; m += 4) s += sA[i * LDA + m] * sT[m * LDA + j];
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      if (part == 0) sT[i * LDA + j] = j < i ? -(sA[i * LDA + j] + s) : (j == i ? 1.f : 0.f);
-      __syncthreads();
-    }
-  }
-  for (int e = tid; e < C * DK; e += kAThreads) {
-    const int t = e / DK, d = e % DK;
-    sKg[t * LDK + d] = sK[t * LDK + d] * __expf(sG[t * LDK + d]);
-  }
-  __syncthreads();
-  // ---- W = T diag(beta) (K o e^G), U = T diag(beta) V, and the per-row products ----
-  float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
-  {
-    // thread -> (row i = tid / 4, columns d = tid % 4 + 4 c): interleaved so
-    // the 4 column groups of a row fall in different banks
-    const int i = tid >> 2, cg = tid & 3;
-    float w[32], u[32];
-#pragma unroll
-    for (int c = 0; c < 32; ++c) w[c] = u[c] = 0.f;
-    for (int m = 0; m <= i; ++m) {
-      const float tb = sT[i * LDA + m] * sBeta[m];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int d = cg + 4 * c;
-        w[c] += tb * sKg[m * LDK + d];
-        u[c] += tb * sV[m * LDK + d];
-      }
-    }
-    const float* gl = sG + (C - 1) * LDK;
-#pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const int d = cg + 4 * c;
-      const float gi = sG[i * LDK + d];
-      blk[kWsW + i * DK + d] = w[c];
-      blk[kWsU + i * DV + d] = u[c];
-      blk[kWsQg + i * DK + d] = sQ[i * LDK + d] * __expf(gi);
-      blk[kWsKr + i * DK + d] = sK[i * LDK + d] * __expf(gl[d] - gi);
-    }
-  }
-  for (int e = tid; e < C * C; e += kAThreads) blk[kWsAq + e] = sAq[(e / C) * LDA + (e % C)];
-  if (tid < DK) blk[kWsGl + tid] = __expf(sG[(C - 1) * LDK + tid]);
 }
 
 // ---- tf32 warp MMA (m16n8k8), fp32 accumulate -------------------------------
@@ -235,6 +72,258 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// ---------------------------------------------------------------------------
+// Kernel A: intra-chunk WY/UT transform, one CTA per (b, h, chunk), 8 warps.
+//  1. load K, scale*Q, g (cumsum -> G), V, beta
+//  2. A_kk, A_qk on 16 x 16 blocks:
+//     - off-diagonal blocks (I > J) as tf32 MMAs of bounded operands, with the
+//       first row r = 16 I of block I as exponent reference:
+//         K~_i = K_i e^{G_i - G_r} (i in I),  K^_j = K_j e^{G_r - G_j} (j < r)
+//       (both <= 1 because G is non-increasing);
+//     - diagonal blocks exactly in fp32 on CUDA cores (4 x 4 sub-blocks split
+//       at their own reference rows, 4 threads per sub-block over d).
+//  3. T = (I + A_kk)^-1 blockwise: diagonal 16 x 16 blocks by per-column
+//     forward substitution in registers, then T_IJ = -T_II sum_M A_IM T_MJ.
+//  4. W = T (beta K e^G), U = T (beta V) as tf32 MMAs.
+// ---------------------------------------------------------------------------
+constexpr int LD = DK + 8;   // 136: fragment reads (row g, col t) and (row t, col g) conflict-free
+constexpr int LT = C + 4;    // 68
+constexpr int kA2K = 0;
+constexpr int kA2Q = kA2K + C * LD;   // later: beta K e^G
+constexpr int kA2G = kA2Q + C * LD;
+constexpr int kA2V = kA2G + C * LD;   // later: beta V
+constexpr int kA2A = kA2V + C * LD;
+constexpr int kA2Aq = kA2A + C * LT;
+constexpr int kA2T = kA2Aq + C * LT;
+constexpr int kA2Beta = kA2T + C * LT;
+constexpr int kA2Floats = kA2Beta + C;
+constexpr size_t kA2Smem = (size_t)kA2Floats * 4;
+constexpr int kA2Threads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kA2Threads, 1)
+kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                 const float* __restrict__ g, const T* __restrict__ beta, float* __restrict__ ws, int B, int Tlen,
+                 int H, float scale) {
+  extern __shared__ __align__(16) float sm[];
+  float* sK = sm + kA2K;
+  float* sQ = sm + kA2Q;
+  float* sG = sm + kA2G;
+  float* sV = sm + kA2V;
+  float* sA = sm + kA2A;
+  float* sAq = sm + kA2Aq;
+  float* sT = sm + kA2T;
+  float* sBeta = sm + kA2Beta;
+  const int nc = Tlen / C;
+  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, tq = lane & 3;  // MMA fragment coordinates
+  const int64_t row0 = ((int64_t)b * Tlen + (int64_t)chunk * C) * H + h;
+  float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
+
+  // ---- 1. load ----
+  for (int e = tid; e < C * DK; e += kA2Threads) {
+    const int t = e / DK, d = e % DK;
+    const int64_t off = (row0 + (int64_t)t * H) * DK + d;
+    sK[t * LD + d] = ld(k + off);
+    sQ[t * LD + d] = ld(q + off) * scale;
+    sG[t * LD + d] = g[off];
+    sV[t * LD + d] = ld(v + (row0 + (int64_t)t * H) * DV + d);
+  }
+  if (tid < C) sBeta[tid] = ld(beta + row0 + (int64_t)tid * H);
+  for (int e = tid; e < C * LT; e += kA2Threads) {
+    sA[e] = 0.f;
+    sAq[e] = 0.f;
+  }
+  __syncthreads();
+  if (tid < DK) {
+    float acc = 0.f;
+    for (int t = 0; t < C; ++t) {
+      acc += sG[t * LD + tid];
+      sG[t * LD + tid] = acc;
+    }
+  }
+  __syncthreads();
+
+  // ---- 2a. diagonal 16 x 16 blocks, exact: 4 blocks x 10 lower 4x4 sub-blocks x 4 d-splits ----
+  if (tid < 160) {
+    const int task = tid >> 2, split = tid & 3;
+    const int D = task / 10;
+    int a = 0, rem = task % 10;
+    while (rem > a) {
+      rem -= a + 1;
+      ++a;
+    }
+    const int bsub = rem;  // sub-block (a, bsub), bsub <= a
+    const int ib = 16 * D + 4 * a, jb = 16 * D + 4 * bsub;
+    const int r = jb + 3;  // reference: last row of the j sub-block
+    float akk[4][4], aqk[4][4];
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y) akk[x][y] = aqk[x][y] = 0.f;
+    for (int d = split; d < DK; d += 4) {
+      const float gr = sG[r * LD + d];
+      float ki[4], qi[4], kj[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const float ei = __expf(sG[(ib + x) * LD + d] - gr);
+        ki[x] = sK[(ib + x) * LD + d] * ei;
+        qi[x] = sQ[(ib + x) * LD + d] * ei;
+        kj[x] = sK[(jb + x) * LD + d] * __expf(gr - sG[(jb + x) * LD + d]);
+      }
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+          akk[x][y] += ki[x] * kj[y];
+          aqk[x][y] += qi[x] * kj[y];
+        }
+    }
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y) {
+        akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 1);
+        akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 2);
+        aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 1);
+        aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 2);
+      }
+    if (split == 0) {
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+          const int i = ib + x, j = jb + y;
+          if (j < i) sA[i * LT + j] = akk[x][y] * sBeta[i];
+          if (j <= i) sAq[i * LT + j] = aqk[x][y];
+        }
+    }
+  }
+  // ---- 2b. off-diagonal 16 x 16 blocks on tensor cores: 12 (I, n-tile) tasks ----
+  for (int task = warp; task < 12; task += 8) {
+    const int I = task < 2 ? 1 : (task < 6 ? 2 : 3);
+    const int nt = task - (I == 1 ? 0 : (I == 2 ? 2 : 6));  // n-tile of 8 columns j in [0, 16 I)
+    const int r = 16 * I;
+    float ckk[4] = {0.f, 0.f, 0.f, 0.f}, cqk[4] = {0.f, 0.f, 0.f, 0.f};
+    const int i0 = r + gq, i1 = r + gq + 8, j = 8 * nt + gq;
+#pragma unroll 4
+    for (int ks = 0; ks < DK / 8; ++ks) {
+      const int d0 = 8 * ks + tq, d1 = d0 + 4;
+      const float gr0 = sG[r * LD + d0], gr1 = sG[r * LD + d1];
+      const float e00 = __expf(sG[i0 * LD + d0] - gr0), e10 = __expf(sG[i1 * LD + d0] - gr0);
+      const float e01 = __expf(sG[i0 * LD + d1] - gr1), e11 = __expf(sG[i1 * LD + d1] - gr1);
+      const uint32_t ak0 = tf32(sK[i0 * LD + d0] * e00), ak1 = tf32(sK[i1 * LD + d0] * e10);
+      const uint32_t ak2 = tf32(sK[i0 * LD + d1] * e01), ak3 = tf32(sK[i1 * LD + d1] * e11);
+      const uint32_t aq0 = tf32(sQ[i0 * LD + d0] * e00), aq1 = tf32(sQ[i1 * LD + d0] * e10);
+      const uint32_t aq2 = tf32(sQ[i0 * LD + d1] * e01), aq3 = tf32(sQ[i1 * LD + d1] * e11);
+      const uint32_t b0 = tf32(sK[j * LD + d0] * __expf(gr0 - sG[j * LD + d0]));
+      const uint32_t b1 = tf32(sK[j * LD + d1] * __expf(gr1 - sG[j * LD + d1]));
+      mma_tf32(ckk, ak0, ak1, ak2, ak3, b0, b1);
+      mma_tf32(cqk, aq0, aq1, aq2, aq3, b0, b1);
+    }
+    // c0,c1: row i0, cols 8nt+2tq (+1); c2,c3: row i1
+    const int jc = 8 * nt + 2 * tq;
+    sA[i0 * LT + jc] = ckk[0] * sBeta[i0];
+    sA[i0 * LT + jc + 1] = ckk[1] * sBeta[i0];
+    sA[i1 * LT + jc] = ckk[2] * sBeta[i1];
+    sA[i1 * LT + jc + 1] = ckk[3] * sBeta[i1];
+    sAq[i0 * LT + jc] = cqk[0];
+    sAq[i0 * LT + jc + 1] = cqk[1];
+    sAq[i1 * LT + jc] = cqk[2];
+    sAq[i1 * LT + jc + 1] = cqk[3];
+  }
+  __syncthreads();
+
+  // ---- 3a. outputs that need raw Q / K; then beta K e^G into sQ, beta V into sV ----
+  {
+    const float* glr = sG + (C - 1) * LD;
+    for (int e = tid; e < C * DK; e += kA2Threads) {
+      const int t = e / DK, d = e % DK;
+      const float gi = sG[t * LD + d], kk = sK[t * LD + d], bt = sBeta[t];
+      blk[kWsQg + t * DK + d] = sQ[t * LD + d] * __expf(gi);
+      blk[kWsKr + t * DK + d] = kk * __expf(glr[d] - gi);
+      sQ[t * LD + d] = bt * kk * __expf(gi);
+      sV[t * LD + d] *= bt;
+    }
+    for (int e = tid; e < C * C; e += kA2Threads) blk[kWsAq + e] = sAq[(e / C) * LT + (e % C)];
+    if (tid < DK) blk[kWsGl + tid] = __expf(glr[tid]);
+  }
+  // ---- 3b. diagonal blocks of T: column j of block D solved in registers ----
+  if (tid < C) {
+    const int D = tid >> 4, jj = tid & 15, base = 16 * D;
+    float col[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m)
+        if (m > jj && m < i) s += sA[(base + i) * LT + base + m] * col[m];
+      col[i] = i > jj ? -(sA[(base + i) * LT + base + jj] + s) : (i == jj ? 1.f : 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) sT[(base + i) * LT + base + jj] = col[i];
+  }
+  for (int e = tid; e < C * C; e += kA2Threads) {  // zero T above the diagonal blocks
+    const int i = e / C, jcol = e % C;
+    if ((jcol >> 4) > (i >> 4)) sT[i * LT + jcol] = 0.f;
+  }
+  __syncthreads();
+  // ---- 3c. off-diagonal blocks of T, level by level: T_IJ = -T_II X_IJ, X_IJ = sum_{M=J}^{I-1} A_IM T_MJ ----
+  for (int I = 1; I < 4; ++I) {
+    float xv[3] = {0.f, 0.f, 0.f};
+    const int nel = 256 * I;  // I blocks J = 0..I-1 of 16 x 16
+    // X into sAq's rows of block I (A_qk is no longer needed)
+    for (int e = tid; e < nel; e += kA2Threads) {
+      const int J = e >> 8, ii = (e >> 4) & 15, jj = e & 15;
+      float s = 0.f;
+      for (int m = 16 * J; m < 16 * I; ++m) s += sA[(16 * I + ii) * LT + m] * sT[m * LT + 16 * J + jj];
+      sAq[(16 * I + ii) * LT + 16 * J + jj] = s;
+    }
+    (void)xv;
+    __syncthreads();
+    for (int e = tid; e < nel; e += kA2Threads) {
+      const int J = e >> 8, ii = (e >> 4) & 15, jj = e & 15;
+      float s = 0.f;
+      for (int m = 0; m <= ii; ++m) s += sT[(16 * I + ii) * LT + 16 * I + m] * sAq[(16 * I + m) * LT + 16 * J + jj];
+      sT[(16 * I + ii) * LT + 16 * J + jj] = -s;
+    }
+    __syncthreads();
+  }
+
+  // ---- 4. W = T (beta K e^G), U = T (beta V): warp -> (m-tile w%4, column half w/4) ----
+  {
+    const int mt = warp & 3, nh = warp >> 2;
+    const int r0 = 16 * mt, c0 = 64 * nh;
+    float w[8][4], u[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[n][e] = u[n][e] = 0.f;
+    const int ksteps = 2 * mt + 2;  // T is lower triangular
+    for (int ks = 0; ks < ksteps; ++ks) {
+      const int k0 = 8 * ks;
+      const uint32_t a0 = tf32(sT[(r0 + gq) * LT + k0 + tq]), a1 = tf32(sT[(r0 + gq + 8) * LT + k0 + tq]);
+      const uint32_t a2 = tf32(sT[(r0 + gq) * LT + k0 + tq + 4]), a3 = tf32(sT[(r0 + gq + 8) * LT + k0 + tq + 4]);
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int col = c0 + 8 * n + gq;
+        mma_tf32(w[n], a0, a1, a2, a3, tf32(sQ[(k0 + tq) * LD + col]), tf32(sQ[(k0 + tq + 4) * LD + col]));
+        mma_tf32(u[n], a0, a1, a2, a3, tf32(sV[(k0 + tq) * LD + col]), tf32(sV[(k0 + tq + 4) * LD + col]));
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int col = c0 + 8 * n + 2 * tq;
+      const int ra = r0 + gq, rb = r0 + gq + 8;
+      *reinterpret_cast<float2*>(blk + kWsW + ra * DK + col) = make_float2(w[n][0], w[n][1]);
+      *reinterpret_cast<float2*>(blk + kWsW + rb * DK + col) = make_float2(w[n][2], w[n][3]);
+      *reinterpret_cast<float2*>(blk + kWsU + ra * DV + col) = make_float2(u[n][0], u[n][1]);
+      *reinterpret_cast<float2*>(blk + kWsU + rb * DV + col) = make_float2(u[n][2], u[n][3]);
+    }
+  }
+}
 
 // ---------------------------------------------------------------------------
 // Kernel B: sequential state pass, one CTA per (b, h, 32 state columns).
@@ -523,10 +612,10 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
   cudaFuncSetAttribute(kda::kda_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kB2Smem);
 #define B2_KDA_LAUNCH(TY)                                                                                         \
   do {                                                                                                            \
-    cudaFuncSetAttribute(kda::kda_intra_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kASmem); \
+    cudaFuncSetAttribute(kda::kda_intra_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kA2Smem); \
     cudaFuncSetAttribute(kda::kda_output_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
                          (int)kda::kCSmem);                                                                       \
-    kda::kda_intra_kernel<TY><<<ga, kda::kAThreads, kda::kASmem, st>>>(                                         \
+    kda::kda_intra_kernel<TY><<<ga, kda::kA2Threads, kda::kA2Smem, st>>>(                                         \
         (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale);        \
     kda::kda_state_kernel<<<gb, kda::kB2Threads, kda::kB2Smem, st>>>(ws, initial_state, final_state, (int)B,     \
                                                                      (int)T, (int)H);                           \
