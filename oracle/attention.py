@@ -64,3 +64,39 @@ def gqa_decode(q, k_cache, v_cache, seq_len, scale, n_q_per_kv):
         p = np.exp(s - s.max())
         out[h] = (p / p.sum()) @ vc[kv]
     return out
+
+
+def decode(q, k_cache, v_cache, seq_lens, scale=None):
+    """Single-token decode attention, float64.
+
+    q [B, Hq, D]; k/v [B, Hkv, S, D] (S >= every seq_len); seq_lens [B].
+    kv head of q head h is h // (Hq // Hkv) (_msl_templates.py:2101-2104);
+    keys beyond seq_len are ignored (kv-cache templates, :1949-2063,
+    :2167-2278); an empty sequence gives 0 (the nan_to_num convention of
+    tests/test_flash_attention.py:117).
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k_cache, dtype=np.float64)
+    v = np.asarray(v_cache, dtype=np.float64)
+    B, Hq, D = q.shape
+    rep = Hq // k.shape[1]
+    scale = 1.0 / np.sqrt(D) if scale is None else scale
+    out = np.zeros((B, Hq, D))
+    for b in range(B):
+        n = int(seq_lens[b])
+        if n == 0:
+            continue
+        for h in range(Hq):
+            s = k[b, h // rep, :n] @ q[b, h] * scale
+            p = np.exp(s - s.max())
+            out[b, h] = (p / p.sum()) @ v[b, h // rep, :n]
+    return out
+
+
+def gather_pages(pages, page_table, seq_len):
+    """Paged KV [n_phys_pages, page_size, (H,) D] + logical->physical table ->
+    contiguous [seq_len, (H,) D] (_msl_templates.py:2279-2532)."""
+    pages = np.asarray(pages)
+    ps = pages.shape[1]
+    rows = [pages[int(page_table[t // ps]), t % ps] for t in range(seq_len)]
+    return np.stack(rows) if rows else np.zeros((0,) + pages.shape[2:])

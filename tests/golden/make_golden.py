@@ -131,6 +131,53 @@ def execute(pipe, bufs):
         out = oatt.gqa_decode(q, k, v, S, scale, rep)
         rec.update(seq_len=S, scale=scale, head_dim=D, n_q_per_kv=rep, q=q, k=k, v=v)
         ob = out.astype(np.float32).reshape(-1)
+    elif name in ("kv_cache_attention", "fp16_kv_attention"):
+        D = _const(msl, r"const uint D = (\d+)u")
+        if name == "kv_cache_attention":
+            q_b, k_b, v_b, o_b, sl_b, sc_b = bufs
+            scale = float(np.frombuffer(bytes(sc_b.mem[:4]), dtype=np.float32)[0])
+            k, v = k_b.f32(), v_b.f32()
+        else:
+            q_b, k_b, v_b, o_b, sl_b = bufs
+            scale = 1.0 / math.sqrt(D)
+            k = np.frombuffer(bytes(k_b.mem), dtype=np.float16).astype(np.float32)
+            v = np.frombuffer(bytes(v_b.mem), dtype=np.float16).astype(np.float32)
+        S = sl_b.u32()
+        q = q_b.f32().reshape(-1, D)
+        H = q.shape[0]
+        k = k.reshape(H, -1, D)
+        v = v.reshape(H, -1, D)
+        out = oatt.decode(q[None], k[None], v[None], [S], scale)[0]
+        rec.update(seq_len=S, scale=scale, head_dim=D, q=q, k=k, v=v)
+        ob = out.astype(np.float32).reshape(-1)
+    elif name == "batched_kv_decode":
+        q_b, k_b, v_b, o_b, sl_b, ms_b, bs_b = bufs
+        D = _const(msl, r"const uint D = (\d+)u")
+        H = _const(msl, r"const uint N_HEADS = (\d+)u")
+        Bsz, S = bs_b.u32(), ms_b.u32()
+        lens = np.frombuffer(bytes(sl_b.mem), dtype=np.uint32)[:Bsz]
+        q = q_b.f32()[: Bsz * H * D].reshape(Bsz, H, D)
+        k = k_b.f32()[: Bsz * H * S * D].reshape(Bsz, H, S, D)
+        v = v_b.f32()[: Bsz * H * S * D].reshape(Bsz, H, S, D)
+        out = oatt.decode(q, k, v, lens, 1.0 / math.sqrt(D))
+        rec.update(seq_lens=lens.astype(np.int64), max_seq_len=S, head_dim=D, q=q, k=k, v=v)
+        ob = out.astype(np.float32).reshape(-1)
+    elif name in ("paged_attention", "multi_head_paged_attention"):
+        q_b, k_b, v_b, pt_b, o_b, sl_b, np_b = bufs
+        D = _const(msl, r"const uint D = (\d+)u")
+        ps = _const(msl, r"const uint PAGE_SIZE = (\d+)u")
+        S, npg = sl_b.u32(), np_b.u32()
+        table = np.frombuffer(bytes(pt_b.mem), dtype=np.uint32)[:npg]
+        q = q_b.f32().reshape(-1, D)
+        H = q.shape[0]
+        kp = k_b.f32().reshape(-1, ps, H, D) if name.startswith("multi") else k_b.f32().reshape(-1, ps, 1, D)
+        vp = v_b.f32().reshape(-1, ps, H, D) if name.startswith("multi") else v_b.f32().reshape(-1, ps, 1, D)
+        kc = oatt.gather_pages(kp, table, S).transpose(1, 0, 2)  # [H, S, D]
+        vc = oatt.gather_pages(vp, table, S).transpose(1, 0, 2)
+        out = oatt.decode(q[None], kc[None], vc[None], [S], 1.0 / math.sqrt(D))[0]
+        rec.update(seq_len=S, n_pages=npg, page_size=ps, head_dim=D, page_table=table.astype(np.int64),
+                   q=q, k=kp, v=vp)
+        ob = out.astype(np.float32).reshape(-1)
     else:
         raise KeyError(name)
     o_b.mem[: ob.nbytes] = ob.tobytes()
@@ -235,6 +282,14 @@ REFERENCE_TESTS = [
     ("test_causal_attention_gpu", "tests/test_emitter.py:5505"),
     ("test_gqa_attention", "tests/test_emitter.py:2482"),
     ("test_gqa_attention_gpu", "tests/test_emitter.py:5717"),
+    ("test_kv_cache_attention", "tests/test_emitter.py:2124"),
+    ("test_kv_cache_attention_gpu", "tests/test_emitter.py:5652"),
+    ("test_batched_kv_decode", "tests/test_emitter.py:2908"),
+    ("test_paged_attention", "tests/test_emitter.py:3188"),
+    ("test_paged_attention_partial_page", "tests/test_emitter.py:3283"),
+    ("test_paged_attention_gpu", "tests/test_emitter.py:5786"),
+    ("test_multi_head_paged_attention", "tests/test_emitter.py:3710"),
+    ("test_fp16_kv_attention", "tests/test_emitter.py:3809"),
 ]
 
 TRITON_FA_SHAPES = {

@@ -20,7 +20,7 @@ REF_TESTS = {r["test"]: r for r in MANIFEST["reference_tests"]}
 
 
 def test_every_reference_test_accepted_the_oracle():
-    assert len(REF_TESTS) == 11
+    assert len(REF_TESTS) == 19
     for name, rec in REF_TESTS.items():
         assert rec["reference_test_passed"], (name, rec["error"])
 
@@ -38,8 +38,16 @@ def test_oracle_matches_reference_expected(name):
     elif rec["kernel"] in ("flash_attention", "causal_attention"):
         out = oatt.flash_attention_template(g["q"], g["k"], g["v"], rec["seq_len"], rec["scale"],
                                             rec["head_dim"], causal=rec["causal"])
-    else:
+    elif rec["kernel"] == "gqa_attention":
         out = oatt.gqa_decode(g["q"], g["k"], g["v"], rec["seq_len"], rec["scale"], rec["n_q_per_kv"])
+    elif rec["kernel"] in ("kv_cache_attention", "fp16_kv_attention"):
+        out = oatt.decode(g["q"][None], g["k"][None], g["v"][None], [rec["seq_len"]], rec["scale"])
+    elif rec["kernel"] == "batched_kv_decode":
+        out = oatt.decode(g["q"], g["k"], g["v"], g["seq_lens"], 1.0 / np.sqrt(rec["head_dim"]))
+    else:  # paged
+        kc = oatt.gather_pages(g["k"], g["page_table"], rec["seq_len"]).transpose(1, 0, 2)
+        vc = oatt.gather_pages(g["v"], g["page_table"], rec["seq_len"]).transpose(1, 0, 2)
+        out = oatt.decode(g["q"][None], kc[None], vc[None], [rec["seq_len"]], 1.0 / np.sqrt(rec["head_dim"]))
     np.testing.assert_allclose(out.reshape(-1), g["expected"], rtol=1e-5, atol=1e-5)
 
 
