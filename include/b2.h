@@ -129,6 +129,31 @@ B2_API int b2_flash_attn_fwd(const void* q, const void* k, const void* v, void* 
                       float scale, int causal, int dtype, void* stream);
 
 /*
+ * Decode attention: one query token per head over a KV cache, split-KV.
+ * Replaces kv_cache_attention, gqa_attention, batched_kv_decode,
+ * paged_attention, multi_head_paged_attention and fp16_kv_attention
+ * (triton_metal/codegen/_msl_templates.py:1949-2627).
+ *   q [B, Hq, D] (q_dtype), o like q.
+ *   page_size == 0: contiguous K/V [B, Hkv, S, D], k/v_strides = element
+ *                   strides (b, h, s).
+ *   page_size  > 0: paged K/V [n_pages, page_size, Hkv, D], page_table
+ *                   int32 [B, max_pages] (logical -> physical page),
+ *                   k/v_strides = element strides (page, token, head).
+ *   seq_lens int32 [B] (<= max_seq_len); kv head of q head h = h / (Hq/Hkv).
+ *   kv_dtype may differ from q_dtype (fp16 KV with fp32 queries).
+ *   workspace: b2_decode_attn_workspace_size(...) bytes (NULL when it is 0).
+ */
+B2_API size_t b2_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t Hkv,
+                                            int64_t D, int64_t max_seq_len);
+B2_API int b2_decode_attn(const void* q, const void* k, const void* v, void* o,
+                          const int32_t* page_table, const int32_t* seq_lens,
+                          void* workspace, int64_t B, int64_t Hq, int64_t Hkv,
+                          int64_t D, int64_t max_seq_len, int64_t page_size,
+                          int64_t max_pages, const int64_t* k_strides,
+                          const int64_t* v_strides, float scale, int q_dtype,
+                          int kv_dtype, void* stream);
+
+/*
  * KDA (chunked gated delta rule) forward.  No reference counterpart: the
  * reference has no KDA code.  Layout [B, T, H, D] contiguous:
  *   q, k, v : dtype (B2_BF16) [B,T,H,Dk|Dv];  g : fp32 [B,T,H,Dk] log-decay

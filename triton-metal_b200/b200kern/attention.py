@@ -75,7 +75,88 @@ def gqa_attention(q, k_cache, v_cache, seq_len, scale, n_q_per_kv):
     hkv = k_cache.numel() // (seq_len * d)
     if hq != hkv * n_q_per_kv:
         raise B2ShapeError(f"{hq} q heads != {hkv} kv heads x {n_q_per_kv}")
-    qq = q.reshape(1, hq, 1, d)
     kk = k_cache.reshape(1, hkv, seq_len, d)
     vv = v_cache.reshape(1, hkv, seq_len, d)
-    return flash_attention(qq, kk, vv, causal=False, scale=scale).reshape(hq, d)
+    return decode_attention(q.reshape(1, hq, d), kk, vv, seq_len, scale).reshape(hq, d)
+
+
+# --------------------------------------------------------------------------
+# decode attention over a KV cache (one query token per head)
+# --------------------------------------------------------------------------
+def _seq_lens(seq_lens, B, device):
+    if isinstance(seq_lens, int):
+        return torch.full((B,), seq_lens, dtype=torch.int32, device=device)
+    return seq_lens.to(device=device, dtype=torch.int32).contiguous()
+
+
+def decode_attention(q, k_cache, v_cache, seq_lens, scale=None, page_table=None, out=None):
+    """o[B, Hq, D] = softmax(scale q K^T) V over the first seq_lens[b] keys.
+
+    Contiguous cache: k/v [B, Hkv, S, D] (any strides, last dim contiguous).
+    Paged cache (page_table int32 [B, max_pages] given): k/v
+    [n_pages, page_size, Hkv, D].  GQA: kv head = q head // (Hq // Hkv).
+    The cache dtype may differ from q's (e.g. fp16 KV with fp32 queries)."""
+    for t in (q, k_cache, v_cache):
+        if not t.is_cuda:
+            raise B2ShapeError("b200kern ops take CUDA tensors (there is no CPU path)")
+    if q.dim() != 3:
+        raise B2ShapeError("q must be [B, Hq, D]")
+    if q.dtype not in _DT or k_cache.dtype not in _DT or v_cache.dtype != k_cache.dtype:
+        raise B2DtypeError("q and the cache must be fp32, fp16 or bf16")
+    B, Hq, D = q.shape
+    if k_cache.stride(-1) != 1:
+        k_cache = k_cache.contiguous()
+    if v_cache.stride(-1) != 1:
+        v_cache = v_cache.contiguous()
+    if page_table is None:
+        Hkv, S = k_cache.shape[1], k_cache.shape[2]
+        ks, vs = k_cache.stride()[:3], v_cache.stride()[:3]
+        ps, max_pages, pt = 0, 0, None
+    else:
+        ps, Hkv = k_cache.shape[1], k_cache.shape[2]
+        pt = page_table.to(device=q.device, dtype=torch.int32).contiguous()
+        max_pages = pt.shape[1]
+        S = max_pages * ps
+        ks, vs = k_cache.stride()[:3], v_cache.stride()[:3]
+    if Hq % Hkv:
+        raise B2ShapeError(f"Hq={Hq} must be a multiple of Hkv={Hkv}")
+    lens = _seq_lens(seq_lens, B, q.device)
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    q = q.contiguous()
+    o = out if out is not None else torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
+    lib = _lib.load()
+    need = int(lib.b2_decode_attn_workspace_size(B, Hq, Hkv, D, S))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    _lib.call("b2_decode_attn", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(),
+              None if pt is None else pt.data_ptr(), lens.data_ptr(), ws.data_ptr(), B, Hq, Hkv, D, S, ps,
+              max_pages, _lib.strides_arg(ks), _lib.strides_arg(vs), scale, _DT[q.dtype], _DT[k_cache.dtype],
+              _stream())
+    return o
+
+
+def kv_cache_attention(Q, K_cache, V_cache, seq_len, scale):
+    """Reference kv_cache_attention buffers: Q [H, D], caches [H, max_seq, D]."""
+    H, D = Q.shape
+    K = K_cache.reshape(1, H, -1, D)
+    V = V_cache.reshape(1, H, -1, D)
+    return decode_attention(Q.reshape(1, H, D), K, V, seq_len, scale).reshape(H, D)
+
+
+def batched_kv_decode(Q, K_cache, V_cache, seq_lens, max_seq_len):
+    """Reference batched_kv_decode: Q [B, H, D], caches [B, H, max_seq_len, D]."""
+    B, H, D = Q.shape
+    K = K_cache.reshape(B, H, max_seq_len, D)
+    V = V_cache.reshape(B, H, max_seq_len, D)
+    return decode_attention(Q, K, V, seq_lens)
+
+
+def paged_attention(Q, K_pages, V_pages, page_table, seq_len, n_pages, page_size):
+    """Reference paged_attention (one head: K_pages [P, page_size, D]) and
+    multi_head_paged_attention (Q [H, D], K_pages [P, page_size, H, D])."""
+    D = Q.shape[-1]
+    Qh = Q.reshape(1, -1, D)
+    H = Qh.shape[1]
+    K = K_pages.reshape(-1, page_size, H, D)
+    V = V_pages.reshape(-1, page_size, H, D)
+    pt = page_table.reshape(1, -1)[:, :n_pages]
+    return decode_attention(Qh, K, V, seq_len, page_table=pt).reshape(Q.shape)
