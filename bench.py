@@ -530,7 +530,96 @@ class KDA:
                           "scaled linearly"}
 
 
-WORKLOADS = {"kda": KDA, "fa_gqa": FlashAttn, "w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
+# --------------------------------------------------------------------------
+# workload: split-KV decode attention over a long KV cache
+# --------------------------------------------------------------------------
+class Decode:
+    """B=32 sequences, Hq=32, Hkv=8, S=8192 cached tokens, D=128, bf16 q and KV
+    cache (1.07 GB > L2); q/k/v = 0.5 N(0,1). One step = one decode token for
+    every sequence (split-KV kernel + combine kernel)."""
+    name = "decode"
+    metric = "GQA decode attention KV-cache read bandwidth"
+    unit = "tokens/s"
+    dtype = "bf16"
+    bound = "hbm"
+
+    def __init__(self, rank, B=32, Hq=32, Hkv=8, S=8192, D=128):
+        import b200kern as bk
+        self.bk, self.B, self.Hq, self.Hkv, self.S, self.D = bk, B, Hq, Hkv, S, D
+        g = torch.Generator().manual_seed(rank)
+        self.q_host = (torch.randn(B, Hq, D, generator=g) * 0.5).bfloat16().pin_memory()
+        self.k = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).bfloat16().cuda()
+        self.v = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).bfloat16().cuda()
+        self.lens = torch.full((B,), S, dtype=torch.int32, device="cuda")
+        self.q = self.q_host.cuda()
+        self.o = torch.empty_like(self.q)
+        self.o_host = torch.empty_like(self.q_host).pin_memory()
+        # algorithmic bytes: the K and V caches once, q and o
+        self.bytes = 2 * B * Hkv * S * D * 2 + 2 * B * Hq * D * 2
+        self.step_work = B              # decoded tokens per step
+        self.value_scale = 1.0
+        self.roof_scale = 1e9
+        self.peak_key, self.peak_unit = "hbm_gbs", "GB/s"
+        self.launches_per_step = 1
+        self.kernels_per_launch = 2     # split kernel + combine kernel
+        self.cfg = {"workload": f"decode B={B} Hq={Hq} Hkv={Hkv} S={S} D={D} kv=bf16",
+                    "algorithmic_bytes": self.bytes, "l2": "KV cache 1.07 GB > 126 MB L2 (no flush needed)",
+                    "kernels_per_step": 2,
+                    "e2e_note": "the KV cache is device-resident state; e2e copies q in and o out per step"}
+
+    def step(self, stream):
+        self.bk.decode_attention(self.q, self.k, self.v, self.lens, out=self.o)
+
+    def launch(self, i, stream):
+        self.step(stream)
+
+    def e2e_step(self):
+        q = self.q_host.to("cuda", non_blocking=True)
+        self.bk.decode_attention(q, self.k, self.v, self.lens, out=self.o)
+        self.o_host.copy_(self.o, non_blocking=True)
+        return self.q_host.numel() * 2, self.o.numel() * 2
+
+    def kernel_work(self):
+        return self.bytes
+
+    def check(self):
+        torch.cuda.synchronize()
+        ok = True
+        rep = self.Hq // self.Hkv
+        for b in (0, self.B - 1):
+            k = self.k[b].double().cpu()
+            v = self.v[b].double().cpu()
+            q = self.q_host[b].double().reshape(self.Hkv, rep, self.D)
+            s = torch.einsum("hrd,hsd->hrs", q, k) / self.D ** 0.5
+            ref = torch.einsum("hrs,hsd->hrd", torch.softmax(s, -1), v).reshape(self.Hq, self.D)
+            got = self.o[b].double().cpu()
+            ok &= bool(((got - ref).abs() <= 1e-2 + 1e-2 * ref.abs()).all())
+        return ok
+
+    def cpu_baseline(self, budget_s=10.0):
+        """The reference's KV-cache decode check (tests/test_emitter.py:2124,
+        softmax(q k^T * scale) v per head) restated in fp32 torch on all host
+        threads, on a sample of sequences, scaled to B."""
+        threads = os.cpu_count()
+        torch.set_num_threads(threads)
+        rep = self.Hq // self.Hkv
+        kc = self.k[:2].float().cpu()
+        vc = self.v[:2].float().cpu()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            b = n % 2
+            q = self.q_host[b].float().reshape(self.Hkv, rep, self.D)
+            s = torch.einsum("hrd,hsd->hrs", q, kc[b]) * (1.0 / self.D ** 0.5)
+            torch.einsum("hrs,hsd->hrd", torch.softmax(s, -1), vc[b])
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or n >= 64:
+                break
+        return {"value": n / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": f"{n} sequences of {self.B} (S={self.S}) in {el:.1f} s; value = sequences decoded per second"}
+
+
+WORKLOADS = {"decode": Decode, "kda": KDA, "fa_gqa": FlashAttn, "w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
 
 
 def make_workload(args, rank):
@@ -542,6 +631,8 @@ def make_workload(args, rank):
         return FlashAttn(rank)
     if args.workload == "kda":
         return KDA(rank)
+    if args.workload == "decode":
+        return Decode(rank)
     raise SystemExit(f"unknown workload {args.workload}")
 
 

@@ -20,6 +20,7 @@
 // [B, max_pages] (logical -> physical page); seq_lens [B].  The KV dtype may
 // differ from the query dtype (fp16 KV with fp32 queries).
 #include "b2_common.cuh"
+#include <type_traits>
 
 namespace b2 {
 namespace dec {
@@ -196,6 +197,262 @@ __global__ void decode_combine_kernel(const Params p) {
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Tensor-core path: 16-bit q and KV cache of the same type, D in {64, 128, 256}.
+//
+// A CTA streams its split of one (batch, kv head) through a STAGES-deep ring
+// of 64-key K/V tiles filled by 16-byte cp.async (zero-filled past the
+// sequence end, so every tile is the same shape).  Tiles are stored
+// row-major with the 16-byte chunks of a row XOR-swizzled by (row & 7) so the
+// 8 row addresses of an ldmatrix hit 8 different bank groups.  Warp w owns
+// keys [16w, 16w + 16) of every tile and keeps its own online-softmax state:
+//   S[16 x 16]  = Q[16 x D] . K_w^T       (rows = the rep query heads, zero
+//                                          padded to 16; mma m16n8k16)
+//   O[16 x D]  += exp2(S - m) . V_w        (P re-used from the accumulator
+//                                          registers as the A operand)
+// The 4 warps' (m, l, O) are merged through shared memory at the end.
+// Per 64-key tile each warp issues 16 ldmatrix + 32 MMAs for D = 128, far
+// below the ~1400 SM cycles the tile's 32 KB take at the CTA's share of HBM
+// bandwidth, so the kernel is bound by the copy stream.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_grp() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_grp() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __half>::value) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+template <int D>
+struct TcCfg {
+  static constexpr int kStages = D == 64 ? 6 : (D == 128 ? 3 : 3);
+  static constexpr int kRowBytes = D * 2;
+  static constexpr int kTileBytes = TK * kRowBytes;           // one of K or V
+  static constexpr int kQBytes = 16 * kRowBytes;
+  static constexpr int kSmem = kQBytes + kStages * 2 * kTileBytes;
+  static constexpr int kChunks = D / 8;                       // 16-byte chunks per row
+  static constexpr int kRowsPerPass = kThreads / kChunks;
+  static_assert(kWarps * D * 16 * 4 + 2 * kWarps * 16 * 4 <= kStages * 2 * kTileBytes, "merge buffer");
+};
+
+// byte offset of 16-byte chunk c of row r in a swizzled [rows][D] 16-bit tile
+template <int D>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return (uint32_t)(r * D * 2 + ((c ^ (r & 7)) << 4));
+}
+
+template <typename T, int D, bool PAGED>
+__global__ void __launch_bounds__(kThreads, D == 256 ? 1 : 2)
+decode_tc_kernel(const Params p) {
+  using C = TcCfg<D>;
+  constexpr int DT = std::is_same<T, __half>::value ? B2_F16 : B2_BF16;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sKV = sQ + C::kQBytes;  // stage s: K at sKV + 2s*tile, V after it
+  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rep = p.Hq / p.Hkv;
+  const int len = p.seq_lens[b];
+  const int s0 = split * p.split_len, s1 = min(len, s0 + p.split_len);
+  const int ntiles = s1 > s0 ? (s1 - s0 + TK - 1) / TK : 0;
+
+  // q rows (zero padded to 16) -> swizzled smem; plain stores, made visible
+  // by the first __syncthreads of the main loop.
+  for (int e = tid; e < 16 * C::kChunks; e += kThreads) {
+    const int r = e / C::kChunks, c = e % C::kChunks;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (r < rep) val = *reinterpret_cast<const uint4*>((const T*)p.q + ((int64_t)b * p.Hq + hk * rep + r) * D + c * 8);
+    *reinterpret_cast<uint4*>(smem + swz<D>(r, c)) = val;
+  }
+
+  const T* kb = (const T*)p.k;
+  const T* vb = (const T*)p.v;
+  const int cc = tid % C::kChunks, r0 = tid / C::kChunks;
+  auto load_tile = [&](int t, int stage) {
+    const int base = s0 + t * TK;
+    const uint32_t dk = sKV + stage * 2 * C::kTileBytes, dv = dk + C::kTileBytes;
+#pragma unroll
+    for (int i = 0; i < TK / C::kRowsPerPass; ++i) {
+      const int r = r0 + i * C::kRowsPerPass, pos = base + r;
+      const bool ok = pos < s1;
+      int64_t ko = 0, vo = 0;
+      if (ok) {
+        if constexpr (PAGED) {
+          const int pg = p.page_table[(int64_t)b * p.max_pages + pos / p.page_size];
+          const int off = pos - (pos / p.page_size) * p.page_size;
+          ko = pg * p.ks[0] + off * p.ks[1] + hk * p.ks[2];
+          vo = pg * p.vs[0] + off * p.vs[1] + hk * p.vs[2];
+        } else {
+          ko = b * p.ks[0] + hk * p.ks[1] + (int64_t)pos * p.ks[2];
+          vo = b * p.vs[0] + hk * p.vs[1] + (int64_t)pos * p.vs[2];
+        }
+      }
+      cp_async16_zfill(dk + swz<D>(r, cc), kb + ko + cc * 8, ok);
+      cp_async16_zfill(dv + swz<D>(r, cc), vb + vo + cc * 8, ok);
+    }
+  };
+
+#pragma unroll
+  for (int st = 0; st < C::kStages - 1; ++st) {
+    if (st < ntiles) load_tile(st, st);
+    cp_async_commit_grp();
+  }
+
+  const float sl2 = p.scale * 1.4426950408889634f;  // scores in log2 units
+  const int g = lane >> 2, tq = lane & 3;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g, g + 8
+  float acc[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+
+  // per-lane ldmatrix row/chunk selectors
+  const int qa_row = (lane & 7) + ((lane >> 3) & 1) * 8, qa_chunk = lane >> 4;
+  const int kb_row = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8, kb_chunk = (lane >> 3) & 1;
+  const int vb_row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vb_chunk = lane >> 4;
+
+  for (int t = 0; t < ntiles; ++t) {
+    cp_async_wait_grp<C::kStages - 2>();
+    __syncthreads();  // tile t visible to all; stage (t - 1) % S free
+    {
+      const int tn = t + C::kStages - 1;
+      if (tn < ntiles) load_tile(tn, tn % C::kStages);
+      cp_async_commit_grp();
+    }
+    const int stage = t % C::kStages;
+    const uint32_t tk = sKV + stage * 2 * C::kTileBytes, tv = tk + C::kTileBytes;
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4], bk0[2], bk1[2];
+      ldsm_x4(sQ + swz<D>(qa_row, 2 * kk + qa_chunk), a[0], a[1], a[2], a[3]);
+      ldsm_x4(tk + swz<D>(kb_row, 2 * kk + kb_chunk), bk0[0], bk0[1], bk1[0], bk1[1]);
+      mma_16816<DT>(s[0], a, bk0);
+      mma_16816<DT>(s[1], a, bk1);
+    }
+    // scale, mask the ragged end, online softmax over this warp's 16 keys
+    const int kpos = s0 + t * TK + warp * 16 + 2 * tq;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const bool ok = kpos + j * 8 + (e & 1) < s1;
+        s[j][e] = ok ? s[j][e] * sl2 : -INFINITY;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float ref0 = mn0 == -INFINITY ? 0.f : mn0, ref1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = exp2f(m0 - ref0), al1 = exp2f(m1 - ref1);
+    m0 = mn0;
+    m1 = mn1;
+    float pr[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      pr[j][0] = exp2f(s[j][0] - ref0);
+      pr[j][1] = exp2f(s[j][1] - ref0);
+      pr[j][2] = exp2f(s[j][2] - ref1);
+      pr[j][3] = exp2f(s[j][3] - ref1);
+    }
+    l0 = l0 * al0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
+    l1 = l1 * al1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
+    uint32_t pa[4];
+    pa[0] = pack2<T>(pr[0][0], pr[0][1]);
+    pa[1] = pack2<T>(pr[0][2], pr[0][3]);
+    pa[2] = pack2<T>(pr[1][0], pr[1][1]);
+    pa[3] = pack2<T>(pr[1][2], pr[1][3]);
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+      uint32_t b0[2], b1[2];
+      ldsm_x4_t(tv + swz<D>(vb_row, 2 * np + vb_chunk), b0[0], b0[1], b1[0], b1[1]);
+      acc[2 * np][0] *= al0;
+      acc[2 * np][1] *= al0;
+      acc[2 * np][2] *= al1;
+      acc[2 * np][3] *= al1;
+      acc[2 * np + 1][0] *= al0;
+      acc[2 * np + 1][1] *= al0;
+      acc[2 * np + 1][2] *= al1;
+      acc[2 * np + 1][3] *= al1;
+      mma_16816<DT>(acc[2 * np], pa, b0);
+      mma_16816<DT>(acc[2 * np + 1], pa, b1);
+    }
+  }
+  cp_async_wait_grp<0>();
+  __syncthreads();  // ring no longer read: reuse it for the merge
+
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  float* sO = reinterpret_cast<float*>(smem + C::kQBytes);  // [warp][16][D]
+  float* sM = sO + kWarps * 16 * D;                         // [warp][16]
+  float* sL = sM + kWarps * 16;
+  if (tq == 0) {
+    sM[warp * 16 + g] = m0;
+    sM[warp * 16 + g + 8] = m1;
+    sL[warp * 16 + g] = l0;
+    sL[warp * 16 + g + 8] = l1;
+  }
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) {
+    float* row0 = sO + (warp * 16 + g) * D + n * 8 + 2 * tq;
+    float* row1 = row0 + 8 * D;
+    *reinterpret_cast<float2*>(row0) = make_float2(acc[n][0], acc[n][1]);
+    *reinterpret_cast<float2*>(row1) = make_float2(acc[n][2], acc[n][3]);
+  }
+  __syncthreads();
+  for (int e = tid; e < rep * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sM[w * 16 + r]);
+    const float ref = M == -INFINITY ? 0.f : M;
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = exp2f(sM[w * 16 + r] - ref);
+      L += f * sL[w * 16 + r];
+      O += f * sO[(w * 16 + r) * D + d];
+    }
+    const int hq = hk * rep + r;
+    if (p.nsplit == 1) {
+      ((T*)p.o)[((int64_t)b * p.Hq + hq) * D + d] = from_f32<T>(L > 0.f ? O / L : 0.f);
+    } else {
+      float* w = p.ws + (((int64_t)b * p.Hq + hq) * p.nsplit + split) * (D + 2);
+      if (d == 0) {
+        w[0] = M * 0.6931471805599453f;  // natural-log units, as the generic kernel
+        w[1] = L;
+      }
+      w[2 + d] = O;
+    }
+  }
+}
+
 static size_t smem_bytes(int D) { return (size_t)(kMaxRep * D + 2 * TK * (D + 1) + kWarps * TK) * 4; }
 
 // Splits so that B * Hkv * nsplit covers the SMs about twice, each split
@@ -259,8 +516,42 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
   p.ws = (float*)workspace;
   B2_CHECK_ARG(p.nsplit == 1 || workspace, B2_ERR_INVALID, "decode_attn: workspace required (%d splits)", p.nsplit);
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t smem = dec::smem_bytes(p.D);
   const dim3 grid(p.nsplit, p.Hkv, p.B);
+  // Tensor-core path: same 16-bit type for q and KV, D in {64, 128, 256},
+  // 16-byte aligned rows (cp.async 16).
+  const bool a16 = ((uintptr_t)k % 16 == 0) && ((uintptr_t)v % 16 == 0) && ((uintptr_t)q % 16 == 0);
+  bool s16 = true;
+  for (int i = 0; i < 3; ++i) s16 = s16 && p.ks[i] % 8 == 0 && p.vs[i] % 8 == 0;
+  if (q_dtype == kv_dtype && q_dtype != B2_F32 && (D == 64 || D == 128 || D == 256) && a16 && s16) {
+#define B2_TC(T, DD)                                                                                       \
+  do {                                                                                                     \
+    const int sm = dec::TcCfg<DD>::kSmem;                                                                  \
+    if (page_size) {                                                                                       \
+      cudaFuncSetAttribute(dec::decode_tc_kernel<T, DD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm); \
+      dec::decode_tc_kernel<T, DD, true><<<grid, dec::kThreads, sm, st>>>(p);                              \
+    } else {                                                                                               \
+      cudaFuncSetAttribute(dec::decode_tc_kernel<T, DD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm); \
+      dec::decode_tc_kernel<T, DD, false><<<grid, dec::kThreads, sm, st>>>(p);                             \
+    }                                                                                                      \
+  } while (0)
+#define B2_TC_D(T)                 \
+  do {                             \
+    if (D == 64) B2_TC(T, 64);     \
+    else if (D == 128) B2_TC(T, 128); \
+    else B2_TC(T, 256);            \
+  } while (0)
+    if (q_dtype == B2_F16) {
+      B2_TC_D(__half);
+      if (p.nsplit > 1) dec::decode_combine_kernel<__half><<<p.B * p.Hq, 128, 0, st>>>(p);
+    } else {
+      B2_TC_D(__nv_bfloat16);
+      if (p.nsplit > 1) dec::decode_combine_kernel<__nv_bfloat16><<<p.B * p.Hq, 128, 0, st>>>(p);
+    }
+#undef B2_TC_D
+#undef B2_TC
+    return launch_status("decode_attn");
+  }
+  const size_t smem = dec::smem_bytes(p.D);
 #define B2_DEC(TQ, TKV)                                                                                     \
   do {                                                                                                      \
     if (page_size) {                                                                                        \
