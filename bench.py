@@ -476,10 +476,10 @@ class KDA:
         self.roof_scale = 1e9
         self.peak_key, self.peak_unit = "hbm_gbs", "GB/s"
         self.launches_per_step = 1
-        self.kernels_per_launch = 2  # intra-chunk kernel + state pass
+        self.kernels_per_launch = 3  # intra-chunk kernel, state pass, output kernel
         self.cfg = {"workload": f"kda B={B} T={T} H={H} Dk=Dv={D} chunk=64",
                     "algorithmic_bytes": self.bytes, "l2": "inputs 810 MB > 126 MB L2",
-                    "kernels_per_step": 2}
+                    "kernels_per_step": 3}
 
     def step(self, stream):
         self.bk.kda_chunk_fwd(self.q, self.k, self.v, self.g, self.beta, out=self.o, workspace=self.ws)
@@ -561,10 +561,11 @@ class Decode:
         self.roof_scale = 1e9
         self.peak_key, self.peak_unit = "hbm_gbs", "GB/s"
         self.launches_per_step = 1
-        self.kernels_per_launch = 2     # split kernel + combine kernel
+        # split kernel, plus the combine kernel when B * Hkv < SMs (KV split)
+        self.kernels_per_launch = 1 if B * Hkv >= torch.cuda.get_device_properties(0).multi_processor_count else 2
         self.cfg = {"workload": f"decode B={B} Hq={Hq} Hkv={Hkv} S={S} D={D} kv=bf16",
                     "algorithmic_bytes": self.bytes, "l2": "KV cache 1.07 GB > 126 MB L2 (no flush needed)",
-                    "kernels_per_step": 2,
+                    "kernels_per_step": self.kernels_per_launch,
                     "e2e_note": "the KV cache is device-resident state; e2e copies q in and o out per step"}
 
     def step(self, stream):

@@ -90,8 +90,8 @@ B2_API int b2_int8_matmul(const void* input, const void* weight, void* output,
  * Plain bf16 GEMM on tcgen05: out[M,N] = x[M,K] @ w[N,K]^T (w K-major, the
  * nn.Linear layout), fp32 accumulate, bf16 out.  The dequantised-weight
  * path of the reference's matmuls (x @ dequant(W), _msl_templates.py:2663,
- * :2716) when W is already bf16.  Needs M % 128 == 0, N % 256 == 0,
- * K % 64 == 0 and 16-byte aligned pointers.
+ * :2716) when W is already bf16.  Any M; needs N % 8 == 0, K % 64 == 0
+ * and 16-byte aligned pointers.
  */
 B2_API int b2_gemm_bf16(const void* x, const void* w, void* out,
                         int64_t M, int64_t N, int64_t K, void* stream);

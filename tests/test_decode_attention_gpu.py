@@ -70,7 +70,7 @@ def _close(out, ref, tol=1e-2):
 @pytest.mark.parametrize("qdt,kvdt", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float16),
                                       (torch.float32, torch.float16), (torch.float32, torch.float32)])
 @pytest.mark.parametrize("B,Hq,Hkv,S,D", [(1, 8, 8, 100, 64), (3, 32, 8, 4096, 128), (2, 16, 1, 777, 128),
-                                          (64, 8, 2, 300, 256)])
+                                          (64, 8, 2, 300, 256), (40, 16, 4, 1000, 128)])
 def test_decode_contiguous(cuda, qdt, kvdt, B, Hq, Hkv, S, D):
     import b200kern as bk
     g = torch.Generator().manual_seed(B * 1000 + S)

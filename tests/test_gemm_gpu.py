@@ -98,3 +98,66 @@ def test_gemm_no_bounded_wait_ran_out(cuda):
     code = ctypes.c_uint(0)
     st = _lib.load().b2_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(code))
     assert st == 0 and code.value == 0, hex(code.value)
+
+
+# ---------------------------------------------------------------------------
+# fp16 activations, asymmetric zeros, ragged M / N, the reference's fp32
+# dtype and [N, K/2] layout on the GEMM path (M > 16).  The dequantised
+# operand is rounded to the activation dtype (with zeros: fma(q, s, -z*s)
+# or (w - z) rounded once), so these use the RMS-scaled bound.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("zeros", [False, True])
+@pytest.mark.parametrize("M,N,K,G", [(256, 512, 512, 128), (200, 264, 256, 64), (17, 1000, 1024, 128)])
+def test_w4_gemm_variants(cuda, dtype, zeros, M, N, K, G):
+    import b200kern as bk
+    from b200kern.synthetic import w4_inputs
+    d = w4_inputs(M, N, K, group_size=G, dtype=dtype, seed=M + N, zeros=zeros)
+    z = None if d["zeros"] is None else d["zeros"].to(cuda)
+    out = bk.int4_matmul(d["x"].to(cuda), d["qweight"].to(cuda), d["scales"].to(cuda), z, group_size=G)
+    assert out.dtype == dtype and tuple(out.shape) == (M, N)
+    wd = bk.int4_dequant(d["qweight"].to(cuda), d["scales"].to(cuda), z, G)
+    ref = d["x"].to(cuda).float() @ wd
+    _close_w4(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("zeros", [False, True])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 512), (130, 72, 192)])
+def test_w8_gemm_variants(cuda, dtype, zeros, M, N, K):
+    import b200kern as bk
+    from b200kern.synthetic import w8_inputs
+    d = w8_inputs(M, N, K, dtype=dtype, seed=M + N, zeros=zeros)
+    z = None if d["zeros"] is None else d["zeros"].to(cuda)
+    out = bk.int8_matmul(d["x"].to(cuda), d["w"].to(cuda), d["scales"].to(cuda), z)
+    assert out.dtype == dtype
+    zf = 0.0 if z is None else z.float()[:, None]
+    ref = d["x"].to(cuda).float() @ ((d["w"].to(cuda).float() - zf) * d["scales"].to(cuda).float()[:, None]).t()
+    _close_w4(out, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(200, 264, 128), (1, 8, 64), (333, 1000, 640)])
+def test_gemm_bf16_ragged(cuda, M, N, K):
+    import b200kern as bk
+    g = torch.Generator().manual_seed(M * N)
+    x = torch.randn(M, K, generator=g).bfloat16().to(cuda)
+    w = (torch.randn(N, K, generator=g) / K ** 0.5).bfloat16().to(cuda)
+    _close(bk.gemm_bf16(x, w), x.float() @ w.float().t())
+
+
+def test_w4_gemm_reference_dtype_and_layout(cuda):
+    """The reference's own buffers: fp32 input, uint8 [N, K/2] weight with
+    low nibble = even k, fp32 scales / zeros [N, K/G], M = 64 rows (GEMM
+    path), against the float64 oracle of _msl_templates.py:2716-2743."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(4242)
+    M, N, K, G = 64, 768, 512, 128
+    x = torch.randn(M, K, generator=g)
+    q = torch.randint(0, 16, (N, K), generator=g, dtype=torch.int32)
+    s = torch.rand(N, K // G, generator=g) * 0.05 + 0.01
+    z = torch.randint(0, 16, (N, K // G), generator=g).float()
+    w = bk.pack_int4_ref(q)
+    out = bk.int4_matmul(x.to(cuda), w.to(cuda), s.to(cuda), z.to(cuda), group_size=G, layout="ref")
+    assert out.dtype == torch.float32
+    ref = oq.int4_matmul(x.double().numpy(), q.t().numpy(), s.t().double().numpy(), z.t().double().numpy(), G)
+    _close_w4(out.cpu(), torch.from_numpy(ref))

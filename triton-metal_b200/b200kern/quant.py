@@ -182,7 +182,7 @@ def int8_matmul(input, weight, scales, zeros=None, out=None):
 def gemm_bf16(x, w, out=None):
     """out[M, N] = x[M, K] @ w[N, K]^T on tcgen05 (bf16 in/out, fp32 accumulate).
 
-    Needs M % 128 == 0, N % 256 == 0, K % 64 == 0."""
+    Needs N % 8 == 0 and K % 64 == 0 (any M)."""
     _check_cuda(x, w)
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or x.dim() != 2 or w.dim() != 2:
         raise B2DtypeError("gemm_bf16 takes bf16 x [M, K] and w [N, K]")

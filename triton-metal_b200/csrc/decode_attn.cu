@@ -455,11 +455,14 @@ decode_tc_kernel(const Params p) {
 
 static size_t smem_bytes(int D) { return (size_t)(kMaxRep * D + 2 * TK * (D + 1) + kWarps * TK) * 4; }
 
-// Splits so that B * Hkv * nsplit covers the SMs about twice, each split
-// at least 4 tiles long.
+// Splits: with at least one (batch, kv head) pair per SM a single split
+// already keeps >= 2 x 32 KB of K/V in flight per SM, enough to saturate HBM,
+// and avoids the partials round trip.  With fewer pairs the sequence is cut
+// so that about 2 CTAs per SM run, each split at least 4 tiles long.
 static int choose_splits(int B, int Hkv, int max_len) {
-  const int target = 2 * num_sms();
-  int ns = (target + B * Hkv - 1) / (B * Hkv);
+  const int pairs = B * Hkv;
+  if (pairs >= num_sms()) return 1;
+  int ns = (2 * num_sms() + pairs - 1) / pairs;
   const int max_ns = (max_len + 4 * TK - 1) / (4 * TK);
   if (ns > max_ns) ns = max_ns;
   return ns < 1 ? 1 : ns;

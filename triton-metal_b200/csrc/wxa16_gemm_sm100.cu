@@ -1,10 +1,11 @@
 // Prefill GEMM on the 5th-generation tensor cores (tcgen05, sm_100a):
-//   out[M, N] (bf16) = x[M, K] (bf16) @ W[K, N]
+//   out[M, N] = x[M, K] @ W[K, N]      (x, out: bf16 or fp16; fp32 accumulate)
 // with W given as
 //   MODE 0: bf16 [N, K] (K-major, nn.Linear layout)       -> b2_gemm_bf16
-//   MODE 1: int8 [N, K] + per-channel scale [N]            -> b2_int8_matmul
+//   MODE 1: int8 [N, K] + per-channel scale [N] (+ zero [N]) -> b2_int8_matmul
 //           (reference int8_matmul, _msl_templates.py:2663-2677)
-//   MODE 2: int4 GPTQ int32 [K/8, N] + group scales [K/G, N] (zero point 8)
+//   MODE 2: int4 GPTQ int32 [K/8, N] + group scales [K/G, N], zero point 8 or
+//           per-group zeros [K/G, N] (asymmetric)
 //                                                          -> b2_int4_matmul
 //           (reference int4_matmul, _msl_templates.py:2716-2743)
 //
@@ -21,7 +22,9 @@
 //   warps 6-21  (MODE 1/2) dequantisers: packed tile -> exact integers ->
 //               scaled bf16 written straight into the 128B-swizzled K-major
 //               B layout the MMA reads, then fence.proxy.async + arrive.
-// All waits are bounded (error word + early exit).
+// M and N may be ragged (multiples of 1 and 8): the TMA boxes past the edge
+// read zeros and the epilogue masks its stores.  All waits are bounded
+// (error word + early exit).
 #include "tc_common.cuh"
 #include <string.h>
 
@@ -34,6 +37,8 @@ constexpr int kBBytes = BN * BK * 2;   // 32 KB
 constexpr int kAccCols = BN;           // fp32 accumulator columns per buffer
 constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kDequantWarps = 16;
+// W8 with zeros: per-tile row sums of x, [2 accumulators][4 k-quarters][BM]
+constexpr int kXsBytes = 2 * 4 * BM * 4;
 
 template <int MODE>
 struct Cfg {
@@ -42,13 +47,15 @@ struct Cfg {
   static constexpr int kStages = (220 * 1024) / kStageBytes;
   static constexpr int kWarps = MODE == 0 ? 6 : 6 + kDequantWarps;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                                  (MODE == 1 ? kXsBytes : 0);
 };
 
 struct Params {
   int M, N, K, G;
-  const __nv_bfloat16* scales;  // MODE 1: [N]; MODE 2: [K/G, N]
-  __nv_bfloat16* out;
+  const uint16_t* scales;  // MODE 1: [N]; MODE 2: [K/G, N]   (activation dtype)
+  const uint16_t* zeros;   // same shape as scales, or null (symmetric)
+  uint16_t* out;
   int tiles_m, tiles_n;
   unsigned* err;
 };
@@ -78,31 +85,84 @@ __device__ __forceinline__ uint32_t unzip_nibbles(uint32_t w) {
   return prmt(w, w, 0x3120);                 // bytes (q0q2)(q1q3)(q4q6)(q5q7) -> (q0q2)(q4q6)(q1q3)(q5q7)
 }
 
-// 8 k-values of one column -> 4 packed bf16 pairs of (q - 8) * s.
-__device__ __forceinline__ uint4 dequant8_int4(uint32_t w, uint32_t s2) {
+// 8 k-values of one column -> 4 packed pairs (activation dtype) of
+// (q - 8) * s (symmetric) or (q - z) * s (asymmetric).  q is exact: OR-ing it
+// into the mantissa of 128.0 (bf16, ulp 1) or 1024.0 (fp16, ulp 1) gives
+// bias + q.  With zeros, z = zi + zf (zi = rint(z)): subtracting the exact
+// pair bz2 = bias + zi leaves q - zi exactly, and one fma adds the small
+// residual zr2 = -zf * s, so the result is rounded once (plus the rounding
+// of the |zf| <= 1/2 residual).
+template <int DT, bool ZP>
+__device__ __forceinline__ uint4 dequant8_int4(uint32_t w, uint32_t s2, uint32_t bz2, uint32_t zr2) {
   const uint32_t u = unzip_nibbles(w);
+  constexpr uint32_t kBias = DT == B2_BF16 ? 0x43004300u : 0x64006400u;
+  constexpr uint32_t kBias8 = DT == B2_BF16 ? 0x43084308u : 0x64086408u;
   uint32_t r[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    uint32_t v = sub2<B2_BF16>(and_or(u >> (4 * j), 0x000F000Fu, 0x43004300u), 0x43084308u);  // q - 8, exact
-    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
+    const uint32_t biased = and_or(u >> (4 * j), 0x000F000Fu, kBias);
+    if constexpr (!ZP) {
+      const uint32_t v = sub2<DT>(biased, kBias8);  // q - 8, exact
+      if constexpr (DT == B2_BF16) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
+      else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
+    } else {
+      const uint32_t v = sub2<DT>(biased, bz2);     // q - zi, exact
+      if constexpr (DT == B2_BF16) asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
+      else asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
+    }
   }
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
-// 4 int8 -> 2 packed bf16 pairs (exact).
-__device__ __forceinline__ void int8x4_to_bf16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+template <int DT>
+__device__ __forceinline__ uint32_t pack_pair(float a, float b) {
+  if constexpr (DT == B2_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+template <int DT>
+__device__ __forceinline__ float ld_act(const uint16_t* p) {
+  return to_f32<typename dtype_of<DT>::T>(*reinterpret_cast<const typename dtype_of<DT>::T*>(p));
+}
+template <int DT>
+__device__ __forceinline__ uint32_t splat(float v) {
+  return pack_pair<DT>(v, v);
+}
+
+// 4 int8 -> 2 packed pairs (activation dtype), exact.
+template <int DT>
+__device__ __forceinline__ void int8x4_to_act(uint32_t w, uint32_t& lo, uint32_t& hi) {
   const uint32_t u = w ^ 0x80808080u;
   const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7650)) - 8388736.f;
   const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7651)) - 8388736.f;
   const float f2 = __uint_as_float(prmt(u, 0x4B000000u, 0x7652)) - 8388736.f;
   const float f3 = __uint_as_float(prmt(u, 0x4B000000u, 0x7653)) - 8388736.f;
-  __nv_bfloat162 a = __floats2bfloat162_rn(f0, f1), b = __floats2bfloat162_rn(f2, f3);
-  lo = *reinterpret_cast<uint32_t*>(&a);
-  hi = *reinterpret_cast<uint32_t*>(&b);
+  lo = pack_pair<DT>(f0, f1);
+  hi = pack_pair<DT>(f2, f3);
 }
 
-template <int MODE>
+// fp32 sum of 8 packed activation values.
+template <int DT>
+__device__ __forceinline__ float sum8(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (DT == B2_BF16) {
+      s += __uint_as_float(w[i] << 16) + __uint_as_float(w[i] & 0xFFFF0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      s += f.x + f.y;
+    }
+  }
+  return s;
+}
+
+template <int MODE, int DT, bool ZP>
 __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
 wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const Params p) {
@@ -118,8 +178,10 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   uint64_t* tfull = empty + C::kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xsready = drain + 1;  // W8 with zeros: row sums of the tile written
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xsready + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* xsbuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // MODE 1 && ZP
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kblocks = p.K / BK;
@@ -134,6 +196,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
+      mbar_init(&xsready[a], kDequantWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -177,7 +240,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   } else if (warp == 1) {
     // ------------------------------ MMA issuer --------------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_f16(BM, BN, true);
+      constexpr uint32_t idesc = tc::idesc_f16(BM, BN, DT == B2_BF16);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -227,28 +290,50 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       if (!wait_or_abort(&tfull[acc], acc_phase, p, 0xB2100005u, abort_flag)) break;
       tc::fence_after_sync();
       const int row = m0 + q * 32 + lane;
-      __nv_bfloat16* orow = p.out + (size_t)row * p.N + n0;
+      float xs = 0.f;  // W8 with zeros: sum_k x[row, k]
+      if constexpr (MODE == 1 && ZP) {
+        if (!wait_or_abort(&xsready[acc], acc_phase, p, 0xB2100008u, abort_flag)) break;
+        const float* xb = xsbuf + acc * 4 * BM + q * 32 + lane;
+        xs = (xb[0] + xb[BM]) + (xb[2 * BM] + xb[3 * BM]);
+      }
+      uint16_t* orow = p.out + (size_t)row * p.N + n0;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
+        // warp-collective: every lane loads, rows / columns past the edge
+        // only skip their stores
         tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccCols + c * 32, r);
         tc::tmem_ld_wait();
+        const int nc = n0 + c * 32;
+        if (row >= p.M || nc >= p.N) continue;
         uint32_t packed[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
           if constexpr (MODE == 1) {
-            const int n = n0 + c * 32 + 2 * j;
-            v0 *= __bfloat162float(p.scales[n]);
-            v1 *= __bfloat162float(p.scales[n + 1]);
+            const int n = nc + 2 * j;
+            if constexpr (ZP) {
+              v0 -= (n < p.N ? ld_act<DT>(p.zeros + n) : 0.f) * xs;
+              v1 -= (n + 1 < p.N ? ld_act<DT>(p.zeros + n + 1) : 0.f) * xs;
+            }
+            v0 *= n < p.N ? ld_act<DT>(p.scales + n) : 0.f;
+            v1 *= n + 1 < p.N ? ld_act<DT>(p.scales + n + 1) : 0.f;
           }
-          __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
-          packed[j] = *reinterpret_cast<uint32_t*>(&h);
+          packed[j] = pack_pair<DT>(v0, v1);
         }
-        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+        if (nc + 32 <= p.N) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+        } else {
+          // ragged N (multiple of 8): whole 16-byte pieces only
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (nc + 8 * j < p.N)
+              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+        }
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -262,17 +347,26 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+    int tile_it = 0;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tile_it) {
       const int n0 = (tile / p.tiles_m) * BN;
-      uint32_t s2 = 0;
+      const bool col_ok = n0 + n < p.N;
+      uint32_t s2 = 0, bz2 = 0, zr2 = 0;
+      float xsum = 0.f;  // W8 with zeros: this thread's quarter of an x row
       int cur_group = -1;
       for (int kb = 0; kb < kblocks; ++kb) {
         if (MODE == 2) {
           const int grp = kb * BK / p.G;
           if (grp != cur_group) {
-            const __nv_bfloat16 s = p.scales[(size_t)grp * p.N + n0 + n];
-            __nv_bfloat162 ss = __halves2bfloat162(s, s);
-            s2 = *reinterpret_cast<uint32_t*>(&ss);
+            const size_t gi = (size_t)grp * p.N + n0 + n;
+            const float sc = col_ok ? ld_act<DT>(p.scales + gi) : 0.f;
+            s2 = splat<DT>(sc);
+            if (ZP) {
+              const float z = col_ok ? ld_act<DT>(p.zeros + gi) : 0.f;
+              const float zi = fminf(fmaxf(rintf(z), -64.f), 64.f);  // bias + zi stays exact
+              bz2 = splat<DT>((DT == B2_BF16 ? 128.f : 1024.f) + zi);
+              zr2 = splat<DT>(-(z - zi) * sc);
+            }
             cur_group = grp;
           }
         }
@@ -287,7 +381,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 #pragma unroll
           for (int rr = 0; rr < BK / 16; ++rr) {
             const int r = h * (BK / 16) + rr;
-            const uint4 v = dequant8_int4(pk[r * BN + n], s2);
+            const uint4 v = dequant8_int4<DT, ZP>(pk[r * BN + n], s2, bz2, zr2);
             *reinterpret_cast<uint4*>(brow + ((r ^ sw) << 4)) = v;
           }
         } else {
@@ -297,12 +391,35 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             const int j = h * (BK / 32) + jj;
             const uint4 v = pk[j];
             uint32_t o[8];
-            int8x4_to_bf16(v.x, o[0], o[1]);
-            int8x4_to_bf16(v.y, o[2], o[3]);
-            int8x4_to_bf16(v.z, o[4], o[5]);
-            int8x4_to_bf16(v.w, o[6], o[7]);
+            int8x4_to_act<DT>(v.x, o[0], o[1]);
+            int8x4_to_act<DT>(v.y, o[2], o[3]);
+            int8x4_to_act<DT>(v.z, o[4], o[5]);
+            int8x4_to_act<DT>(v.w, o[6], o[7]);
             *reinterpret_cast<uint4*>(brow + (((2 * j) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(brow + (((2 * j + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+        if constexpr (MODE == 1 && ZP) {
+          // row d % 128 of the x tile, k-quarter d / 128 (two swizzled chunks)
+          const int ar = d & (BM - 1), aq = d >> 7;
+          const uint8_t* arow = sA + stage * kABytes + ar * 128;
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const uint4 v = *reinterpret_cast<const uint4*>(arow + (((2 * aq + cc) ^ (ar & 7)) << 4));
+            xsum += sum8<DT>(v);
+          }
+          if (kb == kblocks - 1) {
+            // hand the row sums to the epilogue; the buffer of this
+            // accumulator is free once its previous epilogue released it
+            const int acc = tile_it & 1;
+            if (!wait_or_abort(&tempty[acc], ((tile_it >> 1) & 1) ^ 1, p, 0xB2100009u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            xsbuf[acc * 4 * BM + aq * BM + ar] = xsum;
+            xsum = 0.f;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xsready[acc]);
           }
         }
         tc::fence_proxy_async_smem();
@@ -327,24 +444,24 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 
 }  // namespace gemm
 
-template <int MODE>
-static int launch_gemm(const void* x, const void* w, const void* scales, void* out, int64_t M, int64_t N,
-                       int64_t K, int64_t G, cudaStream_t st) {
+template <int MODE, int DT, bool ZP>
+static int launch_gemm(const void* x, const void* w, const void* scales, const void* zeros, void* out, int64_t M,
+                       int64_t N, int64_t K, int64_t G, cudaStream_t st) {
   using namespace gemm;
   using C = Cfg<MODE>;
-  if (M % BM || N % BN || K % BK || (MODE == 2 && (G % BK || K % G))) return B2_ERR_UNSUPPORTED;
+  if (M <= 0 || N % 8 || K % BK || (MODE == 2 && (G % BK || K % G))) return B2_ERR_UNSUPPORTED;
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16)) return B2_ERR_UNSUPPORTED;
   unsigned* err = device_error_word();
   if (!err) {
     set_error("gemm: cannot resolve the device error word");
     return B2_ERR_LAUNCH;
   }
+  const CUtensorMapDataType adt = DT == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
-  if (!make_tmap_2d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
-    return B2_ERR_INVALID;
+  if (!make_tmap_2d(&ta, x, adt, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ERR_INVALID;
   bool okb;
   if (MODE == 0)
-    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    okb = make_tmap_2d(&tb, w, adt, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   else if (MODE == 1)
     okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, BK, BN);
   else
@@ -355,43 +472,54 @@ static int launch_gemm(const void* x, const void* w, const void* scales, void* o
   p.N = (int)N;
   p.K = (int)K;
   p.G = (int)G;
-  p.scales = (const __nv_bfloat16*)scales;
-  p.out = (__nv_bfloat16*)out;
-  p.tiles_m = (int)(M / BM);
-  p.tiles_n = (int)(N / BN);
+  p.scales = (const uint16_t*)scales;
+  p.zeros = (const uint16_t*)zeros;
+  p.out = (uint16_t*)out;
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)((N + BN - 1) / BN);
   p.err = err;
   const int ntiles = p.tiles_m * p.tiles_n;
   int grid = num_sms();
   if (grid > ntiles) grid = ntiles;
-  auto kern = wxa16_gemm_kernel<MODE>;
+  auto kern = wxa16_gemm_kernel<MODE, DT, ZP>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
   kern<<<grid, C::kThreads, C::kSmem, st>>>(ta, tb, p);
   return launch_status("wxa16_gemm");
+}
+
+template <int MODE>
+static int launch_gemm_any(const void* x, const void* w, const void* s, const void* z, void* out, int64_t M,
+                           int64_t N, int64_t K, int64_t G, int dtype, cudaStream_t st) {
+  if (dtype == B2_BF16)
+    return z ? launch_gemm<MODE, B2_BF16, true>(x, w, s, z, out, M, N, K, G, st)
+             : launch_gemm<MODE, B2_BF16, false>(x, w, s, z, out, M, N, K, G, st);
+  if (dtype == B2_F16)
+    return z ? launch_gemm<MODE, B2_F16, true>(x, w, s, z, out, M, N, K, G, st)
+             : launch_gemm<MODE, B2_F16, false>(x, w, s, z, out, M, N, K, G, st);
+  return B2_ERR_UNSUPPORTED;
 }
 
 }  // namespace b2
 
 using namespace b2;
 
-// Called by b2_int4_matmul for M > 16: bf16, symmetric zero point only.
+// Called by b2_int4_matmul for M > 16 (fp16 / bf16, symmetric or per-group zeros).
 int b2_detail_w4_gemm(const void* x, const void* w, void* out, const void* s, const void* z, int64_t M, int64_t N,
                       int64_t K, int64_t G, int dtype, cudaStream_t st) {
-  if (dtype != B2_BF16 || z) return B2_ERR_UNSUPPORTED;
-  return launch_gemm<2>(x, w, s, out, M, N, K, G, st);
+  return launch_gemm_any<2>(x, w, s, z, out, M, N, K, G, dtype, st);
 }
 
-// Called by b2_int8_matmul for M > 16: bf16, symmetric only.
+// Called by b2_int8_matmul for M > 16 (fp16 / bf16, symmetric or per-channel zeros).
 int b2_detail_w8_gemm(const void* x, const void* w, void* out, const void* s, const void* z, int64_t M, int64_t N,
                       int64_t K, int dtype, cudaStream_t st) {
-  if (dtype != B2_BF16 || z) return B2_ERR_UNSUPPORTED;
-  return launch_gemm<1>(x, w, s, out, M, N, K, 0, st);
+  return launch_gemm_any<1>(x, w, s, z, out, M, N, K, 0, dtype, st);
 }
 
 extern "C" int b2_gemm_bf16(const void* x, const void* w, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
   B2_CHECK_ARG(x && w && out, B2_ERR_INVALID, "gemm_bf16: null pointer");
   B2_CHECK_ARG(M > 0 && N > 0 && K > 0, B2_ERR_INVALID, "gemm_bf16: bad shape");
-  int r = launch_gemm<0>(x, w, nullptr, out, M, N, K, 0, (cudaStream_t)stream);
+  int r = launch_gemm<0, B2_BF16, false>(x, w, nullptr, nullptr, out, M, N, K, 0, (cudaStream_t)stream);
   if (r == B2_ERR_UNSUPPORTED)
-    set_error("gemm_bf16: needs M %% 128 == 0, N %% 256 == 0, K %% 64 == 0 and 16-byte aligned pointers");
+    set_error("gemm_bf16: needs N %% 8 == 0, K %% 64 == 0 and 16-byte aligned pointers");
   return r;
 }
