@@ -168,7 +168,7 @@ template <int DT, int NT, int RQ, int NCH, bool ZEROS>
 __global__ void __launch_bounds__(gemv_threads<NCH>(), gemv_min_blocks<NT>())
 w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __restrict__ x,
                       uint16_t* __restrict__ out, int M, int N, int K, int tiles_base, int tiles_rem,
-                      int stages, unsigned* err) {
+                      int stages, int gps, unsigned* err) {
   using T = typename dtype_of<DT>::T;
   using T2 = typename dtype_of<DT>::T2;
   constexpr int R = 4 * RQ;                // weight rows (of 8 k) per stage
@@ -213,10 +213,14 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
     mbar_arrive_expect_tx(sbar, ngroups * sw * 2 * (ZEROS ? 2 : 1));
     tma_load_2d(smem, &maps.s[wide], c0, 0, sbar);
     if constexpr (ZEROS) tma_load_2d(smem + sblk, &maps.z[wide], c0, 0, sbar);
-    for (int s = 0; s < ngroups; ++s) {
+    // One TMA box covers gps consecutive groups (slots slot .. slot + gps - 1,
+    // contiguous in shared memory) and completes on the first slot's barrier.
+    for (int s = 0; s < ngroups; s += gps) {
       const int slot = s % stages;
-      if (s >= stages && !mbar_wait(&empty[slot], ((s / stages) - 1) & 1, err, 0xB2000001u)) return;
-      mbar_arrive_expect_tx(&full[slot], R * sw * 4);
+      if (s >= stages)
+        for (int j = 0; j < gps; ++j)
+          if (!mbar_wait(&empty[slot + j], ((s / stages) - 1) & 1, err, 0xB2000001u)) return;
+      mbar_arrive_expect_tx(&full[slot], gps * R * sw * 4);
       tma_load_2d_hint(ring + (size_t)slot * slot_bytes, &maps.w[wide], c0, s * R, &full[slot], pol);
     }
     return;
@@ -271,11 +275,14 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
         mma_16816<DT>(ds[n][0], ones, b0);
         mma_16816<DT>(ds[n][1], ones, b1);
       }
-    if (!mbar_wait(&full[slot], (s / stages) & 1, err, 0xB2000002u)) {
+    const int slot0 = slot - slot % gps;  // first slot of this group's box
+    if (!mbar_wait(&full[slot0], (s / stages) & 1, err, 0xB2000002u)) {
       alive = false;
       break;
     }
-    const uint32_t* wsm = reinterpret_cast<const uint32_t*>(ring + (size_t)slot * slot_bytes);
+    // the box holds gps groups of R rows x sw columns back to back
+    const uint32_t* wsm =
+        reinterpret_cast<const uint32_t*>(ring + (size_t)slot0 * slot_bytes) + (size_t)(slot - slot0) * R * sw;
     const T* ssm = reinterpret_cast<const T*>(smem) + (size_t)s * sw;
     const T* zsm = reinterpret_cast<const T*>(smem + sblk) + (size_t)s * sw;
 #pragma unroll
@@ -384,7 +391,7 @@ constexpr int kSmemBudgetNT2 = 227 * 1024;
 constexpr int kMaxStages = 64;
 
 struct GemvPlan {
-  int grid, base, rem, stages;
+  int grid, base, rem, stages, gps;
   size_t smem;
 };
 
@@ -409,8 +416,24 @@ static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p) {
   const size_t fixed = sblk * (zeros ? 2 : 1);
   int stages = (int)((budget - fixed - 256) / (slot + 16));
   if (stages > kMaxStages) stages = kMaxStages;
-  if (stages > ngroups) stages = ngroups;
+  // Consumer warp w takes groups w, w + 8, ... and waits on ring slot
+  // s % stages with parity (s / stages) & 1.  A parity wait one phase ahead
+  // of the slot's current phase returns at once, so a slot must only ever be
+  // reused by the warp that used it before (which has already waited for the
+  // previous fill): stages is a multiple of the 8 stage lanes, unless every
+  // group has its own slot.
+  if (stages >= ngroups) stages = ngroups;
+  else stages -= stages % kStageLanes;
   if (stages < 1) return false;
+  // groups per TMA box: the largest of 4, 2, 1 that divides the ring and the
+  // group count and keeps the box within 256 rows (fewer, larger boxes
+  // stream faster: 5 KB boxes ran ~1.5x slower than 10 KB ones)
+  p->gps = 1;
+  for (int gps = 4; gps > 1; gps >>= 1)
+    if (stages % gps == 0 && ngroups % gps == 0 && rows * gps <= 256) {
+      p->gps = gps;
+      break;
+    }
   size_t total = fixed + (size_t)stages * (slot + 16) + 16;
   const size_t red = (size_t)kStageLanes * nt * 8 * kMaxColTiles * 8 * 4;
   if (total < red) total = red;
@@ -440,7 +463,7 @@ static int launch_stream(const void* x, const void* w, void* out, const void* s,
   for (int i = 0; i < 2; ++i) {
     const int wdt = widths[i];
     if (wdt == 0 || (i == 0 && p.rem == 0)) continue;
-    if (!make_tmap_2d(&maps.w[i], w, CU_TENSOR_MAP_DATA_TYPE_UINT32, N, K / 8, (uint64_t)N * 4, wdt, rows) ||
+    if (!make_tmap_2d(&maps.w[i], w, CU_TENSOR_MAP_DATA_TYPE_UINT32, N, K / 8, (uint64_t)N * 4, wdt, rows * p.gps) ||
         !make_tmap_2d(&maps.s[i], s, sdt, N, ngroups, (uint64_t)N * 2, wdt, ngroups) ||
         (ZEROS && !make_tmap_2d(&maps.z[i], z, sdt, N, ngroups, (uint64_t)N * 2, wdt, ngroups)))
       return B2_ERR_INVALID;
@@ -460,7 +483,8 @@ static int launch_stream(const void* x, const void* w, void* out, const void* s,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, kern, maps, (const uint16_t*)x, (uint16_t*)out, M, N, K, p.base, p.rem, p.stages, err);
+  cudaLaunchKernelEx(&cfg, kern, maps, (const uint16_t*)x, (uint16_t*)out, M, N, K, p.base, p.rem, p.stages, p.gps,
+                     err);
   return launch_status("w4_gemv");
 }
 
