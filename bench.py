@@ -35,11 +35,12 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes per launch of the dominant kernel, from the committed ncu
 # summaries in profiles/ (None until captured for that workload).
 NCU_TRAFFIC = {
-    "w4a16_gemv": 23282432,        # profiles/w4a16_gemv_c1_m1.md
+    "w4a16_gemv": 23281408,        # profiles/w4a16_gemv_c1_m1.md
     "w4a16_gemm": 148564992,       # profiles/wxa16_gemm_c2.md
     "w8a16_gemm": 183006208,       # profiles/wxa16_gemm_c2.md
-    "fa_gqa": 638298880,           # profiles/fa_gqa_c3.md
-    "kda": 1372952576,             # profiles/kda_c4.md (state-pass kernel)
+    "fa_gqa": 636796160,           # profiles/fa_gqa_c3.md
+    "kda": 4756892000,             # profiles/kda_c4.md (whole step: intra + state + output kernels)
+    "decode": 1079458448,          # profiles/decode_b32_s8192.md
 }
 
 
