@@ -178,6 +178,31 @@ def execute(pipe, bufs):
         rec.update(seq_len=S, n_pages=npg, page_size=ps, head_dim=D, page_table=table.astype(np.int64),
                    q=q, k=kp, v=vp)
         ob = out.astype(np.float32).reshape(-1)
+    elif name == "sliding_window_attention":
+        q_b, k_b, v_b, o_b, qp_b, sl_b = bufs
+        D = _const(msl, r"const uint D = (\d+)u")
+        W = _const(msl, r"const uint WINDOW = (\d+)u")
+        qp, S = qp_b.u32(), sl_b.u32()
+        q, k, v = q_b.f32()[:D], k_b.f32()[: S * D], v_b.f32()[: S * D]
+        out = oatt.sliding_window_decode(q, k, v, qp, S, W)
+        rec.update(seq_len=S, q_pos=qp, window=W, head_dim=D, q=q, k=k.reshape(S, D), v=v.reshape(S, D))
+        ob = out.astype(np.float32).reshape(-1)
+    elif name == "rope_attention":
+        q_b, k_b, v_b, f_b, o_b, sl_b, qp_b = bufs
+        D = _const(msl, r"const uint D = (\d+)u")
+        S, qp = sl_b.u32(), qp_b.u32()
+        q, k, v = q_b.f32()[:D], k_b.f32()[: S * D], v_b.f32()[: S * D]
+        freqs = f_b.f32()[: D // 2]
+        out = oatt.rope_decode(q, k, v, freqs, S, qp)
+        rec.update(seq_len=S, q_pos=qp, head_dim=D, q=q, k=k.reshape(S, D), v=v.reshape(S, D), freqs=freqs)
+        ob = out.astype(np.float32).reshape(-1)
+    elif name == "repeat_kv":
+        i_b, o_b, h_b, sl_b, hd_b, nr_b = bufs
+        H, S, D, R = h_b.u32(), sl_b.u32(), hd_b.u32(), nr_b.u32()
+        x = i_b.f32()[: H * S * D].reshape(H, S, D)
+        out = oatt.repeat_kv(x, R)
+        rec.update(n_kv_heads=H, seq_len=S, head_dim=D, n_rep=R, x=x)
+        ob = out.astype(np.float32).reshape(-1)
     else:
         raise KeyError(name)
     o_b.mem[: ob.nbytes] = ob.tobytes()
@@ -290,6 +315,10 @@ REFERENCE_TESTS = [
     ("test_paged_attention_gpu", "tests/test_emitter.py:5786"),
     ("test_multi_head_paged_attention", "tests/test_emitter.py:3710"),
     ("test_fp16_kv_attention", "tests/test_emitter.py:3809"),
+    ("test_sliding_window_attention", "tests/test_emitter.py:3933"),
+    ("test_sliding_window_attention_gpu", "tests/test_emitter.py:5866"),
+    ("test_rope_attention", "tests/test_emitter.py:3088"),
+    ("test_repeat_kv", "tests/test_emitter.py:4006"),
 ]
 
 TRITON_FA_SHAPES = {
