@@ -141,6 +141,11 @@ B2_API int b2_flash_attn_fwd(const void* q, const void* k, const void* v, void* 
  *                   k/v_strides = element strides (page, token, head).
  *   seq_lens int32 [B] (<= max_seq_len); kv head of q head h = h / (Hq/Hkv).
  *   kv_dtype may differ from q_dtype (fp16 KV with fp32 queries).
+ *   q_pos int32 [B] or NULL (= seq_len - 1): the query's position.
+ *   window > 0: keys [max(0, q_pos + 1 - window), min(q_pos + 1, seq_len))
+ *     (sliding_window_attention, _msl_templates.py:3335-3431); 0: [0, seq_len).
+ *   rope_freqs fp32 [D/2] or NULL: rotate q at q_pos and key j at j, pairs
+ *     (2d, 2d + 1) by pos * rope_freqs[d] (rope_attention, :1770-1887).
  *   workspace: b2_decode_attn_workspace_size(...) bytes (NULL when it is 0).
  */
 B2_API size_t b2_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t Hkv,
@@ -150,8 +155,18 @@ B2_API int b2_decode_attn(const void* q, const void* k, const void* v, void* o,
                           void* workspace, int64_t B, int64_t Hq, int64_t Hkv,
                           int64_t D, int64_t max_seq_len, int64_t page_size,
                           int64_t max_pages, const int64_t* k_strides,
-                          const int64_t* v_strides, float scale, int q_dtype,
-                          int kv_dtype, void* stream);
+                          const int64_t* v_strides, const int32_t* q_pos,
+                          int64_t window, const float* rope_freqs, float scale,
+                          int q_dtype, int kv_dtype, void* stream);
+
+/*
+ * repeat_kv (make_repeat_kv_kernel, _msl_templates.py:3434-3480):
+ *   out[h, s, d] = in[h / n_rep, s, d]; in [n_kv_heads, seq_len, head_dim],
+ *   out [n_kv_heads * n_rep, seq_len, head_dim], elements of elem_bytes.
+ */
+B2_API int b2_repeat_kv(const void* input, void* output, int64_t n_kv_heads,
+                        int64_t seq_len, int64_t head_dim, int64_t n_rep,
+                        int64_t elem_bytes, void* stream);
 
 /*
  * KDA (chunked gated delta rule) forward.  No reference counterpart: the

@@ -116,3 +116,100 @@ def test_gqa_decode_matches_flash_attention(cuda):
     full = bk.flash_attention(q, k, v, causal=True)[:, :, -1]
     dec = bk.decode_attention(q[:, :, -1].contiguous(), k, v, 512)
     _close(dec.double().cpu().numpy(), full.double().cpu().numpy(), tol=2e-2)
+
+
+# ---------------------------------------------------------------------------
+# sliding window, fused RoPE, repeat_kv
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name", ["test_sliding_window_attention", "test_sliding_window_attention_gpu"])
+def test_sliding_window_golden(cuda, name):
+    import b200kern as bk
+    g, rec = golden("ref_" + name), REF[name]
+    t = lambda a: torch.tensor(a, device=cuda)
+    out = bk.sliding_window_attention(t(g["q"]), t(g["k"]), t(g["v"]), rec["q_pos"], rec["seq_len"], rec["window"])
+    ref = g["expected"] if "expected" in g else g["out"]
+    assert np.abs(out.reshape(-1).cpu().numpy() - ref.reshape(-1)).max() < 1e-3
+
+
+def test_rope_golden(cuda):
+    import b200kern as bk
+    g, rec = golden("ref_test_rope_attention"), REF["test_rope_attention"]
+    t = lambda a: torch.tensor(a, device=cuda)
+    out = bk.rope_attention(t(g["q"]), t(g["k"]), t(g["v"]), t(g["freqs"]), rec["seq_len"], rec["q_pos"])
+    assert np.abs(out.reshape(-1).cpu().numpy() - g["out"].reshape(-1)).max() < 1e-4
+
+
+def test_repeat_kv_golden(cuda):
+    import b200kern as bk
+    g = golden("ref_test_repeat_kv")
+    out = bk.repeat_kv(torch.tensor(g["x"], device=cuda), REF["test_repeat_kv"]["n_rep"])
+    assert np.array_equal(out.reshape(-1).cpu().numpy(), g["out"].reshape(-1))  # a copy: bit-exact
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("paged", [False, True])
+def test_decode_window_rope_large(cuda, dt, paged):
+    """Sliding window + RoPE together, ragged lengths and query positions,
+    GQA, contiguous and paged caches, tensor-core (16-bit) and generic (fp32)."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(11 + paged)
+    B, Hq, Hkv, D, S, W = 3, 16, 4, 128, 2500, 700
+    q = torch.randn(B, Hq, D, generator=g).to(dt)
+    k = torch.randn(B, Hkv, S, D, generator=g).to(dt)
+    v = torch.randn(B, Hkv, S, D, generator=g).to(dt)
+    lens = torch.tensor([2500, 1999, 300], dtype=torch.int32)
+    qpos = torch.tensor([2499, 1200, 299], dtype=torch.int32)
+    freqs = 1.0 / 10000.0 ** (torch.arange(0, D, 2, dtype=torch.float64) / D)
+    if paged:
+        ps = 16
+        npg = S // ps + 1
+        perm = torch.randperm(B * npg, generator=g).to(torch.int32).reshape(B, npg)
+        kp = torch.zeros(B * npg, ps, Hkv, D, dtype=dt)
+        vp = torch.zeros(B * npg, ps, Hkv, D, dtype=dt)
+        for b in range(B):
+            for pg in range(npg):
+                lo, hi = pg * ps, min(S, pg * ps + ps)
+                if lo >= hi:
+                    continue
+                kp[perm[b, pg], : hi - lo] = k[b, :, lo:hi].transpose(0, 1)
+                vp[perm[b, pg], : hi - lo] = v[b, :, lo:hi].transpose(0, 1)
+        out = bk.decode_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), lens.to(cuda), page_table=perm.to(cuda),
+                                  q_pos=qpos, window=W, rope_freqs=freqs.float())
+    else:
+        out = bk.decode_attention(q.to(cuda), k.to(cuda), v.to(cuda), lens.to(cuda), q_pos=qpos, window=W,
+                                  rope_freqs=freqs.float())
+    ref = oatt.decode(q.double().numpy(), k.double().numpy(), v.double().numpy(), lens.numpy(),
+                      q_pos=qpos.numpy(), window=W, rope_freqs=freqs.float().double().numpy())
+    _close(out.double().cpu().numpy(), ref, tol=2e-2 if dt != torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("W", [1, 64, 5000])
+def test_decode_window_edges(cuda, W):
+    """Window of one key, a window inside one tile, a window wider than the cache."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(W)
+    B, Hq, Hkv, D, S = 2, 8, 8, 64, 1000
+    q = torch.randn(B, Hq, D, generator=g).bfloat16()
+    k = torch.randn(B, Hkv, S, D, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, S, D, generator=g).bfloat16()
+    lens = torch.tensor([1000, 517], dtype=torch.int32)
+    out = bk.decode_attention(q.to(cuda), k.to(cuda), v.to(cuda), lens.to(cuda), window=W)
+    ref = oatt.decode(q.double().numpy(), k.double().numpy(), v.double().numpy(), lens.numpy(), window=W)
+    _close(out.double().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dt,shape,rep", [(torch.bfloat16, (8, 4096, 128), 4), (torch.float32, (2, 5, 3), 3),
+                                          (torch.float16, (2, 3, 8, 100, 64), 2)])
+def test_repeat_kv_shapes(cuda, dt, shape, rep):
+    import b200kern as bk
+    x = torch.randn(*shape).to(dt).to(cuda)
+    out = bk.repeat_kv(x, rep)
+    assert torch.equal(out, x.repeat_interleave(rep, dim=-3))
+
+
+def test_decode_no_bounded_wait_ran_out(cuda):
+    import ctypes
+    from b200kern import _lib
+    code = ctypes.c_uint(0)
+    st = _lib.load().b2_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(code))
+    assert st == 0 and code.value == 0, hex(code.value)

@@ -31,7 +31,8 @@ SIGNATURES = {
                                  _pi64, _pi64, _pi64, _pi64, _f32, _i32, _i32, _vp]),
     "b2_decode_attn_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     "b2_decode_attn": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
-                              _pi64, _pi64, _f32, _i32, _i32, _vp]),
+                              _pi64, _pi64, _vp, _i64, _vp, _f32, _i32, _i32, _vp]),
+    "b2_repeat_kv": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "b2_kda_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i64]),
     "b2_kda_fwd_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                   _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),

@@ -84,18 +84,26 @@ def gqa_attention(q, k_cache, v_cache, seq_len, scale, n_q_per_kv):
 # decode attention over a KV cache (one query token per head)
 # --------------------------------------------------------------------------
 def _seq_lens(seq_lens, B, device):
+    """int, sequence or tensor of B per-sequence integers -> int32 [B] on device."""
     if isinstance(seq_lens, int):
         return torch.full((B,), seq_lens, dtype=torch.int32, device=device)
-    return seq_lens.to(device=device, dtype=torch.int32).contiguous()
+    t = torch.as_tensor(seq_lens).to(device=device, dtype=torch.int32).reshape(-1).contiguous()
+    if t.numel() != B:
+        raise B2ShapeError(f"expected {B} per-sequence values, got {t.numel()}")
+    return t
 
 
-def decode_attention(q, k_cache, v_cache, seq_lens, scale=None, page_table=None, out=None):
+def decode_attention(q, k_cache, v_cache, seq_lens, scale=None, page_table=None, out=None, q_pos=None, window=0,
+                     rope_freqs=None):
     """o[B, Hq, D] = softmax(scale q K^T) V over the first seq_lens[b] keys.
 
     Contiguous cache: k/v [B, Hkv, S, D] (any strides, last dim contiguous).
     Paged cache (page_table int32 [B, max_pages] given): k/v
     [n_pages, page_size, Hkv, D].  GQA: kv head = q head // (Hq // Hkv).
-    The cache dtype may differ from q's (e.g. fp16 KV with fp32 queries)."""
+    The cache dtype may differ from q's (e.g. fp16 KV with fp32 queries).
+    q_pos [B] (default seq_len - 1); window > 0 keeps the keys
+    [max(0, q_pos + 1 - window), min(q_pos + 1, seq_len)) (sliding window);
+    rope_freqs [D/2] rotates q at q_pos and each key at its position (RoPE)."""
     for t in (q, k_cache, v_cache):
         if not t.is_cuda:
             raise B2ShapeError("b200kern ops take CUDA tensors (there is no CPU path)")
@@ -127,11 +135,60 @@ def decode_attention(q, k_cache, v_cache, seq_lens, scale=None, page_table=None,
     lib = _lib.load()
     need = int(lib.b2_decode_attn_workspace_size(B, Hq, Hkv, D, S))
     ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    qp = None if q_pos is None else _seq_lens(q_pos, B, q.device)
+    fr = None
+    if rope_freqs is not None:
+        fr = torch.as_tensor(rope_freqs, dtype=torch.float32).to(q.device).contiguous()
+        if fr.numel() != D // 2:
+            raise B2ShapeError(f"rope_freqs must have D/2 = {D // 2} entries")
     _lib.call("b2_decode_attn", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(),
               None if pt is None else pt.data_ptr(), lens.data_ptr(), ws.data_ptr(), B, Hq, Hkv, D, S, ps,
-              max_pages, _lib.strides_arg(ks), _lib.strides_arg(vs), scale, _DT[q.dtype], _DT[k_cache.dtype],
+              max_pages, _lib.strides_arg(ks), _lib.strides_arg(vs), None if qp is None else qp.data_ptr(),
+              int(window), None if fr is None else fr.data_ptr(), scale, _DT[q.dtype], _DT[k_cache.dtype],
               _stream())
     return o
+
+
+def sliding_window_attention(Q, K_cache, V_cache, q_pos, seq_len, window_size, scale=None):
+    """Reference sliding_window_attention (_msl_templates.py:3335-3431):
+    Q [D] (or [H, D]), caches [S, D] (or [H, S, D]); keys
+    [max(0, q_pos + 1 - window_size), min(q_pos + 1, seq_len))."""
+    D = Q.shape[-1]
+    Qh = Q.reshape(1, -1, D)
+    H = Qh.shape[1]
+    K = K_cache.reshape(1, H, -1, D)
+    V = V_cache.reshape(1, H, -1, D)
+    return decode_attention(Qh, K, V, seq_len, scale, q_pos=[int(q_pos)], window=int(window_size)).reshape(Q.shape)
+
+
+def rope_attention(Q, K_cache, V_cache, freqs, seq_len, q_pos):
+    """Reference rope_attention (_msl_templates.py:1770-1887): Q [D] rotated at
+    q_pos, un-rotated caches [S, D] rotated at each key's position, freqs
+    [D/2], scale 1/sqrt(D), keys [0, seq_len)."""
+    D = Q.shape[-1]
+    Qh = Q.reshape(1, -1, D)
+    H = Qh.shape[1]
+    K = K_cache.reshape(1, H, -1, D)
+    V = V_cache.reshape(1, H, -1, D)
+    return decode_attention(Qh, K, V, seq_len, q_pos=[int(q_pos)], rope_freqs=freqs).reshape(Q.shape)
+
+
+def repeat_kv(x, n_rep, out=None):
+    """Reference repeat_kv (_msl_templates.py:3434-3480): [Hkv, S, D] ->
+    [Hkv * n_rep, S, D] with out[h] = x[h // n_rep] (any leading batch dims
+    folded: [..., Hkv, S, D] -> [..., Hkv * n_rep, S, D])."""
+    if not x.is_cuda:
+        raise B2ShapeError("b200kern ops take CUDA tensors (there is no CPU path)")
+    if x.dim() < 3:
+        raise B2ShapeError("repeat_kv takes [..., Hkv, S, D]")
+    x = x.contiguous()
+    *lead, Hkv, S, D = x.shape
+    nb = 1
+    for d in lead:
+        nb *= d
+    res = out if out is not None else torch.empty(*lead, Hkv * n_rep, S, D, dtype=x.dtype, device=x.device)
+    _lib.call("b2_repeat_kv", x.data_ptr(), res.data_ptr(), nb * Hkv, S, D, int(n_rep), x.element_size(), _stream())
+    return res
 
 
 def kv_cache_attention(Q, K_cache, V_cache, seq_len, scale):

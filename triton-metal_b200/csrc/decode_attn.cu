@@ -4,7 +4,8 @@
 // Reference kernels this replaces (triton_metal/codegen/_msl_templates.py):
 //   kv_cache_attention (:1949-2063), gqa_attention (:2064-2164),
 //   batched_kv_decode (:2167-2278), paged_attention (:2279-2404),
-//   multi_head_paged_attention (:2405-2532), fp16_kv_attention (:2533-2627).
+//   multi_head_paged_attention (:2405-2532), fp16_kv_attention (:2533-2627),
+//   sliding_window_attention (:3335-3431), rope_attention (:1770-1887).
 // Those compute one (batch, head) per threadgroup in three passes that
 // recompute Q.K (max, sum, weighted V).  Here:
 //   * one CTA per (KV split, kv head, batch) handles all Hq/Hkv query heads of
@@ -19,6 +20,10 @@
 // (b, h, s); paged K/V [n_pages, page_size, Hkv, D] with page_table
 // [B, max_pages] (logical -> physical page); seq_lens [B].  The KV dtype may
 // differ from the query dtype (fp16 KV with fp32 queries).
+// Options: q_pos [B] (default seq_len - 1) and window W > 0 restrict the
+// keys to [max(0, q_pos + 1 - W), min(q_pos + 1, seq_len)) (sliding window);
+// rope freqs [D/2] rotate q at q_pos and key j at j, pairs (2d, 2d + 1) by
+// angle pos * freqs[d], before the dot products (V is not rotated).
 #include "b2_common.cuh"
 #include <type_traits>
 
@@ -40,7 +45,30 @@ struct Params {
   int B, Hq, Hkv, D, page_size, max_pages, nsplit, split_len;
   int64_t ks[3], vs[3];  // contiguous: (b, h, s) element strides; paged: (page, token, head)
   float scale;
+  const int32_t* q_pos;  // [B] or null (seq_len - 1)
+  int window;            // > 0: sliding window
+  const float* rope;     // [D/2] RoPE frequencies or null
 };
+
+// Key range [lo, hi) of sequence b and its query position.
+__device__ __forceinline__ void key_range(const Params& p, int b, int& lo, int& hi, int& qp) {
+  const int len = p.seq_lens[b];
+  qp = p.q_pos ? p.q_pos[b] : len - 1;
+  lo = 0;
+  hi = len;
+  if (p.window > 0) {
+    lo = max(0, qp + 1 - p.window);
+    hi = min(qp + 1, len);
+  }
+}
+
+// cos / sin of pos * f: the angle is formed and reduced in double precision
+// (positions reach 10^5 radians), the result rounded to float.
+__device__ __forceinline__ float2 rope_cs(double pos, float f) {
+  double sn, cs;
+  sincos(pos * (double)f, &sn, &cs);
+  return make_float2((float)cs, (float)sn);
+}
 
 template <typename T>
 __device__ __forceinline__ float ldf(const T* p) {
@@ -65,12 +93,21 @@ decode_split_kernel(const Params p) {
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rep = p.Hq / p.Hkv;
-  const int len = p.seq_lens[b];
-  const int s0 = split * p.split_len, s1 = min(len, s0 + p.split_len);
+  int lo, hi, qp;
+  key_range(p, b, lo, hi, qp);
+  const int s0 = lo + split * p.split_len, s1 = min(hi, s0 + p.split_len);
 
   for (int e = tid; e < rep * D; e += kThreads) {
     const int hh = e / D, d = e % D;
-    sQ[e] = ldf((const TQ*)p.q + ((int64_t)b * p.Hq + hk * rep + hh) * D + d) * p.scale;
+    const TQ* qrow = (const TQ*)p.q + ((int64_t)b * p.Hq + hk * rep + hh) * D;
+    float val = ldf(qrow + d);
+    if (p.rope) {
+      const int pr = d >> 1;
+      const float2 cs = rope_cs((double)qp, p.rope[pr]);
+      const float a = ldf(qrow + 2 * pr), c = ldf(qrow + 2 * pr + 1);
+      val = (d & 1) ? a * cs.y + c * cs.x : a * cs.x - c * cs.y;
+    }
+    sQ[e] = val * p.scale;
   }
   // per-warp state for its query heads hh = warp, warp + 4, ...
   constexpr int kHPW = kMaxRep / kWarps;       // <= 4 heads per warp
@@ -108,6 +145,17 @@ decode_split_kernel(const Params p) {
       sV[j * LDK + d] = vv;
     }
     __syncthreads();
+    if (p.rope) {  // rotate the staged keys in place at their positions
+      for (int e = tid; e < TK * (D / 2); e += kThreads) {
+        const int j = e / (D / 2), pr = e % (D / 2);
+        const float2 cs = rope_cs((double)(t0 + j), p.rope[pr]);
+        float* kp = sK + j * LDK + 2 * pr;
+        const float a = kp[0], c = kp[1];
+        kp[0] = a * cs.x - c * cs.y;
+        kp[1] = a * cs.y + c * cs.x;
+      }
+      __syncthreads();
+    }
 #pragma unroll
     for (int i = 0; i < kHPW; ++i) {
       const int hh = warp + kWarps * i;
@@ -261,7 +309,7 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return (uint32_t)(r * D * 2 + ((c ^ (r & 7)) << 4));
 }
 
-template <typename T, int D, bool PAGED>
+template <typename T, int D, bool PAGED, bool ROPE>
 __global__ void __launch_bounds__(kThreads, D == 256 ? 1 : 2)
 decode_tc_kernel(const Params p) {
   using C = TcCfg<D>;
@@ -272,8 +320,9 @@ decode_tc_kernel(const Params p) {
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rep = p.Hq / p.Hkv;
-  const int len = p.seq_lens[b];
-  const int s0 = split * p.split_len, s1 = min(len, s0 + p.split_len);
+  int lo, hi, qp;
+  key_range(p, b, lo, hi, qp);
+  const int s0 = lo + split * p.split_len, s1 = min(hi, s0 + p.split_len);
   const int ntiles = s1 > s0 ? (s1 - s0 + TK - 1) / TK : 0;
 
   // q rows (zero padded to 16) -> swizzled smem; plain stores, made visible
@@ -282,6 +331,17 @@ decode_tc_kernel(const Params p) {
     const int r = e / C::kChunks, c = e % C::kChunks;
     uint4 val = make_uint4(0, 0, 0, 0);
     if (r < rep) val = *reinterpret_cast<const uint4*>((const T*)p.q + ((int64_t)b * p.Hq + hk * rep + r) * D + c * 8);
+    if constexpr (ROPE) {  // rotate q at its position (4 pairs per chunk)
+      uint32_t w[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 cs = rope_cs((double)qp, p.rope[c * 4 + u]);
+        const float a = to_f32<T>(reinterpret_cast<const T*>(&w[u])[0]);
+        const float d = to_f32<T>(reinterpret_cast<const T*>(&w[u])[1]);
+        w[u] = pack2<T>(a * cs.x - d * cs.y, a * cs.y + d * cs.x);
+      }
+      val = make_uint4(w[0], w[1], w[2], w[3]);
+    }
     *reinterpret_cast<uint4*>(smem + swz<D>(r, c)) = val;
   }
 
@@ -330,6 +390,15 @@ decode_tc_kernel(const Params p) {
   const int kb_row = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8, kb_chunk = (lane >> 3) & 1;
   const int vb_row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vb_chunk = lane >> 4;
 
+  // RoPE on the staged keys: this thread rotates the chunks it loaded
+  // (4 pairs of chunk cc, rows r0 + i * kRowsPerPass); the angle of the next
+  // row is the previous one times the fixed step rotation.
+  float2 rstep[4];
+  if constexpr (ROPE) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) rstep[u] = rope_cs((double)C::kRowsPerPass, p.rope[cc * 4 + u]);
+  }
+
   for (int t = 0; t < ntiles; ++t) {
     cp_async_wait_grp<C::kStages - 2>();
     __syncthreads();  // tile t visible to all; stage (t - 1) % S free
@@ -340,6 +409,29 @@ decode_tc_kernel(const Params p) {
     }
     const int stage = t % C::kStages;
     const uint32_t tk = sKV + stage * 2 * C::kTileBytes, tv = tk + C::kTileBytes;
+    if constexpr (ROPE) {
+      uint8_t* kt = smem + C::kQBytes + stage * 2 * C::kTileBytes;
+      float2 cs[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) cs[u] = rope_cs((double)(s0 + t * TK + r0), p.rope[cc * 4 + u]);
+#pragma unroll
+      for (int i = 0; i < TK / C::kRowsPerPass; ++i) {
+        uint4* ck = reinterpret_cast<uint4*>(kt + swz<D>(r0 + i * C::kRowsPerPass, cc));
+        uint4 v4 = *ck;
+        uint32_t w[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float a = to_f32<T>(reinterpret_cast<const T*>(&w[u])[0]);
+          const float d = to_f32<T>(reinterpret_cast<const T*>(&w[u])[1]);
+          w[u] = pack2<T>(a * cs[u].x - d * cs[u].y, a * cs[u].y + d * cs[u].x);
+          const float2 nx = make_float2(cs[u].x * rstep[u].x - cs[u].y * rstep[u].y,
+                                        cs[u].x * rstep[u].y + cs[u].y * rstep[u].x);
+          cs[u] = nx;
+        }
+        *ck = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      __syncthreads();  // rotated keys visible to every warp
+    }
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
@@ -482,7 +574,8 @@ extern "C" size_t b2_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t H
 extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void* o, const int32_t* page_table,
                               const int32_t* seq_lens, void* workspace, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
                               int64_t max_seq_len, int64_t page_size, int64_t max_pages, const int64_t* k_strides,
-                              const int64_t* v_strides, float scale, int q_dtype, int kv_dtype, void* stream) {
+                              const int64_t* v_strides, const int32_t* q_pos, int64_t window, const float* rope_freqs,
+                              float scale, int q_dtype, int kv_dtype, void* stream) {
   B2_CHECK_ARG(q && k && v && o && seq_lens && k_strides && v_strides, B2_ERR_INVALID, "decode_attn: null pointer");
   B2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && D > 0 && max_seq_len >= 0, B2_ERR_INVALID, "decode_attn: bad shape");
   B2_CHECK_ARG(Hq % Hkv == 0 && Hq / Hkv <= dec::kMaxRep, B2_ERR_UNSUPPORTED,
@@ -512,8 +605,14 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
     p.vs[i] = v_strides[i];
   }
   p.scale = scale;
-  p.nsplit = dec::choose_splits(p.B, p.Hkv, (int)max_seq_len);
-  p.split_len = (int)((max_seq_len + p.nsplit - 1) / p.nsplit);
+  p.q_pos = q_pos;
+  p.window = (int)(window > 0 ? window : 0);
+  p.rope = rope_freqs;
+  B2_CHECK_ARG(!rope_freqs || D % 2 == 0, B2_ERR_INVALID, "decode_attn: RoPE needs an even head dim");
+  // with a window every sequence has at most `window` keys: split that
+  const int64_t eff_len = (window > 0 && window < max_seq_len) ? window : max_seq_len;
+  p.nsplit = dec::choose_splits(p.B, p.Hkv, (int)eff_len);
+  p.split_len = (int)((eff_len + p.nsplit - 1) / p.nsplit);
   p.split_len = (p.split_len + dec::TK - 1) / dec::TK * dec::TK;
   if (p.split_len == 0) p.split_len = dec::TK;
   p.ws = (float*)workspace;
@@ -526,16 +625,21 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
   bool s16 = true;
   for (int i = 0; i < 3; ++i) s16 = s16 && p.ks[i] % 8 == 0 && p.vs[i] % 8 == 0;
   if (q_dtype == kv_dtype && q_dtype != B2_F32 && (D == 64 || D == 128 || D == 256) && a16 && s16) {
-#define B2_TC(T, DD)                                                                                       \
-  do {                                                                                                     \
-    const int sm = dec::TcCfg<DD>::kSmem;                                                                  \
-    if (page_size) {                                                                                       \
-      cudaFuncSetAttribute(dec::decode_tc_kernel<T, DD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm); \
-      dec::decode_tc_kernel<T, DD, true><<<grid, dec::kThreads, sm, st>>>(p);                              \
-    } else {                                                                                               \
-      cudaFuncSetAttribute(dec::decode_tc_kernel<T, DD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm); \
-      dec::decode_tc_kernel<T, DD, false><<<grid, dec::kThreads, sm, st>>>(p);                             \
-    }                                                                                                      \
+#define B2_TC2(T, DD, PG, RP)                                                                                \
+  do {                                                                                                       \
+    const int sm = dec::TcCfg<DD>::kSmem;                                                                    \
+    cudaFuncSetAttribute(dec::decode_tc_kernel<T, DD, PG, RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm); \
+    dec::decode_tc_kernel<T, DD, PG, RP><<<grid, dec::kThreads, sm, st>>>(p);                                \
+  } while (0)
+#define B2_TC(T, DD)                                    \
+  do {                                                  \
+    if (page_size) {                                    \
+      if (rope_freqs) B2_TC2(T, DD, true, true);        \
+      else B2_TC2(T, DD, true, false);                  \
+    } else {                                            \
+      if (rope_freqs) B2_TC2(T, DD, false, true);       \
+      else B2_TC2(T, DD, false, false);                 \
+    }                                                   \
   } while (0)
 #define B2_TC_D(T)                 \
   do {                             \
@@ -552,6 +656,7 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
     }
 #undef B2_TC_D
 #undef B2_TC
+#undef B2_TC2
     return launch_status("decode_attn");
   }
   const size_t smem = dec::smem_bytes(p.D);
@@ -580,4 +685,45 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
 #undef B2_DEC_KV
 #undef B2_DEC
   return launch_status("decode_attn");
+}
+
+// ---------------------------------------------------------------------------
+// repeat_kv (reference make_repeat_kv_kernel, _msl_templates.py:3434-3480):
+//   out[h, s, d] = in[h / n_rep, s, d],  in [Hkv, S, D] -> out [Hkv n_rep, S, D].
+// Each output head is one contiguous block of S * D elements copied from its
+// kv head; 16-byte vectors when the block allows it (a pure HBM copy).
+// ---------------------------------------------------------------------------
+namespace b2 {
+template <typename V>
+__global__ void repeat_kv_kernel(const V* __restrict__ in, V* __restrict__ out, int64_t per_head, int64_t n_rep,
+                                 int64_t total) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t h = i / per_head, w = i - h * per_head;
+    out[i] = in[(h / n_rep) * per_head + w];
+  }
+}
+}  // namespace b2
+
+extern "C" int b2_repeat_kv(const void* input, void* output, int64_t n_kv_heads, int64_t seq_len, int64_t head_dim,
+                            int64_t n_rep, int64_t elem_bytes, void* stream) {
+  B2_CHECK_ARG(input && output, B2_ERR_INVALID, "repeat_kv: null pointer");
+  B2_CHECK_ARG(n_kv_heads > 0 && seq_len >= 0 && head_dim > 0 && n_rep > 0, B2_ERR_INVALID, "repeat_kv: bad shape");
+  B2_CHECK_ARG(elem_bytes == 1 || elem_bytes == 2 || elem_bytes == 4 || elem_bytes == 8, B2_ERR_DTYPE,
+               "repeat_kv: element size %lld", (long long)elem_bytes);
+  const int64_t bytes = seq_len * head_dim * elem_bytes;  // per head
+  if (bytes == 0) return B2_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t nq = n_kv_heads * n_rep;
+  const int grid = 4 * num_sms();
+  if (bytes % 16 == 0 && aligned(input, 16) && aligned(output, 16)) {
+    repeat_kv_kernel<uint4><<<grid, 256, 0, st>>>((const uint4*)input, (uint4*)output, bytes / 16, n_rep,
+                                                  nq * (bytes / 16));
+  } else if (bytes % 4 == 0 && aligned(input, 4) && aligned(output, 4)) {
+    repeat_kv_kernel<uint32_t><<<grid, 256, 0, st>>>((const uint32_t*)input, (uint32_t*)output, bytes / 4, n_rep,
+                                                     nq * (bytes / 4));
+  } else {
+    repeat_kv_kernel<uint8_t><<<grid, 256, 0, st>>>((const uint8_t*)input, (uint8_t*)output, bytes, n_rep,
+                                                    nq * bytes);
+  }
+  return launch_status("repeat_kv");
 }
