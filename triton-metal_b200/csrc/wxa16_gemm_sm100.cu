@@ -37,13 +37,21 @@ constexpr int kBBytes = BN * BK * 2;   // 32 KB
 constexpr int kAccCols = BN;           // fp32 accumulator columns per buffer
 constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kDequantWarps = 16;
-// W8 with zeros: per-tile row sums of x, [2 accumulators][4 k-quarters][BM]
+// W8 with zeros: per-tile row sums of x, [2 accumulators][4 k-quarters][128 rows] fp32
 constexpr int kXsBytes = 2 * 4 * BM * 4;
 
 template <int MODE>
 struct Cfg {
+  // MODE 2 (W4): a 256-row CTA tile, two M = 128 MMAs per k-step sharing one
+  // dequantised B tile (the dequant work per FLOP halves; TMEM holds the two
+  // M halves instead of a double buffer): 57% -> 85% of the bf16 peak.
+  // MODE 0 / 1: 128 rows, the two TMEM buffers double-buffer consecutive
+  // tiles (W8 with 256 rows fits only 2 stages and measured slower).
+  static constexpr bool TWO = MODE == 2;
+  static constexpr int BMC = TWO ? 2 * BM : BM;
+  static constexpr int kABytesC = BMC * BK * 2;
   static constexpr int kPackedBytes = MODE == 0 ? 0 : (MODE == 1 ? BN * BK : (BK / 8) * BN * 4);
-  static constexpr int kStageBytes = kABytes + kBBytes + kPackedBytes;
+  static constexpr int kStageBytes = kABytesC + kBBytes + kPackedBytes;
   static constexpr int kStages = (220 * 1024) / kStageBytes;
   static constexpr int kWarps = MODE == 0 ? 6 : 6 + kDequantWarps;
   static constexpr int kThreads = kWarps * 32;
@@ -170,7 +178,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sA = smem;
-  uint8_t* sB = sA + C::kStages * kABytes;
+  uint8_t* sB = sA + C::kStages * C::kABytesC;
   uint8_t* sP = sB + C::kStages * kBBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sP + C::kStages * C::kPackedBytes);
   uint64_t* bready = full + C::kStages;
@@ -218,15 +226,15 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % p.tiles_m) * BM, n0 = (tile / p.tiles_m) * BN;
+        const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * BN;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_or_abort(&empty[stage], phase ^ 1, p, 0xB2100001u, abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t bytes = kABytes + (MODE == 0 ? kBBytes : C::kPackedBytes);
+          const uint32_t bytes = C::kABytesC + (MODE == 0 ? kBBytes : C::kPackedBytes);
           mbar_arrive_expect_tx(&full[stage], bytes);
-          tma_load_2d(sA + stage * kABytes, &tmA, kb * BK, m0, &full[stage]);
+          tma_load_2d(sA + stage * C::kABytesC, &tmA, kb * BK, m0, &full[stage]);
           if constexpr (MODE == 0) tma_load_2d(sB + stage * kBBytes, &tmB, kb * BK, n0, &full[stage]);
           if constexpr (MODE == 1) tma_load_2d(sP + stage * C::kPackedBytes, &tmB, kb * BK, n0, &full[stage]);
           if constexpr (MODE == 2) tma_load_2d(sP + stage * C::kPackedBytes, &tmB, n0, kb * (BK / 8), &full[stage]);
@@ -246,6 +254,45 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       bool ok = true;
       int it = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        if constexpr (C::TWO) {
+          // acc half h (TMEM columns h * 256) holds rows h * 128 .. + 127;
+          // each half is released separately by the epilogue of the previous tile
+          const uint32_t tparity = (it & 1) ^ 1;
+          for (int kb = 0; kb < kblocks; ++kb) {
+            if (!wait_or_abort(&full[stage], phase, p, 0xB2100003u, abort_flag) ||
+                !wait_or_abort(&bready[stage], phase, p, 0xB2100004u, abort_flag) ||
+                (kb == 0 && !wait_or_abort(&tempty[0], tparity, p, 0xB2100002u, abort_flag))) {
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
+            const uint64_t da = tc::desc_kmajor_sw128(sA + stage * C::kABytesC);
+            const uint64_t db = tc::desc_kmajor_sw128(sB + stage * kBBytes);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              tc::mma_f16_ss(tmem_base, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+            if (kb == 0) {
+              if (!wait_or_abort(&tempty[1], tparity, p, 0xB210000Au, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc::fence_after_sync();
+            }
+            // rows 128..255 of the A tile start 16 KB in (128-byte rows)
+            const uint64_t da1 = tc::desc_kmajor_sw128(sA + stage * C::kABytesC + BM * BK * 2);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              tc::mma_f16_ss(tmem_base + kAccCols, da1 + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                             (kb | k) != 0);
+            tc::commit(&empty[stage]);
+            if (++stage == C::kStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (ok) tc::commit(&tfull[0]);
+          continue;
+        }
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!wait_or_abort(&tempty[acc], acc_phase ^ 1, p, 0xB2100002u, abort_flag)) break;
@@ -258,7 +305,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             break;
           }
           tc::fence_after_sync();
-          const uint64_t da = tc::desc_kmajor_sw128(sA + stage * kABytes);
+          const uint64_t da = tc::desc_kmajor_sw128(sA + stage * C::kABytesC);
           const uint64_t db = tc::desc_kmajor_sw128(sB + stage * kBBytes);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
@@ -284,60 +331,65 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
-      const int m0 = (tile % p.tiles_m) * BM, n0 = (tile / p.tiles_m) * BN;
-      const int acc = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
+      const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * BN;
+      const int acc = C::TWO ? 0 : (it & 1);
+      const uint32_t acc_phase = C::TWO ? (it & 1) : ((it >> 1) & 1);
       if (!wait_or_abort(&tfull[acc], acc_phase, p, 0xB2100005u, abort_flag)) break;
       tc::fence_after_sync();
-      const int row = m0 + q * 32 + lane;
-      float xs = 0.f;  // W8 with zeros: sum_k x[row, k]
+      float xs2[2] = {0.f, 0.f};  // W8 with zeros: sum_k x[row, k]
       if constexpr (MODE == 1 && ZP) {
+        // double-buffered with the accumulator: the dequantisers refill
+        // buffer acc only after this epilogue released accumulator acc
         if (!wait_or_abort(&xsready[acc], acc_phase, p, 0xB2100008u, abort_flag)) break;
         const float* xb = xsbuf + acc * 4 * BM + q * 32 + lane;
-        xs = (xb[0] + xb[BM]) + (xb[2 * BM] + xb[3 * BM]);
+        xs2[0] = (xb[0] + xb[BM]) + (xb[2 * BM] + xb[3 * BM]);
       }
-      uint16_t* orow = p.out + (size_t)row * p.N + n0;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        // warp-collective: every lane loads, rows / columns past the edge
-        // only skip their stores
-        tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccCols + c * 32, r);
-        tc::tmem_ld_wait();
-        const int nc = n0 + c * 32;
-        if (row >= p.M || nc >= p.N) continue;
-        uint32_t packed[16];
+      for (int h = 0; h < (C::TWO ? 2 : 1); ++h) {
+        const int row = m0 + h * BM + q * 32 + lane;
+        const uint32_t tcol = C::TWO ? h * kAccCols : acc * kAccCols;
+        uint16_t* orow = p.out + (size_t)row * p.N + n0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          // warp-collective: every lane loads, rows / columns past the edge
+          // only skip their stores
+          tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + tcol + c * 32, r);
+          tc::tmem_ld_wait();
+          const int nc = n0 + c * 32;
+          if (row >= p.M || nc >= p.N) continue;
+          uint32_t packed[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
-          if constexpr (MODE == 1) {
-            const int n = nc + 2 * j;
-            if constexpr (ZP) {
-              v0 -= (n < p.N ? ld_act<DT>(p.zeros + n) : 0.f) * xs;
-              v1 -= (n + 1 < p.N ? ld_act<DT>(p.zeros + n + 1) : 0.f) * xs;
+          for (int j = 0; j < 16; ++j) {
+            float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
+            if constexpr (MODE == 1) {
+              const int n = nc + 2 * j;
+              if constexpr (ZP) {
+                v0 -= (n < p.N ? ld_act<DT>(p.zeros + n) : 0.f) * xs2[h];
+                v1 -= (n + 1 < p.N ? ld_act<DT>(p.zeros + n + 1) : 0.f) * xs2[h];
+              }
+              v0 *= n < p.N ? ld_act<DT>(p.scales + n) : 0.f;
+              v1 *= n + 1 < p.N ? ld_act<DT>(p.scales + n + 1) : 0.f;
             }
-            v0 *= n < p.N ? ld_act<DT>(p.scales + n) : 0.f;
-            v1 *= n + 1 < p.N ? ld_act<DT>(p.scales + n + 1) : 0.f;
+            packed[j] = pack_pair<DT>(v0, v1);
           }
-          packed[j] = pack_pair<DT>(v0, v1);
-        }
-        if (nc + 32 <= p.N) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          if (nc + 32 <= p.N) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-        } else {
-          // ragged N (multiple of 8): whole 16-byte pieces only
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (nc + 8 * j < p.N)
+            for (int j = 0; j < 4; ++j)
               dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          } else {
+            // ragged N (multiple of 8): whole 16-byte pieces only
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (nc + 8 * j < p.N)
+                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          }
         }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[C::TWO ? h : acc]);
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   } else if constexpr (MODE != 0) {
     // ------------------------------ dequantisers ------------------------------
@@ -402,15 +454,15 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         if constexpr (MODE == 1 && ZP) {
           // row d % 128 of the x tile, k-quarter d / 128 (two swizzled chunks)
           const int ar = d & (BM - 1), aq = d >> 7;
-          const uint8_t* arow = sA + stage * kABytes + ar * 128;
+          const uint8_t* arow = sA + stage * C::kABytesC + ar * 128;
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             const uint4 v = *reinterpret_cast<const uint4*>(arow + (((2 * aq + cc) ^ (ar & 7)) << 4));
             xsum += sum8<DT>(v);
           }
           if (kb == kblocks - 1) {
-            // hand the row sums to the epilogue; the buffer of this
-            // accumulator is free once its previous epilogue released it
+            // hand the row sums to the epilogue; buffer acc is free once the
+            // epilogue released accumulator acc (the MMA warp's wait)
             const int acc = tile_it & 1;
             if (!wait_or_abort(&tempty[acc], ((tile_it >> 1) & 1) ^ 1, p, 0xB2100009u, abort_flag)) {
               ok = false;
@@ -458,7 +510,7 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   }
   const CUtensorMapDataType adt = DT == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
-  if (!make_tmap_2d(&ta, x, adt, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ERR_INVALID;
+  if (!make_tmap_2d(&ta, x, adt, K, M, K * 2, BK, C::BMC, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ERR_INVALID;
   bool okb;
   if (MODE == 0)
     okb = make_tmap_2d(&tb, w, adt, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -475,7 +527,7 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   p.scales = (const uint16_t*)scales;
   p.zeros = (const uint16_t*)zeros;
   p.out = (uint16_t*)out;
-  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_m = (int)((M + C::BMC - 1) / C::BMC);
   p.tiles_n = (int)((N + BN - 1) / BN);
   p.err = err;
   const int ntiles = p.tiles_m * p.tiles_n;
