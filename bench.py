@@ -344,6 +344,51 @@ class Gemm:
                 "kind": "port", "sample": f"{n} x [{rows} rows of M] x K={self.K} x N={self.N} in {el:.1f} s"}
 
 
+class W4GemvRef(W4Gemv):
+    """C1 in the reference's own layout, read natively: uint8 [N, K/2] (low
+    nibble = even k) and fp16 scales [N, K/G] (same bytes as C1)."""
+    name = "w4a16_gemv_ref"
+    metric = "W4A16 decode GEMV HBM throughput (reference [N, K/2] layout)"
+
+    def __init__(self, M, rank):
+        super().__init__(M, rank)
+        self._gptq0, self._sc0 = self.qw[0], self.sc[0]  # for the CPU baseline
+        ref = self.bk.pack_int4_ref(self.bk.unpack_int4_gptq(self.qw[0].cpu()).t().contiguous())
+        base = ref.cuda()
+        self.qw = [base ^ (i & 0xFF) if i else base for i in range(W4_LAYERS)]
+        self.sc = [s.t().contiguous() for s in self.sc]
+        self.cfg = dict(self.cfg, workload=f"w4a16_gemv_ref M={M} K={W4_K} N={W4_N} G={W4_G} (uint8 [N, K/2])")
+
+    def launch(self, i, stream):
+        self.lib.call("b2_int4_matmul_ref", self.x[i].data_ptr(), self.qw[i].data_ptr(), self.out[i].data_ptr(),
+                      self.sc[i].data_ptr(), None, self.M, W4_N, W4_K, W4_G, 0, stream)
+
+    def e2e_step(self):
+        xd = self.x_host.to("cuda", non_blocking=True)
+        for i in range(W4_LAYERS):
+            self.bk.int4_matmul(xd[i], self.qw[i], self.sc[i], group_size=W4_G, layout="ref", out=self.out[i])
+        self.out_host.copy_(self.out, non_blocking=True)
+        return self.x_host.numel() * 2, self.out.numel() * 2
+
+    def check(self):
+        import numpy as np
+        from oracle import quant as oq
+        torch.cuda.synchronize()
+        q = oq.unpack_int4_ref(self.qw[0].cpu().numpy()).T
+        ref = oq.int4_matmul(self.x[0].double().cpu().numpy(), q, self.sc[0].t().double().cpu().numpy(), None, W4_G)
+        got = self.out[0].double().cpu().numpy()
+        rms = np.sqrt((ref ** 2).mean())
+        return bool((np.abs(got - ref) <= 1e-2 * (np.abs(ref) + rms)).all())
+
+    def cpu_baseline(self, budget_s=10.0):
+        qw, sc = self.qw, self.sc
+        self.qw, self.sc = [self._gptq0], [self._sc0]
+        try:
+            return super().cpu_baseline(budget_s)
+        finally:
+            self.qw, self.sc = qw, sc
+
+
 # --------------------------------------------------------------------------
 # workload: FlashAttention GQA prefill (C3)
 # --------------------------------------------------------------------------
@@ -621,12 +666,14 @@ class Decode:
                 "sample": f"{n} sequences of {self.B} (S={self.S}) in {el:.1f} s; value = sequences decoded per second"}
 
 
-WORKLOADS = {"decode": Decode, "kda": KDA, "fa_gqa": FlashAttn, "w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
+WORKLOADS = {"decode": Decode, "w4a16_gemv_ref": W4GemvRef, "kda": KDA, "fa_gqa": FlashAttn, "w4a16_gemv": W4Gemv, "w4a16_gemm": Gemm, "w8a16_gemm": Gemm, "gemm_bf16": Gemm}
 
 
 def make_workload(args, rank):
     if args.workload == "w4a16_gemv":
         return W4Gemv(args.m, rank)
+    if args.workload == "w4a16_gemv_ref":
+        return W4GemvRef(args.m, rank)
     if args.workload in ("w4a16_gemm", "w8a16_gemm", "gemm_bf16"):
         return Gemm(args.workload, rank)
     if args.workload == "fa_gqa":

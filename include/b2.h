@@ -87,6 +87,20 @@ B2_API int b2_int8_matmul(const void* input, const void* weight, void* output,
                    int dtype, void* stream);
 
 /*
+ * int4_matmul in the reference's own buffers and layouts, natively
+ * (make_int4_matmul_kernel, _msl_templates.py:2682-2745; buffer order
+ * :2705-2712): weight uint8 [N, K/2], byte j of row n = k 2j (low nibble)
+ * and 2j+1 (high nibble) (:2725-2732); scales and zeros [N, K/G] in the
+ * activation dtype (zeros NULL = 8); input [M, K], output [M, N].
+ * M <= 16: K-major mma.sync GEMV (K % 128 == 0, G % 32 == 0); M > 16: the
+ * tcgen05 prefill GEMM (K % 64 == 0, G % 64 == 0); else a generic kernel.
+ */
+B2_API int b2_int4_matmul_ref(const void* input, const void* weight, void* output,
+                              const void* scales, const void* zeros,
+                              int64_t M, int64_t N, int64_t K, int64_t group_size,
+                              int dtype, void* stream);
+
+/*
  * Plain bf16 GEMM on tcgen05: out[M,N] = x[M,K] @ w[N,K]^T (w K-major, the
  * nn.Linear layout), fp32 accumulate, bf16 out.  The dequantised-weight
  * path of the reference's matmuls (x @ dequant(W), _msl_templates.py:2663,

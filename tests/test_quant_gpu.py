@@ -119,14 +119,51 @@ def test_w4_repack_bit_exact(cuda):
     assert np.array_equal(gptq.cpu().numpy(), oq.pack_int4_gptq(q.T))
 
 
+def _close_rms(out, ref, tol=1e-2):
+    """|out - ref| <= tol (|ref| + rms(ref)): for paths whose 16-bit operand is
+    the rounded (q - z) * s (scale folded into the dequantised weight)."""
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    rms = np.sqrt((ref ** 2).mean())
+    err = np.abs(out - ref)
+    assert (err <= tol * (np.abs(ref) + rms)).all(), f"worst ratio {(err / (tol * (np.abs(ref) + rms))).max():.3g}"
+
+
 def test_w4_matches_ref_layout_path(cuda):
+    """GPTQ and reference layouts of the same weights agree with the oracle."""
     import b200kern as bk
     from b200kern.synthetic import w4_inputs
     d = w4_inputs(4, 256, 1024, seed=11)
     ref_w = torch.tensor(oq.pack_int4_ref(d["q"].numpy().T), device=cuda)
     a = bk.int4_matmul(d["x"].to(cuda), d["qweight"].to(cuda), d["scales"].to(cuda))
     b = bk.int4_matmul(d["x"].to(cuda), ref_w, d["scales"].t().contiguous().to(cuda), layout="ref")
-    assert torch.equal(a, b)
+    ref = oq.int4_matmul(d["x"].double().numpy(), d["q"].numpy(), d["scales"].double().numpy(), None, 128)
+    np.testing.assert_allclose(a.double().cpu().numpy(), ref, rtol=1e-2, atol=1e-2)
+    _close_rms(b.double().cpu().numpy(), ref)
+
+
+# ---------------- W4A16 in the reference layout (native) ----------------
+@pytest.mark.parametrize("M", [1, 3, 8, 16, 40, 300])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("zeros", [False, True])
+@pytest.mark.parametrize("G", [32, 128])
+def test_w4_ref_layout_native(cuda, M, dtype, zeros, G):
+    """uint8 [N, K/2] + [N, K/G] scales / zeros read natively: the GEMV
+    (M <= 16), the tcgen05 GEMM (M > 16, G % 64 == 0) or the generic kernel."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(M * 7 + G)
+    N, K = 1000, 2048
+    x = torch.randn(M, K, generator=g).to(dtype)
+    q = torch.randint(0, 16, (N, K), generator=g, dtype=torch.int32)
+    s = (torch.rand(N, K // G, generator=g) * 0.05 + 0.005).to(dtype)
+    z = (torch.rand(N, K // G, generator=g) * 15).to(dtype) if zeros else None
+    w = bk.pack_int4_ref(q)
+    out = bk.int4_matmul(x.to(cuda), w.to(cuda), s.to(cuda), None if z is None else z.to(cuda), group_size=G,
+                         layout="ref")
+    assert out.dtype == dtype and tuple(out.shape) == (M, N)
+    ref = oq.int4_matmul(x.double().numpy(), q.t().numpy(), s.t().double().numpy(),
+                         None if z is None else z.t().double().numpy(), G)
+    _close_rms(out.double().cpu().numpy(), ref)
 
 
 # ---------------- W8A16 GEMV ---------------------------------------------

@@ -23,6 +23,7 @@ SIGNATURES = {
     "b2_last_error": (ctypes.c_char_p, []),
     "b2_device_error": (_i32, [_vp, ctypes.POINTER(ctypes.c_uint)]),
     "b2_int4_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "b2_int4_matmul_ref": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
     "b2_int8_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "b2_gemm_bf16": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "b2_int4_dequant": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),

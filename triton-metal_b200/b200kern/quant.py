@@ -73,7 +73,7 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
     layout="gptq": weight int32 [K/8, N]; scales (and zeros) [K/G, N].
     layout="ref":  weight uint8 [N, K/2] (the reference's buffer); scales
                    and zeros [N, K/G] as in _msl_templates.py:2693-2695.
-                   The weight is repacked on the GPU each call.
+                   Read natively by b2_int4_matmul_ref (no repack).
     zeros=None means the symmetric zero point 8.
     input fp16 / bf16 run natively; fp32 input (the reference's dtype) is
     computed with fp16 activations/scales and returned as fp32.
@@ -86,11 +86,26 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
         if weight.dtype != torch.uint8 or weight.dim() != 2 or weight.shape[1] * 2 != K:
             raise B2ShapeError("ref layout weight must be uint8 [N, K/2]")
         N = weight.shape[0]
-        gptq = torch.empty(K // 8, N, dtype=torch.int32, device=weight.device)
-        _lib.call("b2_int4_repack_ref_to_gptq", _ptr(weight.contiguous()), _ptr(gptq), N, K, _stream())
-        weight = gptq
-        scales = scales.t()
-        zeros = None if zeros is None else zeros.t()
+        if K % group_size or tuple(scales.shape) != (N, K // group_size):
+            raise B2ShapeError(f"ref layout scales must be [N, K/G] = {(N, K // group_size)}")
+        if zeros is not None and tuple(zeros.shape) != tuple(scales.shape):
+            raise B2ShapeError("zeros must have the shape of scales")
+        out_dtype = input.dtype
+        cdt = torch.float16 if input.dtype == torch.float32 else input.dtype
+        if cdt not in _DT:
+            raise B2DtypeError(f"input dtype {input.dtype} unsupported (fp16, bf16, fp32)")
+        x = input.to(cdt).contiguous()
+        s = scales.to(cdt).contiguous()
+        z = None if zeros is None else zeros.to(cdt).contiguous()
+        res = torch.empty(M, N, dtype=cdt, device=input.device)
+        if M:
+            _lib.call("b2_int4_matmul_ref", _ptr(x), _ptr(weight.contiguous()), _ptr(res), _ptr(s), _ptr(z),
+                      M, N, K, group_size, _DT[cdt], _stream())
+        res = res.to(out_dtype)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
     elif layout != LAYOUT_GPTQ:
         raise B2ShapeError(f"unknown layout {layout!r}")
     if weight.dtype != torch.int32 or weight.dim() != 2 or weight.shape[0] * 8 != K:

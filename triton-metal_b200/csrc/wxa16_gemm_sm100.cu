@@ -6,6 +6,9 @@
 //           (reference int8_matmul, _msl_templates.py:2663-2677)
 //   MODE 2: int4 GPTQ int32 [K/8, N] + group scales [K/G, N], zero point 8 or
 //           per-group zeros [K/G, N] (asymmetric)
+//   MODE 3: int4 in the reference's own layout: uint8 [N, K/2], low nibble
+//           = even k, scales (zeros) [N, K/G] (_msl_templates.py:2693-2695,
+//           :2725-2732)                            -> b2_int4_matmul_ref
 //                                                          -> b2_int4_matmul
 //           (reference int4_matmul, _msl_templates.py:2716-2743)
 //
@@ -32,7 +35,6 @@ namespace b2 {
 namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kABytes = BM * BK * 2;   // 16 KB
 constexpr int kBBytes = BN * BK * 2;   // 32 KB
 constexpr int kAccCols = BN;           // fp32 accumulator columns per buffer
 constexpr int kTmemCols = 2 * kAccCols;
@@ -47,10 +49,10 @@ struct Cfg {
   // M halves instead of a double buffer): 57% -> 85% of the bf16 peak.
   // MODE 0 / 1: 128 rows, the two TMEM buffers double-buffer consecutive
   // tiles (W8 with 256 rows fits only 2 stages and measured slower).
-  static constexpr bool TWO = MODE == 2;
+  static constexpr bool TWO = MODE == 2 || MODE == 3;
   static constexpr int BMC = TWO ? 2 * BM : BM;
   static constexpr int kABytesC = BMC * BK * 2;
-  static constexpr int kPackedBytes = MODE == 0 ? 0 : (MODE == 1 ? BN * BK : (BK / 8) * BN * 4);
+  static constexpr int kPackedBytes = MODE == 0 ? 0 : (MODE == 1 ? BN * BK : BN * BK / 2);
   static constexpr int kStageBytes = kABytesC + kBBytes + kPackedBytes;
   static constexpr int kStages = (220 * 1024) / kStageBytes;
   static constexpr int kWarps = MODE == 0 ? 6 : 6 + kDequantWarps;
@@ -115,6 +117,31 @@ __device__ __forceinline__ uint4 dequant8_int4(uint32_t w, uint32_t s2, uint32_t
       else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
     } else {
       const uint32_t v = sub2<DT>(biased, bz2);     // q - zi, exact
+      if constexpr (DT == B2_BF16) asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
+      else asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
+    }
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// Reference layout: byte j of w holds k = 2j (low nibble) and 2j + 1 (high
+// nibble), already a k-ordered pair: one PRMT puts byte j of w and of w >> 4
+// into the two halves, one LOP3 keeps the nibbles and ORs in the bias.
+template <int DT, bool ZP>
+__device__ __forceinline__ uint4 dequant8_int4_ref(uint32_t w, uint32_t s2, uint32_t bz2, uint32_t zr2) {
+  constexpr uint32_t kBias = DT == B2_BF16 ? 0x43004300u : 0x64006400u;
+  constexpr uint32_t kBias8 = DT == B2_BF16 ? 0x43084308u : 0x64086408u;
+  const uint32_t w4 = w >> 4;
+  uint32_t r[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t biased = and_or(prmt(w, w4, (uint32_t)(j | ((4 + j) << 8))), 0x000F000Fu, kBias);
+    if constexpr (!ZP) {
+      const uint32_t v = sub2<DT>(biased, kBias8);
+      if constexpr (DT == B2_BF16) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
+      else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
+    } else {
+      const uint32_t v = sub2<DT>(biased, bz2);
       if constexpr (DT == B2_BF16) asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
       else asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
     }
@@ -238,6 +265,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           if constexpr (MODE == 0) tma_load_2d(sB + stage * kBBytes, &tmB, kb * BK, n0, &full[stage]);
           if constexpr (MODE == 1) tma_load_2d(sP + stage * C::kPackedBytes, &tmB, kb * BK, n0, &full[stage]);
           if constexpr (MODE == 2) tma_load_2d(sP + stage * C::kPackedBytes, &tmB, n0, kb * (BK / 8), &full[stage]);
+          if constexpr (MODE == 3) tma_load_2d(sP + stage * C::kPackedBytes, &tmB, kb * (BK / 2), n0, &full[stage]);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -407,10 +435,11 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       float xsum = 0.f;  // W8 with zeros: this thread's quarter of an x row
       int cur_group = -1;
       for (int kb = 0; kb < kblocks; ++kb) {
-        if (MODE == 2) {
+        if (MODE >= 2) {
           const int grp = kb * BK / p.G;
           if (grp != cur_group) {
-            const size_t gi = (size_t)grp * p.N + n0 + n;
+            // GPTQ: [K/G, N]; reference layout: [N, K/G]
+            const size_t gi = MODE == 2 ? (size_t)grp * p.N + n0 + n : (size_t)(n0 + n) * (p.K / p.G) + grp;
             const float sc = col_ok ? ld_act<DT>(p.scales + gi) : 0.f;
             s2 = splat<DT>(sc);
             if (ZP) {
@@ -435,6 +464,16 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             const int r = h * (BK / 16) + rr;
             const uint4 v = dequant8_int4<DT, ZP>(pk[r * BN + n], s2, bz2, zr2);
             *reinterpret_cast<uint4*>(brow + ((r ^ sw) << 4)) = v;
+          }
+        } else if constexpr (MODE == 3) {
+          // row n of the packed tile: 32 bytes = 64 k, this thread's half is
+          // one 16-byte vector; word i holds k = 32 h + 8 i .. + 7 in k order
+          const uint4 pv = *reinterpret_cast<const uint4*>(sP + stage * C::kPackedBytes + n * (BK / 2) + 16 * h);
+          const uint32_t wv[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 v = dequant8_int4_ref<DT, ZP>(wv[i], s2, bz2, zr2);
+            *reinterpret_cast<uint4*>(brow + (((4 * h + i) ^ sw) << 4)) = v;
           }
         } else {
           const uint4* pk = reinterpret_cast<const uint4*>(sP + stage * C::kPackedBytes + n * BK);
@@ -501,7 +540,7 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
                        int64_t N, int64_t K, int64_t G, cudaStream_t st) {
   using namespace gemm;
   using C = Cfg<MODE>;
-  if (M <= 0 || N % 8 || K % BK || (MODE == 2 && (G % BK || K % G))) return B2_ERR_UNSUPPORTED;
+  if (M <= 0 || N % 8 || K % BK || (MODE >= 2 && (G % BK || K % G))) return B2_ERR_UNSUPPORTED;
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16)) return B2_ERR_UNSUPPORTED;
   unsigned* err = device_error_word();
   if (!err) {
@@ -516,8 +555,10 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
     okb = make_tmap_2d(&tb, w, adt, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   else if (MODE == 1)
     okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, BK, BN);
-  else
+  else if (MODE == 2)
     okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, N, K / 8, N * 4, BN, BK / 8);
+  else
+    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, BK / 2, BN);
   if (!okb) return B2_ERR_INVALID;
   Params p;
   p.M = (int)M;
@@ -559,6 +600,12 @@ using namespace b2;
 int b2_detail_w4_gemm(const void* x, const void* w, void* out, const void* s, const void* z, int64_t M, int64_t N,
                       int64_t K, int64_t G, int dtype, cudaStream_t st) {
   return launch_gemm_any<2>(x, w, s, z, out, M, N, K, G, dtype, st);
+}
+
+// Called by b2_int4_matmul_ref for M > 16: the reference's [N, K/2] layout.
+int b2_detail_w4_gemm_ref(const void* x, const void* w, void* out, const void* s, const void* z, int64_t M,
+                          int64_t N, int64_t K, int64_t G, int dtype, cudaStream_t st) {
+  return launch_gemm_any<3>(x, w, s, z, out, M, N, K, G, dtype, st);
 }
 
 // Called by b2_int8_matmul for M > 16 (fp16 / bf16, symmetric or per-channel zeros).
