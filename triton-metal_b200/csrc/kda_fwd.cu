@@ -163,7 +163,13 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
     for (int x = 0; x < 4; ++x)
 #pragma unroll
       for (int y = 0; y < 4; ++y) akk[x][y] = aqk[x][y] = 0.f;
-    for (int d = split; d < DK; d += 4) {
+    // d visits split + 4 m in an order rotated by the task's slot in the warp:
+    // the 8 tasks of a warp start on rows that are multiples of 4 apart
+    // (= the same bank at row stride 136), so unrotated they would read the
+    // same bank; rotated, the 32 lanes cover 32 banks at every step
+    const int rot = (tid >> 2) & 7;
+    for (int it = 0; it < DK / 4; ++it) {
+      const int d = split + 4 * ((it + rot) & (DK / 4 - 1));
       const float gr = sG[r * LD + d];
       float ki[4], qi[4], kj[4];
 #pragma unroll
