@@ -32,9 +32,6 @@ namespace b2 {
 namespace kda {
 
 constexpr int C = 64, DK = 128, DV = 128;
-constexpr int VB = 16;  // state columns per CTA in kernel B
-constexpr int kBThreads = 256;
-constexpr int LDS = DK + 4;  // padded, 16-byte aligned row stride (kernel B)
 
 // Workspace block per (b, h, chunk), floats
 constexpr size_t kWsW = 0;
