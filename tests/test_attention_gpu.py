@@ -114,6 +114,20 @@ def test_fa_oracle_small_bf16(cuda):
     _close(out, torch.from_numpy(ref))
 
 
+def test_fa_c0_config(cuda):
+    """BASELINE configs[0] (the reference's CPU-runnable case): fp32
+    [2, 8, 1024, 64], causal, scale 1/8, q then k then v ~ N(0, 1) from
+    seed 0, against the float64 restatement of _ref_attention."""
+    import b200kern as bk
+    torch.manual_seed(0)
+    q = torch.randn(2, 8, 1024, 64, dtype=torch.float32)
+    k = torch.randn(2, 8, 1024, 64, dtype=torch.float32)
+    v = torch.randn(2, 8, 1024, 64, dtype=torch.float32)
+    o = bk.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=True, scale=0.125)
+    ref = oatt.attention(q.double().numpy(), k.double().numpy(), v.double().numpy(), causal=True, scale=0.125)
+    np.testing.assert_allclose(o.double().cpu().numpy(), ref, rtol=1e-3, atol=1e-3)
+
+
 def test_fa_no_bounded_wait_ran_out(cuda):
     import ctypes
     from b200kern import _lib
