@@ -39,8 +39,8 @@ constexpr int kBBytes = BN * BK * 2;   // 32 KB
 constexpr int kAccCols = BN;           // fp32 accumulator columns per buffer
 constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kDequantWarps = 16;
-// W8 with zeros: per-tile row sums of x, [2 accumulators][4 k-quarters][128 rows] fp32
-constexpr int kXsBytes = 2 * 4 * BM * 4;
+// W8 with zeros: per-tile row sums of x, [2 k-halves][256 rows] fp32
+constexpr int kXsBytes = 2 * 2 * BM * 4;
 
 template <int MODE>
 struct Cfg {
@@ -49,15 +49,21 @@ struct Cfg {
   // M halves instead of a double buffer): 57% -> 85% of the bf16 peak.
   // MODE 0 / 1: 128 rows, the two TMEM buffers double-buffer consecutive
   // tiles (W8 with 256 rows fits only 2 stages and measured slower).
-  static constexpr bool TWO = MODE == 2 || MODE == 3;
+  static constexpr bool TWO = MODE != 0;
+  // W8: the dequantised B tile lives outside the stage ring, double-buffered
+  // (B buffer kbi & 1 per k-block), so 3 stages of A + packed int8 fit next
+  // to the 256-row A tiles (with B in the ring only 2 stages would fit)
+  static constexpr bool SPLITB = MODE == 1;
   static constexpr int BMC = TWO ? 2 * BM : BM;
   static constexpr int kABytesC = BMC * BK * 2;
   static constexpr int kPackedBytes = MODE == 0 ? 0 : (MODE == 1 ? BN * BK : BN * BK / 2);
-  static constexpr int kStageBytes = kABytesC + kBBytes + kPackedBytes;
-  static constexpr int kStages = (220 * 1024) / kStageBytes;
+  static constexpr int kStageBytes = kABytesC + (SPLITB ? 0 : kBBytes) + kPackedBytes;
+  static constexpr int kStages = SPLITB ? 3 : (220 * 1024) / kStageBytes;
+  static constexpr int kBRegion = SPLITB ? 2 * kBBytes : kStages * kBBytes;
   static constexpr int kWarps = MODE == 0 ? 6 : 6 + kDequantWarps;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + (SPLITB ? kBRegion : 0) + 1024 /*align*/ +
+                                  256 /*barriers*/ +
                                   (MODE == 1 ? kXsBytes : 0);
 };
 
@@ -206,7 +212,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sA = smem;
   uint8_t* sB = sA + C::kStages * C::kABytesC;
-  uint8_t* sP = sB + C::kStages * kBBytes;
+  uint8_t* sP = sB + C::kBRegion;
   uint64_t* full = reinterpret_cast<uint64_t*>(sP + C::kStages * C::kPackedBytes);
   uint64_t* bready = full + C::kStages;
   uint64_t* empty = bready + C::kStages;
@@ -214,7 +220,9 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* xsready = drain + 1;  // W8 with zeros: row sums of the tile written
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xsready + 2);
+  uint64_t* xsfree = xsready + 2;  // ... and read by the epilogue (once per tile)
+  uint64_t* bempty = xsfree + 1;   // W8: B buffer b read by its MMAs
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* xsbuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // MODE 1 && ZP
 
@@ -232,7 +240,9 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
       mbar_init(&xsready[a], kDequantWarps);
+      mbar_init(&bempty[a], 1);
     }
+    mbar_init(xsfree, 4);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -281,21 +291,25 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       uint32_t phase = 0;
       bool ok = true;
       int it = 0;
+      int kbi = 0;  // k-blocks issued so far (B buffer of the W8 mode)
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
         if constexpr (C::TWO) {
           // acc half h (TMEM columns h * 256) holds rows h * 128 .. + 127;
           // each half is released separately by the epilogue of the previous tile
           const uint32_t tparity = (it & 1) ^ 1;
-          for (int kb = 0; kb < kblocks; ++kb) {
+          for (int kb = 0; kb < kblocks; ++kb, ++kbi) {
+            // B: this stage's tile, or (W8) buffer kbi & 1, filled once per use
+            const int bb = C::SPLITB ? (kbi & 1) : stage;
+            const uint32_t bpar = C::SPLITB ? ((kbi >> 1) & 1) : phase;
             if (!wait_or_abort(&full[stage], phase, p, 0xB2100003u, abort_flag) ||
-                !wait_or_abort(&bready[stage], phase, p, 0xB2100004u, abort_flag) ||
+                !wait_or_abort(&bready[bb], bpar, p, 0xB2100004u, abort_flag) ||
                 (kb == 0 && !wait_or_abort(&tempty[0], tparity, p, 0xB2100002u, abort_flag))) {
               ok = false;
               break;
             }
             tc::fence_after_sync();
             const uint64_t da = tc::desc_kmajor_sw128(sA + stage * C::kABytesC);
-            const uint64_t db = tc::desc_kmajor_sw128(sB + stage * kBBytes);
+            const uint64_t db = tc::desc_kmajor_sw128(sB + bb * kBBytes);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
               tc::mma_f16_ss(tmem_base, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb | k) != 0);
@@ -313,6 +327,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
               tc::mma_f16_ss(tmem_base + kAccCols, da1 + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
                              (kb | k) != 0);
             tc::commit(&empty[stage]);
+            if constexpr (C::SPLITB) tc::commit(&bempty[bb]);
             if (++stage == C::kStages) {
               stage = 0;
               phase ^= 1;
@@ -364,13 +379,16 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       const uint32_t acc_phase = C::TWO ? (it & 1) : ((it >> 1) & 1);
       if (!wait_or_abort(&tfull[acc], acc_phase, p, 0xB2100005u, abort_flag)) break;
       tc::fence_after_sync();
-      float xs2[2] = {0.f, 0.f};  // W8 with zeros: sum_k x[row, k]
+      float xs2[2] = {0.f, 0.f};  // W8 with zeros: sum_k x[row, k] of both row halves
       if constexpr (MODE == 1 && ZP) {
-        // double-buffered with the accumulator: the dequantisers refill
-        // buffer acc only after this epilogue released accumulator acc
-        if (!wait_or_abort(&xsready[acc], acc_phase, p, 0xB2100008u, abort_flag)) break;
-        const float* xb = xsbuf + acc * 4 * BM + q * 32 + lane;
-        xs2[0] = (xb[0] + xb[BM]) + (xb[2 * BM] + xb[3 * BM]);
+        if (!wait_or_abort(&xsready[0], it & 1, p, 0xB2100008u, abort_flag)) break;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float* xb = xsbuf + h * BM + q * 32 + lane;
+          xs2[h] = xb[0] + xb[2 * BM];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xsfree);  // the dequantisers may overwrite it
       }
 #pragma unroll 1
       for (int h = 0; h < (C::TWO ? 2 : 1); ++h) {
@@ -428,13 +446,14 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     uint32_t phase = 0;
     bool ok = true;
     int tile_it = 0;
+    int kbi = 0;  // k-blocks dequantised so far (B buffer of the W8 mode)
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tile_it) {
       const int n0 = (tile / p.tiles_m) * BN;
       const bool col_ok = n0 + n < p.N;
       uint32_t s2 = 0, bz2 = 0, zr2 = 0;
       float xsum = 0.f;  // W8 with zeros: this thread's quarter of an x row
       int cur_group = -1;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = 0; kb < kblocks; ++kb, ++kbi) {
         if (MODE >= 2) {
           const int grp = kb * BK / p.G;
           if (grp != cur_group) {
@@ -451,11 +470,13 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             cur_group = grp;
           }
         }
-        if (!wait_or_abort(&full[stage], phase, p, 0xB2100006u, abort_flag)) {
+        const int bb = C::SPLITB ? (kbi & 1) : stage;
+        if (!wait_or_abort(&full[stage], phase, p, 0xB2100006u, abort_flag) ||
+            (C::SPLITB && !wait_or_abort(&bempty[bb], ((kbi >> 1) & 1) ^ 1, p, 0xB210000Bu, abort_flag))) {
           ok = false;
           break;
         }
-        uint8_t* brow = sB + stage * kBBytes + n * 128;
+        uint8_t* brow = sB + bb * kBBytes + n * 128;
         const int sw = n & 7;
         if constexpr (MODE == 2) {
           const uint32_t* pk = reinterpret_cast<const uint32_t*>(sP + stage * C::kPackedBytes);
@@ -491,31 +512,30 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           }
         }
         if constexpr (MODE == 1 && ZP) {
-          // row d % 128 of the x tile, k-quarter d / 128 (two swizzled chunks)
-          const int ar = d & (BM - 1), aq = d >> 7;
+          // row d % 256 of the x tile, k-half d / 256 (four swizzled chunks)
+          const int ar = d & (2 * BM - 1), aq = d >> 8;
           const uint8_t* arow = sA + stage * C::kABytesC + ar * 128;
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const uint4 v = *reinterpret_cast<const uint4*>(arow + (((2 * aq + cc) ^ (ar & 7)) << 4));
+          for (int cc = 0; cc < 4; ++cc) {
+            const uint4 v = *reinterpret_cast<const uint4*>(arow + (((4 * aq + cc) ^ (ar & 7)) << 4));
             xsum += sum8<DT>(v);
           }
           if (kb == kblocks - 1) {
-            // hand the row sums to the epilogue; buffer acc is free once the
-            // epilogue released accumulator acc (the MMA warp's wait)
-            const int acc = tile_it & 1;
-            if (!wait_or_abort(&tempty[acc], ((tile_it >> 1) & 1) ^ 1, p, 0xB2100009u, abort_flag)) {
+            // hand the row sums to the epilogue once it has read the previous
+            // tile's (xsfree completes once per tile)
+            if (!wait_or_abort(xsfree, (tile_it & 1) ^ 1, p, 0xB2100009u, abort_flag)) {
               ok = false;
               break;
             }
-            xsbuf[acc * 4 * BM + aq * BM + ar] = xsum;
+            xsbuf[aq * 2 * BM + ar] = xsum;
             xsum = 0.f;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&xsready[acc]);
+            if (lane == 0) mbar_arrive(&xsready[0]);
           }
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bready[stage]);
+        if (lane == 0) mbar_arrive(&bready[bb]);
         if (++stage == C::kStages) {
           stage = 0;
           phase ^= 1;
