@@ -4,6 +4,8 @@ The library is built in-tree by ``csrc/build.py``.  There is no fallback:
 if the library or a GPU is missing, every op raises.
 """
 import ctypes
+
+import torch
 import os
 
 from .errors import B2Error, raise_for_status
@@ -71,3 +73,13 @@ def call(name, *args):
 
 def strides_arg(t):
     return (ctypes.c_int64 * 3)(*t)
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def current_stream():
+    """cudaStream_t of the caller's current stream on the current device."""
+    if _raw_stream is not None:
+        return _raw_stream(torch.cuda.current_device())
+    return torch.cuda.current_stream().cuda_stream

@@ -24,7 +24,7 @@ _DT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 
 
 def _stream():
-    return torch.cuda.current_stream().cuda_stream
+    return _lib.current_stream()
 
 
 def _strides(t):

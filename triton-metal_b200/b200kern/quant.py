@@ -22,7 +22,7 @@ LAYOUT_REF = "ref"    # uint8 [N, K/2], low nibble = even k (the reference's)
 
 
 def _stream():
-    return torch.cuda.current_stream().cuda_stream
+    return _lib.current_stream()
 
 
 def _check_cuda(*ts):
@@ -78,6 +78,25 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
     input fp16 / bf16 run natively; fp32 input (the reference's dtype) is
     computed with fp16 activations/scales and returned as fp32.
     """
+    if (layout == LAYOUT_GPTQ and zeros is None and input.dtype in _DT and scales.dtype == input.dtype
+            and weight.dtype == torch.int32 and input.dim() == 2 and weight.dim() == 2 and scales.dim() == 2
+            and input.is_cuda and weight.is_cuda and scales.is_cuda and input.is_contiguous()
+            and weight.is_contiguous() and scales.is_contiguous()):
+        # common decode / prefill case: no conversion or copy, straight to the kernel
+        M, K = input.shape
+        N = weight.shape[1]
+        if weight.shape[0] * 8 == K and K % group_size == 0 and scales.shape == (K // group_size, N):
+            if out is not None and out.dtype == input.dtype and out.is_contiguous() and out.shape == (M, N):
+                res = out
+            else:
+                res = torch.empty(M, N, dtype=input.dtype, device=input.device)
+            if M:
+                _lib.call("b2_int4_matmul", input.data_ptr(), weight.data_ptr(), res.data_ptr(), scales.data_ptr(),
+                          None, M, N, K, group_size, _DT[input.dtype], _stream())
+            if out is not None and res is not out:
+                out.copy_(res)
+                return out
+            return res
     _check_cuda(input, weight, scales, zeros)
     if input.dim() != 2:
         raise B2ShapeError(f"input must be [M, K], got {tuple(input.shape)}")
