@@ -49,6 +49,17 @@ __device__ __forceinline__ float ld(const T* p) {
   if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float*>(p);
   else return to_f32<T>(*p);
 }
+// 4 consecutive elements (16 bytes for fp32, 8 for 16-bit types) as floats
+template <typename T>
+__device__ __forceinline__ float4 ld4(const T* p) {
+  if constexpr (sizeof(T) == 4) {
+    return *reinterpret_cast<const float4*>(p);
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const T* h = reinterpret_cast<const T*>(&u);
+    return make_float4(to_f32<T>(h[0]), to_f32<T>(h[1]), to_f32<T>(h[2]), to_f32<T>(h[3]));
+  }
+}
 
 // ---- tf32 warp MMA (m16n8k8), fp32 accumulate -------------------------------
 __device__ __forceinline__ uint32_t tf32(float x) {
@@ -119,14 +130,15 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
   const int64_t row0 = ((int64_t)b * Tlen + (int64_t)chunk * C) * H + h;
   float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
 
-  // ---- 1. load ----
-  for (int e = tid; e < C * DK; e += kA2Threads) {
-    const int t = e / DK, d = e % DK;
+  // ---- 1. load (4 consecutive d per thread: 8- or 16-byte loads, float4 stores) ----
+  for (int e = tid; e < C * DK / 4; e += kA2Threads) {
+    const int t = e / (DK / 4), d = 4 * (e % (DK / 4));
     const int64_t off = (row0 + (int64_t)t * H) * DK + d;
-    sK[t * LD + d] = ld(k + off);
-    sQ[t * LD + d] = ld(q + off) * scale;
-    sG[t * LD + d] = g[off];
-    sV[t * LD + d] = ld(v + (row0 + (int64_t)t * H) * DV + d);
+    const float4 kk = ld4(k + off), qq = ld4(q + off), vv = ld4(v + (row0 + (int64_t)t * H) * DV + d);
+    *reinterpret_cast<float4*>(sK + t * LD + d) = kk;
+    *reinterpret_cast<float4*>(sQ + t * LD + d) = make_float4(qq.x * scale, qq.y * scale, qq.z * scale, qq.w * scale);
+    *reinterpret_cast<float4*>(sG + t * LD + d) = *reinterpret_cast<const float4*>(g + off);
+    *reinterpret_cast<float4*>(sV + t * LD + d) = vv;
   }
   if (tid < C) sBeta[tid] = ld(beta + row0 + (int64_t)tid * H);
   for (int e = tid; e < C * LT; e += kA2Threads) {
@@ -242,13 +254,27 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
   // ---- 3a. outputs that need raw Q / K; then beta K e^G into sQ, beta V into sV ----
   {
     const float* glr = sG + (C - 1) * LD;
-    for (int e = tid; e < C * DK; e += kA2Threads) {
-      const int t = e / DK, d = e % DK;
-      const float gi = sG[t * LD + d], kk = sK[t * LD + d], bt = sBeta[t];
-      blk[kWsQg + t * DK + d] = sQ[t * LD + d] * __expf(gi);
-      blk[kWsKr + t * DK + d] = kk * __expf(glr[d] - gi);
-      sQ[t * LD + d] = bt * kk * __expf(gi);
-      sV[t * LD + d] *= bt;
+    for (int e = tid; e < C * DK / 4; e += kA2Threads) {
+      const int t = e / (DK / 4), d = 4 * (e % (DK / 4));
+      const float bt = sBeta[t];
+      const float4 gi = *reinterpret_cast<const float4*>(sG + t * LD + d);
+      const float4 kk = *reinterpret_cast<const float4*>(sK + t * LD + d);
+      const float4 qq = *reinterpret_cast<const float4*>(sQ + t * LD + d);
+      const float4 gl = *reinterpret_cast<const float4*>(glr + d);
+      float4 vv = *reinterpret_cast<const float4*>(sV + t * LD + d);
+      const float4 eg = make_float4(__expf(gi.x), __expf(gi.y), __expf(gi.z), __expf(gi.w));
+      *reinterpret_cast<float4*>(blk + kWsQg + t * DK + d) =
+          make_float4(qq.x * eg.x, qq.y * eg.y, qq.z * eg.z, qq.w * eg.w);
+      *reinterpret_cast<float4*>(blk + kWsKr + t * DK + d) =
+          make_float4(kk.x * __expf(gl.x - gi.x), kk.y * __expf(gl.y - gi.y), kk.z * __expf(gl.z - gi.z),
+                      kk.w * __expf(gl.w - gi.w));
+      *reinterpret_cast<float4*>(sQ + t * LD + d) =
+          make_float4(bt * kk.x * eg.x, bt * kk.y * eg.y, bt * kk.z * eg.z, bt * kk.w * eg.w);
+      vv.x *= bt;
+      vv.y *= bt;
+      vv.z *= bt;
+      vv.w *= bt;
+      *reinterpret_cast<float4*>(sV + t * LD + d) = vv;
     }
     for (int e = tid; e < C * C; e += kA2Threads) blk[kWsAq + e] = sAq[(e / C) * LT + (e % C)];
     if (tid < DK) blk[kWsGl + tid] = __expf(glr[tid]);
@@ -600,6 +626,8 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
                           int64_t T, int64_t H, int64_t Dk, int64_t Dv, int64_t chunk, float scale, int dtype,
                           void* stream) {
   B2_CHECK_ARG(q && k && v && g && beta && o && workspace, B2_ERR_INVALID, "kda_fwd: null pointer");
+  B2_CHECK_ARG(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(g, 16), B2_ERR_ALIGN,
+               "kda_fwd: q, k, v and g must be 16-byte aligned");
   B2_CHECK_ARG(B > 0 && T > 0 && H > 0, B2_ERR_INVALID, "kda_fwd: bad shape");
   B2_CHECK_ARG(Dk == kda::DK && Dv == kda::DV, B2_ERR_UNSUPPORTED, "kda_fwd: Dk = Dv = 128 only (got %lld, %lld)",
                (long long)Dk, (long long)Dv);
