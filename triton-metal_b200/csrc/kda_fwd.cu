@@ -43,6 +43,13 @@ constexpr size_t kWsGl = kWsAq + (size_t)C * C;
 constexpr size_t kWsVp = kWsGl + DK;                  // V' = U - W S (state pass -> output)
 constexpr size_t kWsS = kWsVp + (size_t)C * DV;       // state entering the chunk
 constexpr size_t kWsBlock = kWsS + (size_t)DK * DV;
+// Qg, A_qk, V' and S_c feed only the output kernel's tf32 MMAs, whose 10-bit
+// mantissa fp16 matches (all four are O(1)): they are stored as fp16 in the
+// first half of their fp32-sized regions, halving the output pass's traffic.
+__device__ __forceinline__ __half* ws_h(float* blk, size_t off) { return reinterpret_cast<__half*>(blk + off); }
+__device__ __forceinline__ const __half* ws_h(const float* blk, size_t off) {
+  return reinterpret_cast<const __half*>(blk + off);
+}
 
 template <typename T>
 __device__ __forceinline__ float ld(const T* p) {
@@ -263,8 +270,11 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
       const float4 gl = *reinterpret_cast<const float4*>(glr + d);
       float4 vv = *reinterpret_cast<const float4*>(sV + t * LD + d);
       const float4 eg = make_float4(__expf(gi.x), __expf(gi.y), __expf(gi.z), __expf(gi.w));
-      *reinterpret_cast<float4*>(blk + kWsQg + t * DK + d) =
-          make_float4(qq.x * eg.x, qq.y * eg.y, qq.z * eg.z, qq.w * eg.w);
+      {
+        __half2 lo = __floats2half2_rn(qq.x * eg.x, qq.y * eg.y), hi = __floats2half2_rn(qq.z * eg.z, qq.w * eg.w);
+        *reinterpret_cast<uint2*>(ws_h(blk, kWsQg) + t * DK + d) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+      }
       *reinterpret_cast<float4*>(blk + kWsKr + t * DK + d) =
           make_float4(kk.x * __expf(gl.x - gi.x), kk.y * __expf(gl.y - gi.y), kk.z * __expf(gl.z - gi.z),
                       kk.w * __expf(gl.w - gi.w));
@@ -276,7 +286,11 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
       vv.w *= bt;
       *reinterpret_cast<float4*>(sV + t * LD + d) = vv;
     }
-    for (int e = tid; e < C * C; e += kA2Threads) blk[kWsAq + e] = sAq[(e / C) * LT + (e % C)];
+    for (int e = tid; e < C * C / 2; e += kA2Threads) {
+      const int r = (2 * e) / C, c2 = (2 * e) % C;
+      *reinterpret_cast<__half2*>(ws_h(blk, kWsAq) + 2 * e) =
+          __floats2half2_rn(sAq[r * LT + c2], sAq[r * LT + c2 + 1]);
+    }
     if (tid < DK) blk[kWsGl + tid] = __expf(glr[tid]);
   }
   // ---- 3b. diagonal blocks of T: column j of block D solved in registers ----
@@ -440,7 +454,8 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
           const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = v0 + 8 * nt + 2 * t;
-          *reinterpret_cast<float2*>(blk + kWsS + row * DV + col) = make_float2(acc[mt][nt][e], acc[mt][nt][e + 1]);
+          *reinterpret_cast<__half2*>(ws_h(blk, kWsS) + row * DV + col) =
+              __floats2half2_rn(acc[mt][nt][e], acc[mt][nt][e + 1]);
         }
 
     // V' = U - W S: warp w owns chunk rows 16w .. 16w+15
@@ -470,7 +485,7 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
           const float v0f = sU[row * LB + col] - p[nt][e], v1f = sU[row * LB + col + 1] - p[nt][e + 1];
           sVp[row * LB + col] = v0f;
           sVp[row * LB + col + 1] = v1f;
-          *reinterpret_cast<float2*>(blk + kWsVp + row * DV + v0 + col) = make_float2(v0f, v1f);
+          *reinterpret_cast<__half2*>(ws_h(blk, kWsVp) + row * DV + v0 + col) = __floats2half2_rn(v0f, v1f);
         }
     }
     __syncthreads();  // V' complete; every warp finished reading sS
@@ -534,41 +549,43 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 //   O = (scale Q o e^G) S_c + A_qk V'     (64 x 128; tf32 MMAs)
 // ---------------------------------------------------------------------------
 constexpr int kCThreads = 128;
-constexpr int LQ = DK + 4;   // A reads (row g, col t)
-constexpr int LAQ = C + 4;
-constexpr int LBS = DV + 8;  // B reads (row t, col g)
+constexpr int LQ = DK + 8;   // halves; A reads (row g, col t): word stride 68 = 4 banks apart
+constexpr int LAQ = C + 8;   // halves; word stride 36
+constexpr int LBS = DV + 8;  // halves; B reads (row t, col g)
 constexpr int kCQ = 0;
 constexpr int kCA = kCQ + C * LQ;
 constexpr int kCS = kCA + C * LAQ;
 constexpr int kCV = kCS + DK * LBS;
-constexpr int kCFloats = kCV + C * LBS;
-constexpr size_t kCSmem = (size_t)kCFloats * 4;
+constexpr int kCHalves = kCV + C * LBS;
+constexpr size_t kCSmem = (size_t)kCHalves * 2;
+
+__device__ __forceinline__ uint32_t tf32h(__half x) { return tf32(__half2float(x)); }  // exact
 
 template <typename T>
-__global__ void __launch_bounds__(kCThreads, 1)
+__global__ void __launch_bounds__(kCThreads, 2)
 kda_output_kernel(const float* __restrict__ ws, T* __restrict__ o, int B, int Tlen, int H) {
-  extern __shared__ __align__(16) float sm[];
-  float* sQ = sm + kCQ;
-  float* sA = sm + kCA;
-  float* sS = sm + kCS;
-  float* sV = sm + kCV;
+  extern __shared__ __align__(16) __half smh[];
+  __half* sQ = smh + kCQ;
+  __half* sA = smh + kCA;
+  __half* sS = smh + kCS;
+  __half* sV = smh + kCV;
   const int nc = Tlen / C;
   const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
-  for (int e = tid; e < C * DK / 4; e += kCThreads) {
-    const int r = e / (DK / 4), c4 = e % (DK / 4);
-    cp_async16(sQ + r * LQ + 4 * c4, blk + kWsQg + r * DK + 4 * c4);
-    cp_async16(sV + r * LBS + 4 * c4, blk + kWsVp + r * DV + 4 * c4);
+  for (int e = tid; e < C * DK / 8; e += kCThreads) {
+    const int r = e / (DK / 8), c8 = e % (DK / 8);
+    cp_async16(sQ + r * LQ + 8 * c8, ws_h(blk, kWsQg) + r * DK + 8 * c8);
+    cp_async16(sV + r * LBS + 8 * c8, ws_h(blk, kWsVp) + r * DV + 8 * c8);
   }
-  for (int e = tid; e < DK * DV / 4; e += kCThreads) {
-    const int r = e / (DV / 4), c4 = e % (DV / 4);
-    cp_async16(sS + r * LBS + 4 * c4, blk + kWsS + r * DV + 4 * c4);
+  for (int e = tid; e < DK * DV / 8; e += kCThreads) {
+    const int r = e / (DV / 8), c8 = e % (DV / 8);
+    cp_async16(sS + r * LBS + 8 * c8, ws_h(blk, kWsS) + r * DV + 8 * c8);
   }
-  for (int e = tid; e < C * C / 4; e += kCThreads) {
-    const int r = e / (C / 4), c4 = e % (C / 4);
-    cp_async16(sA + r * LAQ + 4 * c4, blk + kWsAq + r * C + 4 * c4);
+  for (int e = tid; e < C * C / 8; e += kCThreads) {
+    const int r = e / (C / 8), c8 = e % (C / 8);
+    cp_async16(sA + r * LAQ + 8 * c8, ws_h(blk, kWsAq) + r * C + 8 * c8);
   }
   cp_async_commit();
   cp_async_wait<0>();
@@ -583,23 +600,23 @@ kda_output_kernel(const float* __restrict__ ws, T* __restrict__ o, int B, int Tl
 #pragma unroll 2
   for (int ks = 0; ks < DK / 8; ++ks) {
     const int k0 = 8 * ks;
-    const uint32_t a0 = tf32(sQ[(r0 + g) * LQ + k0 + t]), a1 = tf32(sQ[(r0 + g + 8) * LQ + k0 + t]);
-    const uint32_t a2 = tf32(sQ[(r0 + g) * LQ + k0 + t + 4]), a3 = tf32(sQ[(r0 + g + 8) * LQ + k0 + t + 4]);
+    const uint32_t a0 = tf32h(sQ[(r0 + g) * LQ + k0 + t]), a1 = tf32h(sQ[(r0 + g + 8) * LQ + k0 + t]);
+    const uint32_t a2 = tf32h(sQ[(r0 + g) * LQ + k0 + t + 4]), a3 = tf32h(sQ[(r0 + g + 8) * LQ + k0 + t + 4]);
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt)
-      mma_tf32(acc[nt], a0, a1, a2, a3, tf32(sS[(k0 + t) * LBS + 8 * nt + g]),
-               tf32(sS[(k0 + t + 4) * LBS + 8 * nt + g]));
+      mma_tf32(acc[nt], a0, a1, a2, a3, tf32h(sS[(k0 + t) * LBS + 8 * nt + g]),
+               tf32h(sS[(k0 + t + 4) * LBS + 8 * nt + g]));
   }
   // A_qk is lower triangular: k-steps beyond this warp's last row contribute 0
   const int ksteps = (r0 + 16) / 8;
   for (int ks = 0; ks < ksteps; ++ks) {
     const int k0 = 8 * ks;
-    const uint32_t a0 = tf32(sA[(r0 + g) * LAQ + k0 + t]), a1 = tf32(sA[(r0 + g + 8) * LAQ + k0 + t]);
-    const uint32_t a2 = tf32(sA[(r0 + g) * LAQ + k0 + t + 4]), a3 = tf32(sA[(r0 + g + 8) * LAQ + k0 + t + 4]);
+    const uint32_t a0 = tf32h(sA[(r0 + g) * LAQ + k0 + t]), a1 = tf32h(sA[(r0 + g + 8) * LAQ + k0 + t]);
+    const uint32_t a2 = tf32h(sA[(r0 + g) * LAQ + k0 + t + 4]), a3 = tf32h(sA[(r0 + g + 8) * LAQ + k0 + t + 4]);
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt)
-      mma_tf32(acc[nt], a0, a1, a2, a3, tf32(sV[(k0 + t) * LBS + 8 * nt + g]),
-               tf32(sV[(k0 + t + 4) * LBS + 8 * nt + g]));
+      mma_tf32(acc[nt], a0, a1, a2, a3, tf32h(sV[(k0 + t) * LBS + 8 * nt + g]),
+               tf32h(sV[(k0 + t + 4) * LBS + 8 * nt + g]));
   }
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt)
