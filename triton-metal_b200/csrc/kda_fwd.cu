@@ -43,13 +43,16 @@ constexpr size_t kWsGl = kWsAq + (size_t)C * C;
 constexpr size_t kWsVp = kWsGl + DK;                  // V' = U - W S (state pass -> output)
 constexpr size_t kWsS = kWsVp + (size_t)C * DV;       // state entering the chunk
 constexpr size_t kWsBlock = kWsS + (size_t)DK * DV;
-// Qg, A_qk, V' and S_c feed only the output kernel's tf32 MMAs, whose 10-bit
-// mantissa fp16 matches (all four are O(1)): they are stored as fp16 in the
-// first half of their fp32-sized regions, halving the output pass's traffic.
+// W, U, Kr (state pass) and Qg, A_qk, V', S_c (output pass) feed only tf32
+// MMAs, whose 10-bit mantissa fp16 matches, and are O(1): they are stored as
+// fp16 in the first half of their fp32-sized regions, halving the workspace
+// traffic.  The state itself is carried in fp32 registers.
 __device__ __forceinline__ __half* ws_h(float* blk, size_t off) { return reinterpret_cast<__half*>(blk + off); }
 __device__ __forceinline__ const __half* ws_h(const float* blk, size_t off) {
   return reinterpret_cast<const __half*>(blk + off);
 }
+__device__ __forceinline__ uint32_t tf32(float x);
+__device__ __forceinline__ uint32_t tf32h(__half x) { return tf32(__half2float(x)); }  // exact
 
 template <typename T>
 __device__ __forceinline__ float ld(const T* p) {
@@ -275,9 +278,12 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
         *reinterpret_cast<uint2*>(ws_h(blk, kWsQg) + t * DK + d) =
             make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
       }
-      *reinterpret_cast<float4*>(blk + kWsKr + t * DK + d) =
-          make_float4(kk.x * __expf(gl.x - gi.x), kk.y * __expf(gl.y - gi.y), kk.z * __expf(gl.z - gi.z),
-                      kk.w * __expf(gl.w - gi.w));
+      {
+        __half2 lo = __floats2half2_rn(kk.x * __expf(gl.x - gi.x), kk.y * __expf(gl.y - gi.y));
+        __half2 hi = __floats2half2_rn(kk.z * __expf(gl.z - gi.z), kk.w * __expf(gl.w - gi.w));
+        *reinterpret_cast<uint2*>(ws_h(blk, kWsKr) + t * DK + d) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+      }
       *reinterpret_cast<float4*>(sQ + t * LD + d) =
           make_float4(bt * kk.x * eg.x, bt * kk.y * eg.y, bt * kk.z * eg.z, bt * kk.w * eg.w);
       vv.x *= bt;
@@ -360,10 +366,10 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
     for (int n = 0; n < 8; ++n) {
       const int col = c0 + 8 * n + 2 * tq;
       const int ra = r0 + gq, rb = r0 + gq + 8;
-      *reinterpret_cast<float2*>(blk + kWsW + ra * DK + col) = make_float2(w[n][0], w[n][1]);
-      *reinterpret_cast<float2*>(blk + kWsW + rb * DK + col) = make_float2(w[n][2], w[n][3]);
-      *reinterpret_cast<float2*>(blk + kWsU + ra * DV + col) = make_float2(u[n][0], u[n][1]);
-      *reinterpret_cast<float2*>(blk + kWsU + rb * DV + col) = make_float2(u[n][2], u[n][3]);
+      *reinterpret_cast<__half2*>(ws_h(blk, kWsW) + ra * DK + col) = __floats2half2_rn(w[n][0], w[n][1]);
+      *reinterpret_cast<__half2*>(ws_h(blk, kWsW) + rb * DK + col) = __floats2half2_rn(w[n][2], w[n][3]);
+      *reinterpret_cast<__half2*>(ws_h(blk, kWsU) + ra * DV + col) = __floats2half2_rn(u[n][0], u[n][1]);
+      *reinterpret_cast<__half2*>(ws_h(blk, kWsU) + rb * DV + col) = __floats2half2_rn(u[n][2], u[n][3]);
     }
   }
 }
@@ -378,43 +384,43 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
 // ---------------------------------------------------------------------------
 constexpr int SV = 32;        // state columns per CTA
 constexpr int kB2Threads = 128;
-constexpr int LW = DK + 4;    // sW row stride: A-fragment reads (row g, col t) conflict-free
-constexpr int LKR = DK + 8;   // sKr row stride: transposed A reads (row t, col g) conflict-free
-constexpr int LB = SV + 8;    // B-operand tiles (row t, col g) conflict-free
-constexpr int kB2Stage = C * LW + C * LKR + C * LB;  // floats per stage
-constexpr int kB2S = 2 * kB2Stage;
-constexpr int kB2Vp = kB2S + DK * LB;
-constexpr int kB2Floats = kB2Vp + C * LB;
-constexpr size_t kB2Smem = (size_t)kB2Floats * 4;
+constexpr int LW = DK + 8;    // sW row stride (halves): A-fragment reads (row g, col t), word stride 68
+constexpr int LKR = DK + 8;   // sKr row stride (halves): transposed A reads (row t, col g)
+constexpr int LU = SV + 8;    // sU row stride (halves)
+constexpr int LB = SV + 8;    // fp32 B-operand tiles sS / sVp (row t, col g) conflict-free
+constexpr int kB2StageBytes = (C * LW + C * LKR + C * LU) * 2;  // fp16 W, Kr, U slice
+constexpr int kB2SBytes = 2 * kB2StageBytes;                    // fp32 state tile after the two stages
+constexpr int kB2VpBytes = kB2SBytes + DK * LB * 4;
+constexpr size_t kB2Smem = (size_t)kB2VpBytes + C * LB * 4;
 
-__device__ __forceinline__ void b2_load_stage(float* st, const float* blk, int v0, int tid) {
-  float* sW = st;
-  float* sKr = sW + C * LW;
-  float* sU = sKr + C * LKR;
-  for (int e = tid; e < C * DK / 4; e += kB2Threads) {
-    const int r = e / (DK / 4), c4 = e % (DK / 4);
-    cp_async16(sW + r * LW + 4 * c4, blk + kWsW + r * DK + 4 * c4);
-    cp_async16(sKr + r * LKR + 4 * c4, blk + kWsKr + r * DK + 4 * c4);
+__device__ __forceinline__ void b2_load_stage(unsigned char* st, const float* blk, int v0, int tid) {
+  __half* sW = reinterpret_cast<__half*>(st);
+  __half* sKr = sW + C * LW;
+  __half* sU = sKr + C * LKR;
+  for (int e = tid; e < C * DK / 8; e += kB2Threads) {
+    const int r = e / (DK / 8), c8 = e % (DK / 8);
+    cp_async16(sW + r * LW + 8 * c8, ws_h(blk, kWsW) + r * DK + 8 * c8);
+    cp_async16(sKr + r * LKR + 8 * c8, ws_h(blk, kWsKr) + r * DK + 8 * c8);
   }
-  for (int e = tid; e < C * SV / 4; e += kB2Threads) {
-    const int r = e / (SV / 4), c4 = e % (SV / 4);
-    cp_async16(sU + r * LB + 4 * c4, blk + kWsU + r * DV + v0 + 4 * c4);
+  for (int e = tid; e < C * SV / 8; e += kB2Threads) {
+    const int r = e / (SV / 8), c8 = e % (SV / 8);
+    cp_async16(sU + r * LU + 8 * c8, ws_h(blk, kWsU) + r * DV + v0 + 8 * c8);
   }
 }
 
 __global__ void __launch_bounds__(kB2Threads, 1)
 kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ s_out, int B, int Tlen,
                  int H) {
-  extern __shared__ __align__(16) float sm[];
-  float* sS = sm + kB2S;
-  float* sVp = sm + kB2Vp;
+  extern __shared__ __align__(16) unsigned char smb[];
+  float* sS = reinterpret_cast<float*>(smb + kB2SBytes);
+  float* sVp = reinterpret_cast<float*>(smb + kB2VpBytes);
   const int nc = Tlen / C;
   const int v0 = blockIdx.x * SV, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   float* head = ws + ((size_t)b * H + h) * nc * kWsBlock;
 
-  b2_load_stage(sm, head, v0, tid);
+  b2_load_stage(smb, head, v0, tid);
   cp_async_commit();
 
   // state rows of this warp: m-tiles 2w, 2w+1 (dk rows 32w .. 32w+31), all 32 columns
@@ -433,18 +439,18 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 
   for (int c = 0; c < nc; ++c) {
     float* blk = head + (size_t)c * kWsBlock;
-    float* st = sm + (c & 1) * kB2Stage;
+    unsigned char* st = smb + (c & 1) * kB2StageBytes;
     if (c + 1 < nc) {
-      b2_load_stage(sm + ((c + 1) & 1) * kB2Stage, blk + kWsBlock, v0, tid);
+      b2_load_stage(smb + ((c + 1) & 1) * kB2StageBytes, blk + kWsBlock, v0, tid);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();  // stage c and sS visible to all
-    const float* sW = st;
-    const float* sKr = sW + C * LW;
-    const float* sU = sKr + C * LKR;
+    const __half* sW = reinterpret_cast<const __half*>(st);
+    const __half* sKr = sW + C * LW;
+    const __half* sU = sKr + C * LKR;
 
     // state entering this chunk -> workspace (read by kernel C)
 #pragma unroll
@@ -469,8 +475,8 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 #pragma unroll 4
       for (int ks = 0; ks < DK / 8; ++ks) {
         const int k0 = 8 * ks;
-        const uint32_t a0 = tf32(sW[(r0 + g) * LW + k0 + t]), a1 = tf32(sW[(r0 + g + 8) * LW + k0 + t]);
-        const uint32_t a2 = tf32(sW[(r0 + g) * LW + k0 + t + 4]), a3 = tf32(sW[(r0 + g + 8) * LW + k0 + t + 4]);
+        const uint32_t a0 = tf32h(sW[(r0 + g) * LW + k0 + t]), a1 = tf32h(sW[(r0 + g + 8) * LW + k0 + t]);
+        const uint32_t a2 = tf32h(sW[(r0 + g) * LW + k0 + t + 4]), a3 = tf32h(sW[(r0 + g + 8) * LW + k0 + t + 4]);
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
           const uint32_t b0 = tf32(sS[(k0 + t) * LB + 8 * nt + g]), b1 = tf32(sS[(k0 + t + 4) * LB + 8 * nt + g]);
@@ -482,7 +488,7 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
           const int row = r0 + g + 8 * (e >> 1), col = 8 * nt + 2 * t;
-          const float v0f = sU[row * LB + col] - p[nt][e], v1f = sU[row * LB + col + 1] - p[nt][e + 1];
+          const float v0f = __half2float(sU[row * LU + col]) - p[nt][e], v1f = __half2float(sU[row * LU + col + 1]) - p[nt][e + 1];
           sVp[row * LB + col] = v0f;
           sVp[row * LB + col + 1] = v1f;
           *reinterpret_cast<__half2*>(ws_h(blk, kWsVp) + row * DV + v0 + col) = __floats2half2_rn(v0f, v1f);
@@ -510,8 +516,8 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
           const int m0 = 32 * warp + 16 * mt;  // dk rows; A[m][k] = Kr[k][m]
-          const uint32_t a0 = tf32(sKr[(k0 + t) * LKR + m0 + g]), a1 = tf32(sKr[(k0 + t) * LKR + m0 + g + 8]);
-          const uint32_t a2 = tf32(sKr[(k0 + t + 4) * LKR + m0 + g]), a3 = tf32(sKr[(k0 + t + 4) * LKR + m0 + g + 8]);
+          const uint32_t a0 = tf32h(sKr[(k0 + t) * LKR + m0 + g]), a1 = tf32h(sKr[(k0 + t) * LKR + m0 + g + 8]);
+          const uint32_t a2 = tf32h(sKr[(k0 + t + 4) * LKR + m0 + g]), a3 = tf32h(sKr[(k0 + t + 4) * LKR + m0 + g + 8]);
 #pragma unroll
           for (int nt = 0; nt < 4; ++nt) {
             const uint32_t b0 = tf32(sVp[(k0 + t) * LB + 8 * nt + g]), b1 = tf32(sVp[(k0 + t + 4) * LB + 8 * nt + g]);
@@ -558,8 +564,6 @@ constexpr int kCS = kCA + C * LAQ;
 constexpr int kCV = kCS + DK * LBS;
 constexpr int kCHalves = kCV + C * LBS;
 constexpr size_t kCSmem = (size_t)kCHalves * 2;
-
-__device__ __forceinline__ uint32_t tf32h(__half x) { return tf32(__half2float(x)); }  // exact
 
 template <typename T>
 __global__ void __launch_bounds__(kCThreads, 2)
