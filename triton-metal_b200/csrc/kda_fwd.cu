@@ -140,16 +140,34 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
   const int64_t row0 = ((int64_t)b * Tlen + (int64_t)chunk * C) * H + h;
   float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
 
-  // ---- 1. load (4 consecutive d per thread: 8- or 16-byte loads, float4 stores) ----
-  for (int e = tid; e < C * DK / 4; e += kA2Threads) {
-    const int t = e / (DK / 4), d = 4 * (e % (DK / 4));
-    const int64_t off = (row0 + (int64_t)t * H) * DK + d;
-    const float4 kk = ld4(k + off), qq = ld4(q + off), vv = ld4(v + (row0 + (int64_t)t * H) * DV + d);
-    *reinterpret_cast<float4*>(sK + t * LD + d) = kk;
-    *reinterpret_cast<float4*>(sQ + t * LD + d) = make_float4(qq.x * scale, qq.y * scale, qq.z * scale, qq.w * scale);
-    *reinterpret_cast<float4*>(sG + t * LD + d) = *reinterpret_cast<const float4*>(g + off);
-    *reinterpret_cast<float4*>(sV + t * LD + d) = vv;
+  // ---- 1. load: g by cp.async; q, k, v as 4 consecutive d per thread, every
+  // global load issued before the first shared store (latency overlapped) ----
+  constexpr int kNL = C * DK / 4 / kA2Threads;  // 8 vectors per thread per tensor
+  for (int i = 0; i < kNL; ++i) {
+    const int e = tid + i * kA2Threads, t = e / (DK / 4), d = 4 * (e % (DK / 4));
+    cp_async16(sG + t * LD + d, g + (row0 + (int64_t)t * H) * DK + d);
   }
+  cp_async_commit();
+  {
+    float4 kk[kNL], qq[kNL], vv[kNL];
+#pragma unroll
+    for (int i = 0; i < kNL; ++i) {
+      const int e = tid + i * kA2Threads, t = e / (DK / 4), d = 4 * (e % (DK / 4));
+      const int64_t off = (row0 + (int64_t)t * H) * DK + d;
+      kk[i] = ld4(k + off);
+      qq[i] = ld4(q + off);
+      vv[i] = ld4(v + (row0 + (int64_t)t * H) * DV + d);
+    }
+#pragma unroll
+    for (int i = 0; i < kNL; ++i) {
+      const int e = tid + i * kA2Threads, t = e / (DK / 4), d = 4 * (e % (DK / 4));
+      *reinterpret_cast<float4*>(sK + t * LD + d) = kk[i];
+      *reinterpret_cast<float4*>(sQ + t * LD + d) =
+          make_float4(qq[i].x * scale, qq[i].y * scale, qq[i].z * scale, qq[i].w * scale);
+      *reinterpret_cast<float4*>(sV + t * LD + d) = vv[i];
+    }
+  }
+  cp_async_wait<0>();
   if (tid < C) sBeta[tid] = ld(beta + row0 + (int64_t)tid * H);
   for (int e = tid; e < C * LT; e += kA2Threads) {
     sA[e] = 0.f;
@@ -226,8 +244,10 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
         }
     }
   }
-  // ---- 2b. off-diagonal 16 x 16 blocks on tensor cores: 12 (I, n-tile) tasks ----
-  for (int task = warp; task < 12; task += 8) {
+  // ---- 2b. off-diagonal 16 x 16 blocks on tensor cores: 12 (I, n-tile) tasks,
+  // run by warps 5-7 (4 each) while warps 0-4 do the diagonal blocks above
+  // (disjoint outputs, shared read-only inputs) ----
+  for (int task = warp - 5; warp >= 5 && task < 12; task += 3) {
     const int I = task < 2 ? 1 : (task < 6 ? 2 : 3);
     const int nt = task - (I == 1 ? 0 : (I == 2 ? 2 : 6));  // n-tile of 8 columns j in [0, 16 I)
     const int r = 16 * I;
