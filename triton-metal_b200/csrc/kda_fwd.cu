@@ -117,7 +117,7 @@ constexpr int kA2T = kA2Aq + C * LT;
 constexpr int kA2Beta = kA2T + C * LT;
 constexpr int kA2Floats = kA2Beta + C;
 constexpr size_t kA2Smem = (size_t)kA2Floats * 4;
-constexpr int kA2Threads = 256;
+constexpr int kA2Threads = 512;  // 16 warps: one CTA per SM (shared memory), every phase split finer
 
 template <typename T>
 __global__ void __launch_bounds__(kA2Threads, 1)
@@ -142,7 +142,7 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
 
   // ---- 1. load: g by cp.async; q, k, v as 4 consecutive d per thread, every
   // global load issued before the first shared store (latency overlapped) ----
-  constexpr int kNL = C * DK / 4 / kA2Threads;  // 8 vectors per thread per tensor
+  constexpr int kNL = C * DK / 4 / kA2Threads;  // vectors per thread per tensor
   for (int i = 0; i < kNL; ++i) {
     const int e = tid + i * kA2Threads, t = e / (DK / 4), d = 4 * (e % (DK / 4));
     cp_async16(sG + t * LD + d, g + (row0 + (int64_t)t * H) * DK + d);
@@ -183,9 +183,10 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
   }
   __syncthreads();
 
-  // ---- 2a. diagonal 16 x 16 blocks, exact: 4 blocks x 10 lower 4x4 sub-blocks x 4 d-splits ----
-  if (tid < 160) {
-    const int task = tid >> 2, split = tid & 3;
+  // ---- 2a. diagonal 16 x 16 blocks, exact: 4 blocks x 10 lower 4x4 sub-blocks x 8 d-splits
+  // (warps 0-9) ----
+  if (tid < 320) {
+    const int task = tid >> 3, split = tid & 7;
     const int D = task / 10;
     int a = 0, rem = task % 10;
     while (rem > a) {
@@ -200,13 +201,13 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
     for (int x = 0; x < 4; ++x)
 #pragma unroll
       for (int y = 0; y < 4; ++y) akk[x][y] = aqk[x][y] = 0.f;
-    // d visits split + 4 m in an order rotated by the task's slot in the warp:
-    // the 8 tasks of a warp start on rows that are multiples of 4 apart
+    // d visits split + 8 m in an order rotated by the task's slot in the warp:
+    // the 4 tasks of a warp start on rows that are multiples of 4 apart
     // (= the same bank at row stride 136), so unrotated they would read the
     // same bank; rotated, the 32 lanes cover 32 banks at every step
-    const int rot = (tid >> 2) & 7;
-    for (int it = 0; it < DK / 4; ++it) {
-      const int d = split + 4 * ((it + rot) & (DK / 4 - 1));
+    const int rot = (tid >> 3) & 3;
+    for (int it = 0; it < DK / 8; ++it) {
+      const int d = split + 8 * ((it + rot) & (DK / 8 - 1));
       const float gr = sG[r * LD + d];
       float ki[4], qi[4], kj[4];
 #pragma unroll
@@ -230,8 +231,10 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
       for (int y = 0; y < 4; ++y) {
         akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 1);
         akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 2);
+        akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 4);
         aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 1);
         aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 2);
+        aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 4);
       }
     if (split == 0) {
 #pragma unroll
@@ -245,9 +248,9 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
     }
   }
   // ---- 2b. off-diagonal 16 x 16 blocks on tensor cores: 12 (I, n-tile) tasks,
-  // run by warps 5-7 (4 each) while warps 0-4 do the diagonal blocks above
+  // run by warps 10-15 (2 each) while warps 0-9 do the diagonal blocks above
   // (disjoint outputs, shared read-only inputs) ----
-  for (int task = warp - 5; warp >= 5 && task < 12; task += 3) {
+  for (int task = warp - 10; warp >= 10 && task < 12; task += 6) {
     const int I = task < 2 ? 1 : (task < 6 ? 2 : 3);
     const int nt = task - (I == 1 ? 0 : (I == 2 ? 2 : 6));  // n-tile of 8 columns j in [0, 16 I)
     const int r = 16 * I;
@@ -361,13 +364,13 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
     __syncthreads();
   }
 
-  // ---- 4. W = T (beta K e^G), U = T (beta V): warp -> (m-tile w%4, column half w/4) ----
+  // ---- 4. W = T (beta K e^G), U = T (beta V): warp -> (m-tile w%4, column quarter w/4) ----
   {
     const int mt = warp & 3, nh = warp >> 2;
-    const int r0 = 16 * mt, c0 = 64 * nh;
-    float w[8][4], u[8][4];
+    const int r0 = 16 * mt, c0 = 32 * nh;
+    float w[4][4], u[4][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) w[n][e] = u[n][e] = 0.f;
     const int ksteps = 2 * mt + 2;  // T is lower triangular
@@ -376,14 +379,14 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
       const uint32_t a0 = tf32(sT[(r0 + gq) * LT + k0 + tq]), a1 = tf32(sT[(r0 + gq + 8) * LT + k0 + tq]);
       const uint32_t a2 = tf32(sT[(r0 + gq) * LT + k0 + tq + 4]), a3 = tf32(sT[(r0 + gq + 8) * LT + k0 + tq + 4]);
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < 4; ++n) {
         const int col = c0 + 8 * n + gq;
         mma_tf32(w[n], a0, a1, a2, a3, tf32(sQ[(k0 + tq) * LD + col]), tf32(sQ[(k0 + tq + 4) * LD + col]));
         mma_tf32(u[n], a0, a1, a2, a3, tf32(sV[(k0 + tq) * LD + col]), tf32(sV[(k0 + tq + 4) * LD + col]));
       }
     }
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < 4; ++n) {
       const int col = c0 + 8 * n + 2 * tq;
       const int ra = r0 + gq, rb = r0 + gq + 8;
       *reinterpret_cast<__half2*>(ws_h(blk, kWsW) + ra * DK + col) = __floats2half2_rn(w[n][0], w[n][1]);
