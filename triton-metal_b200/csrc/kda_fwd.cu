@@ -399,9 +399,11 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
 
 // ---------------------------------------------------------------------------
 // Kernel B: sequential state pass, one CTA per (b, h, 32 state columns).
-// Per chunk (tf32 tensor-core MMAs, fp32 state in registers):
+// Per chunk (fp16 m16n8k16 MMAs with fp32 accumulate; the fp32 state lives in
+// registers, its fp16 operand copy S^T in shared memory):
 //   V' = U - W S          (64 x 32, K = 128)
-//   S  = e^{G_last} o S + Kr^T V'   (128 x 32, K = 64)
+//   S  = e^{G_last} o S + Kr^T V'   (128 x 32, K = 64; Kr^T by ldmatrix.trans)
+// S and V' enter the MMAs rounded to fp16, the 10-bit mantissa tf32 gave.
 // and stores V' and the state entering the chunk for kernel C.  The next
 // chunk's W, Kr and U slice stream in with cp.async while this one computes.
 // ---------------------------------------------------------------------------
@@ -410,11 +412,12 @@ constexpr int kB2Threads = 128;
 constexpr int LW = DK + 8;    // sW row stride (halves): A-fragment reads (row g, col t), word stride 68
 constexpr int LKR = DK + 8;   // sKr row stride (halves): transposed A reads (row t, col g)
 constexpr int LU = SV + 8;    // sU row stride (halves)
-constexpr int LB = SV + 8;    // fp32 B-operand tiles sS / sVp (row t, col g) conflict-free
+constexpr int LS = DK + 8;    // sSt row stride (halves): S^T, one row per state column
+constexpr int LVT = C + 8;    // sVt row stride (halves): V'^T
 constexpr int kB2StageBytes = (C * LW + C * LKR + C * LU) * 2;  // fp16 W, Kr, U slice
-constexpr int kB2SBytes = 2 * kB2StageBytes;                    // fp32 state tile after the two stages
-constexpr int kB2VpBytes = kB2SBytes + DK * LB * 4;
-constexpr size_t kB2Smem = (size_t)kB2VpBytes + C * LB * 4;
+constexpr int kB2SBytes = 2 * kB2StageBytes;                    // S^T after the two stages
+constexpr int kB2VtBytes = kB2SBytes + SV * LS * 2;
+constexpr size_t kB2Smem = (size_t)kB2VtBytes + SV * LVT * 2;
 
 __device__ __forceinline__ void b2_load_stage(unsigned char* st, const float* blk, int v0, int tid) {
   __half* sW = reinterpret_cast<__half*>(st);
@@ -431,12 +434,18 @@ __device__ __forceinline__ void b2_load_stage(unsigned char* st, const float* bl
   }
 }
 
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 __global__ void __launch_bounds__(kB2Threads, 1)
 kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ s_out, int B, int Tlen,
                  int H) {
   extern __shared__ __align__(16) unsigned char smb[];
-  float* sS = reinterpret_cast<float*>(smb + kB2SBytes);
-  float* sVp = reinterpret_cast<float*>(smb + kB2VpBytes);
+  __half* sSt = reinterpret_cast<__half*>(smb + kB2SBytes);   // S^T, fp16 operand copy
+  __half* sVt = reinterpret_cast<__half*>(smb + kB2VtBytes);  // V'^T, fp16 operand copy
   const int nc = Tlen / C;
   const int v0 = blockIdx.x * SV, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -446,7 +455,7 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
   b2_load_stage(smb, head, v0, tid);
   cp_async_commit();
 
-  // state rows of this warp: m-tiles 2w, 2w+1 (dk rows 32w .. 32w+31), all 32 columns
+  // state rows of this warp: m-tiles 2w, 2w+1 (dk rows 32w .. 32w+31), all 32 columns, fp32
   float acc[2][4][4];
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
@@ -457,7 +466,7 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
         const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
         const float v = s0 ? s0[(((size_t)b * H + h) * DK + row) * DV + v0 + col] : 0.f;
         acc[mt][nt][e] = v;
-        sS[row * LB + col] = v;
+        sSt[col * LS + row] = __float2half_rn(v);
       }
 
   for (int c = 0; c < nc; ++c) {
@@ -470,7 +479,7 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();  // stage c and sS visible to all
+    __syncthreads();  // stage c and S^T visible to all
     const __half* sW = reinterpret_cast<const __half*>(st);
     const __half* sKr = sW + C * LW;
     const __half* sU = sKr + C * LKR;
@@ -487,7 +496,7 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
               __floats2half2_rn(acc[mt][nt][e], acc[mt][nt][e + 1]);
         }
 
-    // V' = U - W S: warp w owns chunk rows 16w .. 16w+15
+    // V' = U - W S (fp16 MMAs m16n8k16, fp32 accumulate): warp w owns chunk rows 16w .. 16w+15
     {
       float p[4][4];
 #pragma unroll
@@ -495,15 +504,20 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 #pragma unroll
         for (int e = 0; e < 4; ++e) p[nt][e] = 0.f;
       const int r0 = 16 * warp;
-#pragma unroll 4
-      for (int ks = 0; ks < DK / 8; ++ks) {
-        const int k0 = 8 * ks;
-        const uint32_t a0 = tf32h(sW[(r0 + g) * LW + k0 + t]), a1 = tf32h(sW[(r0 + g + 8) * LW + k0 + t]);
-        const uint32_t a2 = tf32h(sW[(r0 + g) * LW + k0 + t + 4]), a3 = tf32h(sW[(r0 + g + 8) * LW + k0 + t + 4]);
+#pragma unroll 2
+      for (int ks = 0; ks < DK / 16; ++ks) {
+        const int k0 = 16 * ks;
+        uint32_t a[4];
+        a[0] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g) * LW + k0 + 2 * t);
+        a[1] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g + 8) * LW + k0 + 2 * t);
+        a[2] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g) * LW + k0 + 2 * t + 8);
+        a[3] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g + 8) * LW + k0 + 2 * t + 8);
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
-          const uint32_t b0 = tf32(sS[(k0 + t) * LB + 8 * nt + g]), b1 = tf32(sS[(k0 + t + 4) * LB + 8 * nt + g]);
-          mma_tf32(p[nt], a0, a1, a2, a3, b0, b1);
+          uint32_t bb[2];
+          bb[0] = *reinterpret_cast<const uint32_t*>(sSt + (8 * nt + g) * LS + k0 + 2 * t);
+          bb[1] = *reinterpret_cast<const uint32_t*>(sSt + (8 * nt + g) * LS + k0 + 2 * t + 8);
+          mma_16816<B2_F16>(p[nt], a, bb);
         }
       }
 #pragma unroll
@@ -511,15 +525,16 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
           const int row = r0 + g + 8 * (e >> 1), col = 8 * nt + 2 * t;
-          const float v0f = __half2float(sU[row * LU + col]) - p[nt][e], v1f = __half2float(sU[row * LU + col + 1]) - p[nt][e + 1];
-          sVp[row * LB + col] = v0f;
-          sVp[row * LB + col + 1] = v1f;
+          const float2 u = __half22float2(*reinterpret_cast<const __half2*>(sU + row * LU + col));
+          const float v0f = u.x - p[nt][e], v1f = u.y - p[nt][e + 1];
+          sVt[col * LVT + row] = __float2half_rn(v0f);
+          sVt[(col + 1) * LVT + row] = __float2half_rn(v1f);
           *reinterpret_cast<__half2*>(ws_h(blk, kWsVp) + row * DV + v0 + col) = __floats2half2_rn(v0f, v1f);
         }
     }
-    __syncthreads();  // V' complete; every warp finished reading sS
+    __syncthreads();  // V'^T complete; every warp finished reading S^T
 
-    // S = e^{G_last} o S + Kr^T V'
+    // S = e^{G_last} o S + Kr^T V' (A = Kr^T by ldmatrix.trans, B = V'^T rows)
     {
       const float* glp = blk + kWsGl;
 #pragma unroll
@@ -533,18 +548,21 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
           acc[mt][nt][3] *= gl1;
         }
       }
-#pragma unroll 2
-      for (int ks = 0; ks < C / 8; ++ks) {
-        const int k0 = 8 * ks;
+      const int mat = lane >> 3;
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        const int k0 = 16 * ks;
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
           const int m0 = 32 * warp + 16 * mt;  // dk rows; A[m][k] = Kr[k][m]
-          const uint32_t a0 = tf32h(sKr[(k0 + t) * LKR + m0 + g]), a1 = tf32h(sKr[(k0 + t) * LKR + m0 + g + 8]);
-          const uint32_t a2 = tf32h(sKr[(k0 + t + 4) * LKR + m0 + g]), a3 = tf32h(sKr[(k0 + t + 4) * LKR + m0 + g + 8]);
+          uint32_t a[4];
+          ldsm_x4_trans(smem_u32(sKr + (k0 + (lane & 7) + ((mat >> 1) << 3)) * LKR + m0 + ((mat & 1) << 3)), a);
 #pragma unroll
           for (int nt = 0; nt < 4; ++nt) {
-            const uint32_t b0 = tf32(sVp[(k0 + t) * LB + 8 * nt + g]), b1 = tf32(sVp[(k0 + t + 4) * LB + 8 * nt + g]);
-            mma_tf32(acc[mt][nt], a0, a1, a2, a3, b0, b1);
+            uint32_t bb[2];
+            bb[0] = *reinterpret_cast<const uint32_t*>(sVt + (8 * nt + g) * LVT + k0 + 2 * t);
+            bb[1] = *reinterpret_cast<const uint32_t*>(sVt + (8 * nt + g) * LVT + k0 + 2 * t + 8);
+            mma_16816<B2_F16>(acc[mt][nt], a, bb);
           }
         }
       }
@@ -555,10 +573,10 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
-            sS[row * LB + col] = acc[mt][nt][e];
+            sSt[col * LS + row] = __float2half_rn(acc[mt][nt][e]);
           }
     }
-    __syncthreads();  // new S visible; stage c may be overwritten by the next prefetch
+    __syncthreads();  // new S^T visible; stage c may be overwritten by the next prefetch
   }
   if (s_out) {
 #pragma unroll
