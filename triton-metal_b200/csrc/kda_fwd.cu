@@ -593,7 +593,7 @@ kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __
 
 // ---------------------------------------------------------------------------
 // Kernel C: outputs, one CTA per (b, h, chunk), fully parallel:
-//   O = (scale Q o e^G) S_c + A_qk V'     (64 x 128; tf32 MMAs)
+//   O = (scale Q o e^G) S_c + A_qk V'     (64 x 128; fp16 MMAs on the fp16 operands)
 // ---------------------------------------------------------------------------
 constexpr int kCThreads = 128;
 constexpr int LQ = DK + 8;   // halves; A reads (row g, col t): word stride 68 = 4 banks apart
@@ -642,26 +642,45 @@ kda_output_kernel(const float* __restrict__ ws, T* __restrict__ o, int B, int Tl
   for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+  // fp16 m16n8k16 MMAs: A fragments (row-major Qg, A_qk) by 32-bit loads, B
+  // fragments of the row-major [k][n] tiles (S_c, V') by ldmatrix.trans,
+  // matrices (k lo, n lo), (k hi, n lo), (k lo, n hi), (k hi, n hi)
+  const int mat = lane >> 3;
+  const int brow = (lane & 7) + ((mat & 1) << 3), bcol = (mat >> 1) << 3;
 #pragma unroll 2
-  for (int ks = 0; ks < DK / 8; ++ks) {
-    const int k0 = 8 * ks;
-    const uint32_t a0 = tf32h(sQ[(r0 + g) * LQ + k0 + t]), a1 = tf32h(sQ[(r0 + g + 8) * LQ + k0 + t]);
-    const uint32_t a2 = tf32h(sQ[(r0 + g) * LQ + k0 + t + 4]), a3 = tf32h(sQ[(r0 + g + 8) * LQ + k0 + t + 4]);
+  for (int ks = 0; ks < DK / 16; ++ks) {
+    const int k0 = 16 * ks;
+    uint32_t a[4];
+    a[0] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g) * LQ + k0 + 2 * t);
+    a[1] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g + 8) * LQ + k0 + 2 * t);
+    a[2] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g) * LQ + k0 + 2 * t + 8);
+    a[3] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g + 8) * LQ + k0 + 2 * t + 8);
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-      mma_tf32(acc[nt], a0, a1, a2, a3, tf32h(sS[(k0 + t) * LBS + 8 * nt + g]),
-               tf32h(sS[(k0 + t + 4) * LBS + 8 * nt + g]));
+    for (int np = 0; np < 8; ++np) {
+      uint32_t bf[4];
+      ldsm_x4_trans(smem_u32(sS + (k0 + brow) * LBS + 16 * np + bcol), bf);
+      const uint32_t b0[2] = {bf[0], bf[1]}, b1[2] = {bf[2], bf[3]};
+      mma_16816<B2_F16>(acc[2 * np], a, b0);
+      mma_16816<B2_F16>(acc[2 * np + 1], a, b1);
+    }
   }
   // A_qk is lower triangular: k-steps beyond this warp's last row contribute 0
-  const int ksteps = (r0 + 16) / 8;
+  const int ksteps = warp + 1;
   for (int ks = 0; ks < ksteps; ++ks) {
-    const int k0 = 8 * ks;
-    const uint32_t a0 = tf32h(sA[(r0 + g) * LAQ + k0 + t]), a1 = tf32h(sA[(r0 + g + 8) * LAQ + k0 + t]);
-    const uint32_t a2 = tf32h(sA[(r0 + g) * LAQ + k0 + t + 4]), a3 = tf32h(sA[(r0 + g + 8) * LAQ + k0 + t + 4]);
+    const int k0 = 16 * ks;
+    uint32_t a[4];
+    a[0] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g) * LAQ + k0 + 2 * t);
+    a[1] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g + 8) * LAQ + k0 + 2 * t);
+    a[2] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g) * LAQ + k0 + 2 * t + 8);
+    a[3] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g + 8) * LAQ + k0 + 2 * t + 8);
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-      mma_tf32(acc[nt], a0, a1, a2, a3, tf32h(sV[(k0 + t) * LBS + 8 * nt + g]),
-               tf32h(sV[(k0 + t + 4) * LBS + 8 * nt + g]));
+    for (int np = 0; np < 8; ++np) {
+      uint32_t bf[4];
+      ldsm_x4_trans(smem_u32(sV + (k0 + brow) * LBS + 16 * np + bcol), bf);
+      const uint32_t b0[2] = {bf[0], bf[1]}, b1[2] = {bf[2], bf[3]};
+      mma_16816<B2_F16>(acc[2 * np], a, b0);
+      mma_16816<B2_F16>(acc[2 * np + 1], a, b1);
+    }
   }
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt)
