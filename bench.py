@@ -39,7 +39,7 @@ NCU_TRAFFIC = {
     "w4a16_gemm": 148564992,       # profiles/wxa16_gemm_c2.md
     "w8a16_gemm": 183006208,       # profiles/wxa16_gemm_c2.md
     "fa_gqa": 636796160,           # profiles/fa_gqa_c3.md
-    "kda": None,                   # workspace now fp16: the committed capture (4.76 GB, fp32) no longer applies
+    "kda": 2723812096,             # profiles/kda_c4.md (whole step: intra + state + output kernels)
     "decode": 1079458448,          # profiles/decode_b32_s8192.md
 }
 
