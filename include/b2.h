@@ -143,6 +143,19 @@ B2_API int b2_flash_attn_fwd(const void* q, const void* k, const void* v, void* 
                       float scale, int causal, int dtype, void* stream);
 
 /*
+ * Causal sliding-window FlashAttention (prefill): query s attends to keys
+ * s - window + 1 .. s (window > 0; Sq == Skv).  Same tensors and strides as
+ * b2_flash_attn_fwd; the prefill form of sliding_window_attention
+ * (_msl_templates.py:3335-3431).  tcgen05 kernel for D = 128 bf16/fp16.
+ */
+B2_API int b2_flash_attn_fwd_window(const void* q, const void* k, const void* v, void* o,
+                                    int64_t B, int64_t Hq, int64_t Hkv,
+                                    int64_t Sq, int64_t Skv, int64_t D,
+                                    const int64_t* q_strides, const int64_t* k_strides,
+                                    const int64_t* v_strides, const int64_t* o_strides,
+                                    float scale, int64_t window, int dtype, void* stream);
+
+/*
  * Decode attention: one query token per head over a KV cache, split-KV.
  * Replaces kv_cache_attention, gqa_attention, batched_kv_decode,
  * paged_attention, multi_head_paged_attention and fp16_kv_attention

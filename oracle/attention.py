@@ -20,11 +20,14 @@ Restates the reference's attention math:
 import numpy as np
 
 
-def attention(q, k, v, causal=False, scale=None):
+def attention(q, k, v, causal=False, scale=None, window=0):
     """q [..., Hq, Sq, D], k/v [..., Hkv, Skv, D] -> [..., Hq, Sq, D] float64.
 
     Causal follows the reference mask: key j is visible to query i iff j <= i
     (tests/test_flash_attention.py:111-114 builds tril over an N x N square).
+    window > 0 (with causal) also hides keys j <= i - window: the key range
+    the reference's sliding_window_attention keeps for a query at position i
+    (_msl_templates.py:3335-3431, start = max(0, pos + 1 - window)).
     """
     q = np.asarray(q, dtype=np.float64)
     k = np.asarray(k, dtype=np.float64)
@@ -40,6 +43,8 @@ def attention(q, k, v, causal=False, scale=None):
     if causal:
         sq, skv = s.shape[-2], s.shape[-1]
         mask = np.tril(np.ones((sq, skv), dtype=bool))
+        if window > 0:
+            mask &= ~np.tril(np.ones((sq, skv), dtype=bool), -window)
         s = np.where(mask, s, -np.inf)
     m = np.max(s, axis=-1, keepdims=True)
     with np.errstate(invalid="ignore"):

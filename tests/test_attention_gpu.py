@@ -128,6 +128,73 @@ def test_fa_c0_config(cuda):
     np.testing.assert_allclose(o.double().cpu().numpy(), ref, rtol=1e-3, atol=1e-3)
 
 
+def _ref_window(q, k, v, window):
+    """fp32 causal sliding-window attention: key j visible to query i iff i - window < j <= i."""
+    rep = q.shape[1] // k.shape[1]
+    qf, kf, vf = q.float(), k.repeat_interleave(rep, 1).float(), v.repeat_interleave(rep, 1).float()
+    s = qf @ kf.transpose(-1, -2) / math.sqrt(q.shape[-1])
+    i = torch.arange(q.shape[2], device=q.device)[:, None]
+    j = torch.arange(k.shape[2], device=q.device)[None, :]
+    s = s.masked_fill((j > i) | (j <= i - window), float("-inf"))
+    return torch.softmax(s, -1) @ vf
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,Hq,Hkv,S,window", [(1, 2, 2, 384, 1), (1, 2, 1, 384, 64), (2, 4, 2, 1000, 128),
+                                               (1, 4, 2, 1000, 200), (1, 2, 2, 2048, 256), (1, 8, 2, 2048, 1000),
+                                               (1, 2, 1, 512, 4096), (1, 2, 2, 700, 129)])
+def test_fa_window_tcgen05(cuda, dtype, B, Hq, Hkv, S, window):
+    """Sliding-window prefill on the tcgen05 kernel (D = 128): windows below,
+    at, between and above the 128-key tile, and one wider than the sequence
+    (= plain causal)."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(S + window)
+    q = (torch.randn(B, Hq, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
+    k = (torch.randn(B, Hkv, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
+    v = (torch.randn(B, Hkv, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
+    out = bk.flash_attention(q, k, v, causal=True, window=window)
+    _close(out, _ref_window(q, k, v, window))
+
+
+def test_fa_window_large_logits(cuda):
+    """Window plus the lazy O rescale: a running max that grows by > 2^8
+    inside the window."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(5)
+    base = torch.randn(1, 4, 768, 128, generator=g)
+    base[:, :, 400:] *= 6.0
+    q = base.bfloat16().to(cuda)
+    k = (torch.randn(1, 4, 768, 128, generator=g) * 2).bfloat16().to(cuda)
+    v = torch.randn(1, 4, 768, 128, generator=g).bfloat16().to(cuda)
+    out = bk.flash_attention(q, k, v, causal=True, window=300)
+    _close(out, _ref_window(q, k, v, 300))
+
+
+@pytest.mark.parametrize("D,dtype", [(64, torch.float32), (96, torch.bfloat16), (128, torch.float32)])
+def test_fa_window_generic_vs_oracle(cuda, D, dtype):
+    """The CUDA-core kernel (D != 128 or fp32) with a window vs the float64 oracle."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(D)
+    q = torch.randn(1, 4, 300, D, generator=g).to(dtype)
+    k = torch.randn(1, 2, 300, D, generator=g).to(dtype)
+    v = torch.randn(1, 2, 300, D, generator=g).to(dtype)
+    out = bk.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=True, window=37).double().cpu()
+    ref = oatt.attention(q.double().numpy(), k.double().numpy(), v.double().numpy(), causal=True, window=37)
+    _close(out, torch.from_numpy(ref))
+
+
+def test_fa_window_tcgen05_vs_oracle(cuda):
+    """tcgen05 window path vs the float64 oracle."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(13)
+    q = (torch.randn(1, 4, 640, 128, generator=g) * 0.5).bfloat16()
+    k = (torch.randn(1, 2, 640, 128, generator=g) * 0.5).bfloat16()
+    v = (torch.randn(1, 2, 640, 128, generator=g) * 0.5).bfloat16()
+    out = bk.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=True, window=160).float().cpu()
+    ref = oatt.attention(q.double().numpy(), k.double().numpy(), v.double().numpy(), causal=True, window=160)
+    _close(out, torch.from_numpy(ref))
+
+
 def test_fa_no_bounded_wait_ran_out(cuda):
     import ctypes
     from b200kern import _lib

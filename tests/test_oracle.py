@@ -140,3 +140,22 @@ def test_kda_oracle_matches_fla(rec):
     o, S = okda.recurrent(g["q"], g["k"], g["v"], g["g"], g["beta"], initial_state=g.get("s0"))
     np.testing.assert_allclose(o, g["o"], rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(S, g["S"], rtol=1e-4, atol=1e-4)
+
+
+def test_oracle_attention_window_matches_loop():
+    """The vectorised window mask vs a per-query loop over keys
+    max(0, i + 1 - window) .. i (the decode window's start rule)."""
+    r = np.random.default_rng(7)
+    q, k, v = (r.standard_normal((1, 2, 40, 8)) for _ in range(3))
+    w = 6
+    got = oatt.attention(q, k, v, causal=True, window=w)
+    s = q @ np.swapaxes(k, -1, -2) / np.sqrt(8)
+    want = np.zeros_like(q)
+    for i in range(40):
+        js = np.arange(max(0, i + 1 - w), i + 1)
+        p = np.exp(s[..., i, js] - s[..., i, js].max(-1, keepdims=True))
+        p /= p.sum(-1, keepdims=True)
+        want[..., i, :] = np.einsum("bhj,bhjd->bhd", p, v[:, :, js, :])
+    np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12)
+    np.testing.assert_array_equal(oatt.attention(q, k, v, causal=True, window=40),
+                                  oatt.attention(q, k, v, causal=True))

@@ -32,6 +32,8 @@ SIGNATURES = {
     "b2_int4_repack_ref_to_gptq": (_i32, [_vp, _vp, _i64, _i64, _vp]),
     "b2_flash_attn_fwd": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                  _pi64, _pi64, _pi64, _pi64, _f32, _i32, _i32, _vp]),
+    "b2_flash_attn_fwd_window": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64,
+                                        _pi64, _f32, _i64, _i32, _vp]),
     "b2_decode_attn_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     "b2_decode_attn": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                               _pi64, _pi64, _vp, _i64, _vp, _f32, _i32, _i32, _vp]),

@@ -34,7 +34,11 @@ def _strides(t):
     return t, _lib.strides_arg(t.stride()[:3])
 
 
-def flash_attention(q, k, v, causal=False, scale=None, out=None):
+def flash_attention(q, k, v, causal=False, scale=None, out=None, window=0):
+    """O = softmax(scale Q K^T [causal]) V for [B, H, S, D] tensors (GQA when Hq > Hkv).
+
+    window > 0 (needs causal): query s sees keys s - window + 1 .. s only
+    (Mistral-style sliding window)."""
     for t in (q, k, v):
         if not t.is_cuda:
             raise B2ShapeError("b200kern ops take CUDA tensors (there is no CPU path)")
@@ -57,6 +61,12 @@ def flash_attention(q, k, v, causal=False, scale=None, out=None):
     if o.stride(3) != 1:
         raise B2ShapeError("out must have a contiguous last dimension")
     os_ = _lib.strides_arg(o.stride()[:3])
+    if window:
+        if not causal or window < 0:
+            raise B2ShapeError("a sliding window needs causal=True and window > 0")
+        _lib.call("b2_flash_attn_fwd_window", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                  B, Hq, Hkv, Sq, Skv, D, qs, ks, vs, os_, float(scale), int(window), _DT[q.dtype], _stream())
+        return o
     _lib.call("b2_flash_attn_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
               B, Hq, Hkv, Sq, Skv, D, qs, ks, vs, os_, float(scale), int(bool(causal)), _DT[q.dtype], _stream())
     return o

@@ -36,6 +36,7 @@ constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 struct Params {
   int B, Hq, Hkv, Sq, Skv, causal, q_tiles;
+  int window;  // > 0 (causal only): key kv visible to qpos iff qpos - window < kv <= qpos
   float scale_log2;
   __nv_bfloat16* o;
   int64_t os_b, os_h, os_s;
@@ -135,7 +136,7 @@ __device__ __forceinline__ float row_max(uint32_t tS, int kv0, int qpos, const P
       float v = __uint_as_float(sv[e]);
       if constexpr (MASK) {
         const int kv = kv0 + 32 * c + e;
-        if (kv >= p.Skv || (p.causal && kv > qpos)) v = -INFINITY;
+        if (kv >= p.Skv || (p.causal && kv > qpos) || (p.window > 0 && kv <= qpos - p.window)) v = -INFINITY;
       }
       mx = fmaxf(mx, v);
     }
@@ -161,8 +162,9 @@ __device__ __forceinline__ float exp_to_p(uint32_t tS, int kv0, int qpos, float 
       float p1 = ex2(fmaf(__uint_as_float(sv[2 * e + 1]), sc, -mref));
       if constexpr (MASK) {
         const int kv = kv0 + 32 * c + 2 * e;
-        if (kv >= p.Skv || (p.causal && kv > qpos)) p0 = 0.f;
-        if (kv + 1 >= p.Skv || (p.causal && kv + 1 > qpos)) p1 = 0.f;
+        if (kv >= p.Skv || (p.causal && kv > qpos) || (p.window > 0 && kv <= qpos - p.window)) p0 = 0.f;
+        if (kv + 1 >= p.Skv || (p.causal && kv + 1 > qpos) || (p.window > 0 && kv + 1 <= qpos - p.window))
+          p1 = 0.f;
       }
       rs0 += p0;
       rs1 += p1;
@@ -207,13 +209,18 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hkv);
   const int nkv_all = (p.Skv + BKV - 1) / BKV;
-  int q0[2], nkv[2];
+  // Tile u visits KV tiles kb[u] .. nkv[u]-1 (kb > 0 only with a sliding
+  // window); the pair shares the K/V ring over the union jb .. nkv_max-1.
+  int q0[2], nkv[2], kb[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     q0[u] = (2 * pi + u) * BQ;
     nkv[u] = (2 * pi + u < p.q_tiles) ? (p.causal ? min(nkv_all, (q0[u] + BQ - 1) / BKV + 1) : nkv_all) : 0;
+    kb[u] = p.window > 0 ? min(max(0, q0[u] - p.window + 1) / BKV, nkv[u]) : 0;
   }
   const int nkv_max = max(nkv[0], nkv[1]);
+  const int jb = kb[0];
+  auto active = [&](int u, int j) { return j >= kb[u] && j < nkv[u]; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -254,7 +261,7 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       }
       int kst = 0, vst = 0;
       uint32_t kph = 0, vph = 0;
-      for (int j = 0; j < nkv_max; ++j) {
+      for (int j = jb; j < nkv_max; ++j) {
         if (!wait_abort(&k_empty[kst], kph ^ 1, p.err, 0xB2300001u, abort_flag)) break;
         mbar_arrive_expect_tx(&k_full[kst], kTile);
         tma_load_4d(sK + kst * kTile, &tmK, 0, j * BKV, hk, b, &k_full[kst]);
@@ -285,37 +292,38 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tc::commit(&s_full[u]);
       };
       // prologue: S_u(0)
-      if (ok && nkv_max > 0) {
+      if (ok && nkv_max > jb) {
         ok = wait_abort(&k_full[kst], kph, p.err, 0xB2300004u, abort_flag);
         if (ok) {
           tc::fence_after_sync();
           for (int u = 0; u < 2; ++u)
-            if (nkv[u] > 0) issue_s(u);
+            if (active(u, jb)) issue_s(u);
           tc::commit(&k_empty[kst]);
           if (++kst == kKStages) { kst = 0; kph ^= 1; }
         }
       }
-      for (int j = 0; j < nkv_max && ok; ++j) {
+      for (int j = jb; j < nkv_max && ok; ++j) {
         if (!wait_abort(&v_full[vst], vph, p.err, 0xB2300005u, abort_flag)) {
           ok = false;
           break;
         }
-        const bool next_k = (j + 1 < nkv[0]) || (j + 1 < nkv[1]);
+        const bool next_k = active(0, j + 1) || active(1, j + 1);
         bool k_waited = false;
         for (int u = 0; u < 2 && ok; ++u) {
-          if (j >= nkv[u]) continue;
-          if (!wait_abort(&p_ready[u], j & 1, p.err, 0xB2300006u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after_sync();
+          if (active(u, j)) {
+            if (!wait_abort(&p_ready[u], (j - kb[u]) & 1, p.err, 0xB2300006u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint64_t db = tc::smem_desc(sV + vst * kTile + kk * 16 * 128, kAtom, 1024, tc::kSwizzle128B);
-            mma_f16_ts(tmem + 256 * u + 128, tmem + 256 * u + kk * 8, db, idPV, (j | kk) != 0);
+            for (int kk = 0; kk < BKV / 16; ++kk) {
+              const uint64_t db = tc::smem_desc(sV + vst * kTile + kk * 16 * 128, kAtom, 1024, tc::kSwizzle128B);
+              mma_f16_ts(tmem + 256 * u + 128, tmem + 256 * u + kk * 8, db, idPV, (j != kb[u]) || kk != 0);
+            }
+            if (j == nkv[u] - 1) tc::commit(&o_done[u]);
           }
-          if (j == nkv[u] - 1) tc::commit(&o_done[u]);
-          if (j + 1 < nkv[u]) {
+          if (active(u, j + 1)) {
             if (!k_waited) {
               if (!wait_abort(&k_full[kst], kph, p.err, 0xB2300007u, abort_flag)) {
                 ok = false;
@@ -350,14 +358,15 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t tS = tmem + 256 * u + lane_off, tO = tS + 128;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv[u] && ok; ++j) {
-      if (!wait_abort(&s_full[u], j & 1, p.err, 0xB2300009u, abort_flag)) {
+    for (int j = kb[u]; j < nkv[u] && ok; ++j) {
+      if (!wait_abort(&s_full[u], (j - kb[u]) & 1, p.err, 0xB2300009u, abort_flag)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
       const int kv0 = j * BKV;
-      const bool need_mask = (p.causal && kv0 + BKV - 1 > q0[u]) || kv0 + BKV > p.Skv;
+      const bool need_mask = (p.causal && kv0 + BKV - 1 > q0[u]) || kv0 + BKV > p.Skv ||
+                             (p.window > 0 && kv0 <= q0[u] + BQ - 1 - p.window);
       // pass 1: row max of the raw scores (scale > 0 commutes with max)
       float mx = need_mask ? row_max<true, F16>(tS, kv0, qpos, p) : row_max<false, F16>(tS, kv0, qpos, p);
       mx *= p.scale_log2;
@@ -368,7 +377,7 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         l *= alpha;
         m_used = mx;
       }
-      if (__any_sync(0xffffffffu, need) && j >= 1) {
+      if (__any_sync(0xffffffffu, need) && j > kb[u]) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -390,7 +399,7 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       if (lane == 0) mbar_arrive(&p_ready[u]);
     }
     // epilogue: O_u / l -> global (rows beyond Sq are not stored)
-    if (ok && nkv[u] > 0 && wait_abort(&o_done[u], 0, p.err, 0xB230000Au, abort_flag)) {
+    if (ok && nkv[u] > kb[u] && wait_abort(&o_done[u], 0, p.err, 0xB230000Au, abort_flag)) {
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.o + b * p.os_b + h * p.os_h + (int64_t)qpos * p.os_s;
@@ -448,6 +457,7 @@ struct GenParams {
   const void *q, *k, *v;
   void* o;
   int B, Hq, Hkv, Sq, Skv, D, causal;
+  int window;  // > 0 (causal only): keys s - window + 1 .. s (sliding window)
   float scale;
   int64_t qs[3], ks[3], vs[3], os[3];
 };
@@ -474,7 +484,8 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(const GenParams p) {
   }
   float m = -INFINITY, l = 0.f;
   const int kend = p.causal ? min(p.Skv, s + 1) : p.Skv;
-  for (int j = 0; j < kend; ++j) {
+  const int kbeg = p.window > 0 ? max(0, s - p.window + 1) : 0;
+  for (int j = kbeg; j < kend; ++j) {
     const T* kr = kb + (int64_t)j * p.ks[2];
     float dot = 0.f;
 #pragma unroll
@@ -537,10 +548,41 @@ static bool strides_ok16(const int64_t* s) { return s[0] % 8 == 0 && s[1] % 8 ==
 
 using namespace b2;
 
-extern "C" int b2_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq,
-                                 int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, const int64_t* qs,
-                                 const int64_t* ks, const int64_t* vs, const int64_t* os, float scale, int causal,
-                                 int dtype, void* stream) {
+static int launch_fa_generic(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq,
+                             int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, const int64_t* qs, const int64_t* ks,
+                             const int64_t* vs, const int64_t* os, float scale, int causal, int window, int dtype,
+                             cudaStream_t st) {
+  fa::GenParams g;
+  g.q = q;
+  g.k = k;
+  g.v = v;
+  g.o = o;
+  g.B = (int)B;
+  g.Hq = (int)Hq;
+  g.Hkv = (int)Hkv;
+  g.Sq = (int)Sq;
+  g.Skv = (int)Skv;
+  g.D = (int)D;
+  g.causal = causal;
+  g.window = window;
+  g.scale = scale;
+  for (int i = 0; i < 3; ++i) {
+    g.qs[i] = qs[i];
+    g.ks[i] = ks[i];
+    g.vs[i] = vs[i];
+    g.os[i] = os[i];
+  }
+  const int64_t rows = B * Hq * Sq;
+  const unsigned blocks = (unsigned)((rows + 3) / 4);
+  if (dtype == B2_F32) fa::fa_generic_kernel<float><<<blocks, 128, 0, st>>>(g);
+  else if (dtype == B2_BF16) fa::fa_generic_kernel<__nv_bfloat16><<<blocks, 128, 0, st>>>(g);
+  else fa::fa_generic_kernel<__half><<<blocks, 128, 0, st>>>(g);
+  return launch_status("fa_generic");
+}
+
+static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv,
+                       int64_t Sq, int64_t Skv, int64_t D, const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                       const int64_t* os, float scale, int causal, int window, int dtype, void* stream) {
   B2_CHECK_ARG(q && k && v && o && qs && ks && vs && os, B2_ERR_INVALID, "flash_attn_fwd: null pointer");
   B2_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && Sq >= 0 && Skv >= 0 && D > 0, B2_ERR_INVALID,
                "flash_attn_fwd: bad shape");
@@ -568,6 +610,7 @@ extern "C" int b2_flash_attn_fwd(const void* q, const void* k, const void* v, vo
       p.Sq = (int)Sq;
       p.Skv = (int)Skv;
       p.causal = causal;
+      p.window = window;
       p.q_tiles = (int)((Sq + fa::BQ - 1) / fa::BQ);
       p.scale_log2 = scale * fa::kLog2e;
       p.o = (__nv_bfloat16*)o;
@@ -587,29 +630,25 @@ extern "C" int b2_flash_attn_fwd(const void* q, const void* k, const void* v, vo
       return launch_status("fa_fwd");
     }
   }
-  fa::GenParams g;
-  g.q = q;
-  g.k = k;
-  g.v = v;
-  g.o = o;
-  g.B = (int)B;
-  g.Hq = (int)Hq;
-  g.Hkv = (int)Hkv;
-  g.Sq = (int)Sq;
-  g.Skv = (int)Skv;
-  g.D = (int)D;
-  g.causal = causal;
-  g.scale = scale;
-  for (int i = 0; i < 3; ++i) {
-    g.qs[i] = qs[i];
-    g.ks[i] = ks[i];
-    g.vs[i] = vs[i];
-    g.os[i] = os[i];
-  }
-  const int64_t rows = B * Hq * Sq;
-  const unsigned blocks = (unsigned)((rows + 3) / 4);
-  if (dtype == B2_F32) fa::fa_generic_kernel<float><<<blocks, 128, 0, st>>>(g);
-  else if (dtype == B2_BF16) fa::fa_generic_kernel<__nv_bfloat16><<<blocks, 128, 0, st>>>(g);
-  else fa::fa_generic_kernel<__half><<<blocks, 128, 0, st>>>(g);
-  return launch_status("fa_generic");
+  return launch_fa_generic(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, qs, ks, vs, os, scale, causal, window, dtype, st);
+}
+
+extern "C" int b2_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq,
+                                 int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, const int64_t* qs,
+                                 const int64_t* ks, const int64_t* vs, const int64_t* os, float scale, int causal,
+                                 int dtype, void* stream) {
+  return fa_fwd_impl(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, qs, ks, vs, os, scale, causal, 0, dtype, stream);
+}
+
+// Causal sliding-window FlashAttention (Mistral-style): query s attends to
+// keys s - window + 1 .. s.  The prefill counterpart of the decode window
+// (sliding_window_attention, _msl_templates.py:3335-3431).  Same dispatch as
+// b2_flash_attn_fwd: the tcgen05 kernel for D = 128 bf16/fp16 (each Q tile
+// visits only the KV tiles its window reaches), else the CUDA-core kernel.
+extern "C" int b2_flash_attn_fwd_window(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq,
+                                        int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, const int64_t* qs,
+                                        const int64_t* ks, const int64_t* vs, const int64_t* os, float scale,
+                                        int64_t window, int dtype, void* stream) {
+  B2_CHECK_ARG(window > 0 && window <= 2147483647, B2_ERR_INVALID, "flash_attn_fwd_window: window must be > 0");
+  return fa_fwd_impl(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, qs, ks, vs, os, scale, 1, (int)window, dtype, stream);
 }
