@@ -66,6 +66,35 @@ def test_w4_gemv_c1(cuda, M, dtype):
     _check(out, ref)
 
 
+@pytest.mark.parametrize("N,K,G", [(11008, 4096, 128), (4096, 4096, 64), (14336, 4096, 128), (20000, 1024, 128),
+                                   (8, 256, 128), (1000, 2048, 64), (512, 128, 128), (11008, 4096, 32),
+                                   (4096, 2048, 256)])
+def test_w4_gemv_m1_fp16(cuda, N, K, G):
+    """The M = 1 fp16 symmetric decode shape (the fast fp16 dequant): narrow
+    and wide N, slabs of 8 .. 128 columns, more CTAs than SMs, G = 32 .. 256."""
+    import b200kern as bk
+    from b200kern.synthetic import w4_inputs
+    d = w4_inputs(1, N, K, group_size=G, seed=N + G)
+    out = bk.int4_matmul(d["x"].to(cuda), d["qweight"].to(cuda), d["scales"].to(cuda), group_size=G)
+    ref = oq.int4_matmul(_np(d["x"]), d["q"].numpy(), _np(d["scales"]), None, G)
+    _check(out, ref)
+
+
+@pytest.mark.parametrize("xscale", [1e-4, 1.0, 300.0])
+def test_w4_gemv_m1_fp16_x_range(cuda, xscale):
+    """Activations from near-subnormal to large (|x| ~ 1e3): x / 16 in the
+    fast fp16 dequant and the bias correction stay within tolerance relative
+    to the output scale."""
+    import b200kern as bk
+    from b200kern.synthetic import w4_inputs
+    d = w4_inputs(1, 2048, 4096, seed=3)
+    x = (d["x"].float() * xscale).half()
+    out = bk.int4_matmul(x.to(cuda), d["qweight"].to(cuda), d["scales"].to(cuda))
+    ref = oq.int4_matmul(_np(x), d["q"].numpy(), _np(d["scales"]), None, 128)
+    mag = np.abs(ref).max()
+    np.testing.assert_allclose(_np(out) / mag, ref / mag, rtol=0, atol=2e-3)
+
+
 @pytest.mark.parametrize("G", [32, 64, 128, 256])
 def test_w4_gemv_group_sizes_and_zeros(cuda, G):
     import b200kern as bk
