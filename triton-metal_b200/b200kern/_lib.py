@@ -64,12 +64,17 @@ def load():
     return lib
 
 
+_fns = {}
+
+
 def call(name, *args):
     """Invoke an int-returning entry point and raise on a non-zero status."""
-    lib = load()
-    status = getattr(lib, name)(*args)
+    fn = _fns.get(name)
+    if fn is None:
+        fn = _fns[name] = getattr(load(), name)
+    status = fn(*args)
     if status != 0:
-        raise_for_status(status, name, lib.b2_last_error().decode())
+        raise_for_status(status, name, load().b2_last_error().decode())
     return status
 
 

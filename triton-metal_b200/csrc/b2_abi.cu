@@ -2,6 +2,7 @@
 // device error word of the bounded waits, and tensor-map encoding.
 #include "b2_common.cuh"
 #include <string.h>
+#include <mutex>
 
 namespace b2 {
 // Device-side error word: bounded waits record a non-zero code here.
@@ -53,8 +54,42 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// A tensor map encodes only the address, shape, strides, box and modes, so a
+// map built once is valid for every later call with the same arguments.  A
+// small per-thread direct-mapped cache saves the driver call (~1 us of host
+// time) on the repeated small launches of a decode loop.
+namespace {
+struct TmapKey {
+  const void* base;
+  uint64_t inner, outer, stride;
+  uint32_t box_inner, box_outer;
+  int dt, swizzle;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && inner == o.inner && outer == o.outer && stride == o.stride &&
+           box_inner == o.box_inner && box_outer == o.box_outer && dt == o.dt && swizzle == o.swizzle;
+  }
+};
+struct TmapEntry {
+  bool valid;
+  TmapKey key;
+  CUtensorMap map;
+};
+constexpr int kTmapCache = 256;
+thread_local TmapEntry t_tmap_cache[kTmapCache];
+}  // namespace
+
 bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  const TmapKey key{base, inner, outer, row_stride_bytes, box_inner, box_outer, (int)dt, (int)swizzle};
+  uint64_t h = reinterpret_cast<uintptr_t>(base) >> 4;
+  h ^= inner * 0x9E3779B97F4A7C15ull ^ outer * 0xC2B2AE3D27D4EB4Full ^ ((uint64_t)box_inner << 32 | box_outer) ^
+       ((uint64_t)dt << 8 | (uint64_t)swizzle);
+  h ^= h >> 29;
+  TmapEntry& e = t_tmap_cache[h % kTmapCache];
+  if (e.valid && e.key == key) {
+    *map = e.map;
+    return true;
+  }
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled unavailable");
@@ -71,7 +106,37 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, ui
               (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
     return false;
   }
+  e.valid = true;
+  e.key = key;
+  e.map = *map;
   return true;
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device)
+// and size instead of on every launch.
+void set_max_smem(const void* func, int bytes) {
+  struct Entry {
+    const void* func;
+    int dev, bytes;
+  };
+  static std::mutex mu;
+  static Entry done[256];
+  static int n = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n; ++i)
+      if (done[i].func == func && done[i].dev == dev && done[i].bytes >= bytes) return;
+  }
+  cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (done[i].func == func && done[i].dev == dev) {
+      if (bytes > done[i].bytes) done[i].bytes = bytes;
+      return;
+    }
+  if (n < 256) done[n++] = Entry{func, dev, bytes};
 }
 }  // namespace b2
 

@@ -127,6 +127,10 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, ui
 
 int num_sms();
 
+// cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes), cached per
+// (kernel, device): the driver call is only made when the size grows.
+void set_max_smem(const void* func, int bytes);
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

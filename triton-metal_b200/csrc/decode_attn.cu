@@ -628,7 +628,7 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
 #define B2_TC2(T, DD, PG, RP)                                                                                \
   do {                                                                                                       \
     const int sm = dec::TcCfg<DD>::kSmem;                                                                    \
-    cudaFuncSetAttribute(dec::decode_tc_kernel<T, DD, PG, RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm); \
+    set_max_smem((const void*)dec::decode_tc_kernel<T, DD, PG, RP>, sm);                                     \
     dec::decode_tc_kernel<T, DD, PG, RP><<<grid, dec::kThreads, sm, st>>>(p);                                \
   } while (0)
 #define B2_TC(T, DD)                                    \
@@ -663,12 +663,10 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
 #define B2_DEC(TQ, TKV)                                                                                     \
   do {                                                                                                      \
     if (page_size) {                                                                                        \
-      cudaFuncSetAttribute(dec::decode_split_kernel<TQ, TKV, true>,                                        \
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                         \
+      set_max_smem((const void*)dec::decode_split_kernel<TQ, TKV, true>, (int)smem);                      \
       dec::decode_split_kernel<TQ, TKV, true><<<grid, dec::kThreads, smem, st>>>(p);                       \
     } else {                                                                                                \
-      cudaFuncSetAttribute(dec::decode_split_kernel<TQ, TKV, false>,                                       \
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                         \
+      set_max_smem((const void*)dec::decode_split_kernel<TQ, TKV, false>, (int)smem);                     \
       dec::decode_split_kernel<TQ, TKV, false><<<grid, dec::kThreads, smem, st>>>(p);                      \
     }                                                                                                       \
     if (p.nsplit > 1) dec::decode_combine_kernel<TQ><<<p.B * p.Hq, 128, 0, st>>>(p);                        \

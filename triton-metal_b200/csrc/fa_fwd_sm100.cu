@@ -620,11 +620,10 @@ static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int
       p.err = err;
       dim3 grid((p.q_tiles + 1) / 2, (unsigned)Hq, (unsigned)B);
       if (f16) {
-        cudaFuncSetAttribute(fa::fa_fwd2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa::kSmem2);
+        set_max_smem((const void*)fa::fa_fwd2_kernel<true>, (int)fa::kSmem2);
         fa::fa_fwd2_kernel<true><<<grid, fa::kThreads2, fa::kSmem2, st>>>(tq, tk, tv, p);
       } else {
-        cudaFuncSetAttribute(fa::fa_fwd2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)fa::kSmem2);
+        set_max_smem((const void*)fa::fa_fwd2_kernel<false>, (int)fa::kSmem2);
         fa::fa_fwd2_kernel<false><<<grid, fa::kThreads2, fa::kSmem2, st>>>(tq, tk, tv, p);
       }
       return launch_status("fa_fwd");

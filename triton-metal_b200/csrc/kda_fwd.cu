@@ -721,12 +721,11 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
   float* ws = (float*)workspace;
   const dim3 ga((unsigned)(T / chunk), (unsigned)H, (unsigned)B);
   const dim3 gb(kda::DV / kda::SV, (unsigned)H, (unsigned)B);
-  cudaFuncSetAttribute(kda::kda_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kB2Smem);
+  set_max_smem((const void*)kda::kda_state_kernel, (int)kda::kB2Smem);
 #define B2_KDA_LAUNCH(TY)                                                                                         \
   do {                                                                                                            \
-    cudaFuncSetAttribute(kda::kda_intra_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kda::kA2Smem); \
-    cudaFuncSetAttribute(kda::kda_output_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
-                         (int)kda::kCSmem);                                                                       \
+    set_max_smem((const void*)kda::kda_intra_kernel<TY>, (int)kda::kA2Smem);                                     \
+    set_max_smem((const void*)kda::kda_output_kernel<TY>, (int)kda::kCSmem);                                      \
     kda::kda_intra_kernel<TY><<<ga, kda::kA2Threads, kda::kA2Smem, st>>>(                                         \
         (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale);        \
     kda::kda_state_kernel<<<gb, kda::kB2Threads, kda::kB2Smem, st>>>(ws, initial_state, final_state, (int)B,     \

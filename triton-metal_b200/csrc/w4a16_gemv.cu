@@ -497,7 +497,7 @@ static int launch_stream(const void* x, const void* w, void* out, const void* s,
       return B2_ERR_INVALID;
   }
   auto kern = w4_gemv_stream_kernel<DT, NT, RQ, NCH, ZEROS>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  set_max_smem((const void*)kern, (int)p.smem);
   // Programmatic dependent launch: may overlap the previous kernel of the
   // stream; the kernel itself orders every dependent access after
   // griddepcontrol.wait (a no-op when the previous kernel did not trigger).

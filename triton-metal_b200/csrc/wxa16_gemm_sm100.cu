@@ -595,7 +595,7 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   int grid = num_sms();
   if (grid > ntiles) grid = ntiles;
   auto kern = wxa16_gemm_kernel<MODE, DT, ZP>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+  set_max_smem((const void*)kern, (int)C::kSmem);
   kern<<<grid, C::kThreads, C::kSmem, st>>>(ta, tb, p);
   return launch_status("wxa16_gemm");
 }
