@@ -394,17 +394,20 @@ class W4GemvRef(W4Gemv):
 # --------------------------------------------------------------------------
 class FlashAttn:
     """B=4, Hq=32, Hkv=8, S=8192, D=128, causal, bf16; q/k/v = 0.5 N(0,1).
-    One step = one forward over the whole batch (q/k/v/o 671 MB > L2)."""
+    One step = one forward over the whole batch (q/k/v/o 671 MB > L2).
+    --window W > 0: causal sliding window (query i sees keys i-W+1 .. i);
+    FLOPs then count the visible (query, key) pairs only."""
     name = "fa_gqa"
     metric = "FlashAttention GQA prefill throughput"
     unit = "tokens/s"
     dtype = "bf16"
     bound = "tensor"
 
-    def __init__(self, rank, B=4, Hq=32, Hkv=8, S=8192, D=128, causal=True):
+    def __init__(self, rank, B=4, Hq=32, Hkv=8, S=8192, D=128, causal=True, window=0):
         import b200kern as bk
         self.bk = bk
         self.B, self.Hq, self.Hkv, self.S, self.D, self.causal = B, Hq, Hkv, S, D, causal
+        self.window = window
         g = torch.Generator().manual_seed(rank)
         self.q_host = (torch.randn(B, Hq, S, D, generator=g) * 0.5).bfloat16().pin_memory()
         self.k_host = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).bfloat16().pin_memory()
@@ -412,25 +415,32 @@ class FlashAttn:
         self.q, self.k, self.v = (t.cuda() for t in (self.q_host, self.k_host, self.v_host))
         self.o = torch.empty_like(self.q)
         self.o_host = torch.empty_like(self.q_host).pin_memory()
-        self.flops = 4.0 * B * Hq * S * S * D / (2 if causal else 1)
+        if window:
+            w = min(window, S)  # visible pairs: sum_i min(i + 1, W)
+            pairs = w * (w + 1) / 2 + (S - w) * w
+            self.flops = 4.0 * B * Hq * pairs * D
+        else:
+            self.flops = 4.0 * B * Hq * S * S * D / (2 if causal else 1)
         self.step_work = B * S          # tokens per step
         self.value_scale = 1.0
         self.roof_scale = 1e12
         self.peak_key, self.peak_unit = "bf16_tflops_sustained", "TFLOP/s"
         self.launches_per_step = 1
-        self.cfg = {"workload": f"fa_gqa B={B} Hq={Hq} Hkv={Hkv} S={S} D={D} causal={causal}",
-                    "flop_convention": "4*B*Hq*S^2*D/2 (causal half)",
+        self.cfg = {"workload": f"fa_gqa B={B} Hq={Hq} Hkv={Hkv} S={S} D={D} causal={causal}"
+                                + (f" window={window}" if window else ""),
+                    "flop_convention": "4*B*Hq*S^2*D/2 (causal half)" if not window
+                    else "4*B*Hq*D*(visible query-key pairs)",
                     "l2": "q/k/v/o 671 MB > 126 MB L2 (no flush needed)"}
 
     def step(self, stream):
-        self.bk.flash_attention(self.q, self.k, self.v, causal=self.causal, out=self.o)
+        self.bk.flash_attention(self.q, self.k, self.v, causal=self.causal, out=self.o, window=self.window)
 
     def launch(self, i, stream):
         self.step(stream)
 
     def e2e_step(self):
         q, k, v = (h.to("cuda", non_blocking=True) for h in (self.q_host, self.k_host, self.v_host))
-        self.bk.flash_attention(q, k, v, causal=self.causal, out=self.o)
+        self.bk.flash_attention(q, k, v, causal=self.causal, out=self.o, window=self.window)
         self.o_host.copy_(self.o, non_blocking=True)
         return sum(t.numel() * 2 for t in (self.q_host, self.k_host, self.v_host)), self.o.numel() * 2
 
@@ -447,6 +457,8 @@ class FlashAttn:
         if self.causal:
             kpos = torch.arange(self.S)[None, :]
             s = s.masked_fill(kpos > rows[:, None], float("-inf"))
+            if self.window:
+                s = s.masked_fill(kpos <= rows[:, None] - self.window, float("-inf"))
         return torch.softmax(s, -1) @ v
 
     def check(self):
@@ -475,6 +487,9 @@ class FlashAttn:
             s = (q * (1.0 / self.D ** 0.5)) @ k.t()
             if self.causal:
                 s = s.masked_fill(torch.ones(self.S, self.S, dtype=torch.bool).triu(1), float("-inf"))
+                if self.window:
+                    s = s.masked_fill(torch.ones(self.S, self.S, dtype=torch.bool).tril(-self.window),
+                                      float("-inf"))
             torch.softmax(s, -1).nan_to_num(0.0) @ v
             n += 1
             el = time.perf_counter() - t0
@@ -677,7 +692,7 @@ def make_workload(args, rank):
     if args.workload in ("w4a16_gemm", "w8a16_gemm", "gemm_bf16"):
         return Gemm(args.workload, rank)
     if args.workload == "fa_gqa":
-        return FlashAttn(rank)
+        return FlashAttn(rank, window=args.window)
     if args.workload == "kda":
         return KDA(rank)
     if args.workload == "decode":
@@ -807,6 +822,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="w4a16_gemv", choices=sorted(WORKLOADS))
     ap.add_argument("--m", type=int, default=1, help="GEMV rows (decode batch), 1..16")
+    ap.add_argument("--window", type=int, default=0, help="fa_gqa: causal sliding window (0 = none)")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     args = ap.parse_args()
     if args.impl == "reference":
