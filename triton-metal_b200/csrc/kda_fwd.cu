@@ -23,7 +23,7 @@
 // exp(G_i - G_r) and exp(G_r - G_j) are <= 1 off the diagonal (and the
 // diagonal blocks span at most 3 steps).
 // Kernel B (one CTA per (b, h, 32 columns of Dv)) carries the fp32 state
-// through the chunks in order on tf32 tensor cores (columns of the state are
+// through the chunks in order on fp16 tensor cores (columns of the state are
 // independent: the transition acts on the Dk side only), storing V' and each
 // chunk's entering state; kernel C (parallel over chunks) forms the outputs.
 #include "b2_common.cuh"
