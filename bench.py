@@ -392,6 +392,13 @@ class W4GemvRef(W4Gemv):
 # --------------------------------------------------------------------------
 # workload: FlashAttention GQA prefill (C3)
 # --------------------------------------------------------------------------
+def fa_visible_pairs(S, window):
+    """(query, key) pairs a causal sliding window of W keys leaves visible
+    over S positions: sum_i min(i + 1, W)."""
+    w = min(window, S)
+    return w * (w + 1) // 2 + (S - w) * w
+
+
 class FlashAttn:
     """B=4, Hq=32, Hkv=8, S=8192, D=128, causal, bf16; q/k/v = 0.5 N(0,1).
     One step = one forward over the whole batch (q/k/v/o 671 MB > L2).
@@ -416,9 +423,7 @@ class FlashAttn:
         self.o = torch.empty_like(self.q)
         self.o_host = torch.empty_like(self.q_host).pin_memory()
         if window:
-            w = min(window, S)  # visible pairs: sum_i min(i + 1, W)
-            pairs = w * (w + 1) / 2 + (S - w) * w
-            self.flops = 4.0 * B * Hq * pairs * D
+            self.flops = 4.0 * B * Hq * fa_visible_pairs(S, window) * D
         else:
             self.flops = 4.0 * B * Hq * S * S * D / (2 if causal else 1)
         self.step_work = B * S          # tokens per step

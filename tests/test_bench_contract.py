@@ -43,3 +43,13 @@ def test_traffic_figures_name_workloads(bench):
     for key, val in bench.NCU_TRAFFIC.items():
         assert key in names, key
         assert val is None or val > 0
+
+
+def test_fa_window_visible_pairs(bench):
+    # brute force over small S: key j visible to query i iff i - W < j <= i
+    for S in (1, 7, 64, 200):
+        for W in (1, 3, 64, 199, 200, 500):
+            want = sum(1 for i in range(S) for j in range(S) if i - W < j <= i)
+            assert bench.fa_visible_pairs(S, W) == want, (S, W)
+    # W >= S is plain causal (S (S + 1) / 2 pairs)
+    assert bench.fa_visible_pairs(8192, 8192) == 8192 * 8193 // 2
