@@ -127,6 +127,16 @@ B2_API int b2_int4_repack_ref_to_gptq(const void* ref_weight, void* gptq_weight,
                                int64_t N, int64_t K, void* stream);
 
 /*
+ * Host plan of the W4 decode GEMV (M <= 16) for one shape; no device work.
+ * info[6] = {grid, 8-column tiles per CTA slab, CTAs with one extra tile,
+ * ring stages, quantisation groups per TMA box, shared-memory bytes} for a
+ * GPU with `sms` SMs.  B2_ERR_UNSUPPORTED when the streaming GEMV does not
+ * take the shape (b2_int4_matmul then runs the generic kernel).
+ */
+B2_API int b2_w4_gemv_plan(int64_t M, int64_t N, int64_t K, int64_t group_size, int zeros, int sms,
+                           int64_t* info);
+
+/*
  * FlashAttention forward.  q [B, Hq, S, D], k/v [B, Hkv, S, D], o like q,
  * each with arbitrary element strides (b, h, s; the last dim contiguous).
  * GQA maps q head h to kv head h / (Hq/Hkv), the reference's head map

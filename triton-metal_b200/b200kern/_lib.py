@@ -30,6 +30,7 @@ SIGNATURES = {
     "b2_gemm_bf16": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "b2_int4_dequant": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "b2_int4_repack_ref_to_gptq": (_i32, [_vp, _vp, _i64, _i64, _vp]),
+    "b2_w4_gemv_plan": (_i32, [_i64, _i64, _i64, _i64, _i32, _i32, _pi64]),
     "b2_flash_attn_fwd": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                  _pi64, _pi64, _pi64, _pi64, _f32, _i32, _i32, _vp]),
     "b2_flash_attn_fwd_window": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64,

@@ -424,11 +424,11 @@ struct GemvPlan {
 };
 
 // Column-slab split over the SMs and shared-memory ring size for one shape.
-static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p) {
+static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p, int sms) {
   const int budget = nt == 1 ? kSmemBudgetNT1 : kSmemBudgetNT2;
   // one CTA per SM; each owns a slab of <= 128 columns (8-column granules)
   const int tiles8 = N / 8;
-  int ctas = num_sms();
+  int ctas = sms;
   if (tiles8 < ctas) ctas = tiles8;
   int base = tiles8 / ctas, rem = tiles8 % ctas;
   if (base + (rem ? 1 : 0) > kMaxColTiles) {  // very wide N: more CTAs than SMs
@@ -477,7 +477,7 @@ template <int DT, int NT, int RQ, int NCH, bool ZEROS>
 static int launch_stream(const void* x, const void* w, void* out, const void* s, const void* z, int M, int N, int K,
                          int G, cudaStream_t st) {
   GemvPlan p;
-  if (!gemv_plan(N, K, G, ZEROS, NT, &p)) return B2_ERR_UNSUPPORTED;
+  if (!gemv_plan(N, K, G, ZEROS, NT, &p, num_sms())) return B2_ERR_UNSUPPORTED;
   unsigned* err = device_error_word();
   if (!err) {
     set_error("w4_gemv: cannot resolve the device error word");
@@ -620,4 +620,27 @@ extern "C" int b2_int4_repack_ref_to_gptq(const void* ref_weight, void* gptq_wei
   w4_repack_kernel<<<(int)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
       (const uint8_t*)ref_weight, (uint32_t*)gptq_weight, N, K);
   return launch_status("w4_repack");
+}
+
+// Host plan of the streaming decode GEMV for one shape, for tests and tools
+// (no device work): info = {grid, slab tiles (8 columns) per CTA, CTAs with
+// one extra tile, ring stages, groups per TMA box, shared-memory bytes}.
+extern "C" int b2_w4_gemv_plan(int64_t M, int64_t N, int64_t K, int64_t group_size, int zeros, int sms,
+                               int64_t* info) {
+  B2_CHECK_ARG(info && sms > 0 && M > 0 && N > 0 && K > 0 && group_size > 0, B2_ERR_INVALID,
+               "w4_gemv_plan: bad arguments");
+  const int64_t spg = group_size / 32;
+  if (!(M <= 16 && N % 8 == 0 && K % group_size == 0 && group_size % 32 == 0 &&
+        (spg == 1 || spg == 2 || spg == 4 || spg == 8) && K / group_size <= 256 && N < (1ll << 31) &&
+        K < (1ll << 31)))
+    return B2_ERR_UNSUPPORTED;
+  GemvPlan p;
+  if (!gemv_plan((int)N, (int)K, (int)group_size, zeros != 0, M <= 8 ? 1 : 2, &p, sms)) return B2_ERR_UNSUPPORTED;
+  info[0] = p.grid;
+  info[1] = p.base;
+  info[2] = p.rem;
+  info[3] = p.stages;
+  info[4] = p.gps;
+  info[5] = (int64_t)p.smem;
+  return B2_OK;
 }
