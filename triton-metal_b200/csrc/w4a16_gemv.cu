@@ -168,6 +168,9 @@ __device__ __forceinline__ void pairs_f16_fast(uint32_t w, uint32_t (&d)[4]) {
   d[3] = and_or(w8, 0x00F000F0u, 0x64006400u);
 }
 
+// Shared bytes of the XS copy of x (M == 1): K / 8 rows of 16 B, 128-aligned.
+__host__ __device__ inline int gemv_xs_bytes(int K) { return (K * 2 + 127) / 128 * 128; }
+
 template <int NCH>
 constexpr int gemv_threads() { return (kStageLanes * NCH + 1) * 32; }
 
@@ -178,7 +181,10 @@ template <int NT>
 constexpr int gemv_min_blocks() { return NT == 1 ? 2 : 1; }
 
 // RQ = row quads per stage (G / 32); NT = 8-row tiles of M; NCH = column halves.
-template <int DT, int NT, int RQ, int NCH, bool ZEROS>
+// XS (M == 1): each consumer warp copies the x rows of its own groups into
+// shared memory once (cp.async, no CTA barrier) instead of re-reading them
+// from L2 in every group round.
+template <int DT, int NT, int RQ, int NCH, bool ZEROS, bool XS>
 __global__ void __launch_bounds__(gemv_threads<NCH>(), gemv_min_blocks<NT>())
 w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __restrict__ x,
                       uint16_t* __restrict__ out, int M, int N, int K, int tiles_base, int tiles_rem,
@@ -201,7 +207,8 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
   const int max_sw = (tiles_base + (tiles_rem ? 1 : 0)) * 8;
   const int sblk = ((ngroups * max_sw * 2) + 127) / 128 * 128;  // scale block bytes
   const int slot_bytes = R * max_sw * 4;
-  uint8_t* ring = smem + sblk * (ZEROS ? 2 : 1);
+  uint8_t* xsb = smem + sblk * (ZEROS ? 2 : 1);        // XS: x rows, 16 B each
+  uint8_t* ring = xsb + (XS ? gemv_xs_bytes(K) : 0);
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)stages * slot_bytes);
   uint64_t* empty = full + stages;
   uint64_t* sbar = empty + stages;
@@ -260,10 +267,23 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
   // x (and the output we overwrite) may be produced / still read by the
   // previous kernel in the stream: wait for it before touching either.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  const uint4* xs4 = reinterpret_cast<const uint4*>(xsb);
+  if constexpr (XS) {
+    // the rows of this warp's groups sid, sid + 8, ... (row r of group s is x row s * R + r)
+    const int nrow = ((ngroups - sid + kStageLanes - 1) / kStageLanes) * R;
+    for (int i = lane; i < nrow; i += 32) {
+      const int row = (sid + kStageLanes * (i / R)) * R + i % R;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(xsb + 16 * row)),
+                   "l"(x + 8 * (size_t)row)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+  }
   bool alive = mbar_wait(sbar, 0, err, 0xB2000003u);
   for (int s = sid; s < ngroups && alive; s += kStageLanes) {
     const int slot = s % stages;
-    // x fragments of this group (L2 hits), loaded before the stage wait
+    // x fragments of this group (L2 hits, or this warp's shared copy), loaded before the stage wait
     uint32_t bp[RQ][NT][4];
 #pragma unroll
     for (int rq = 0; rq < RQ; ++rq) {
@@ -272,7 +292,11 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
       for (int n = 0; n < NT; ++n) {
         const int m = g + 8 * n;
         uint4 xv = make_uint4(0, 0, 0, 0);
-        if (m < M) xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K + 8 * row));
+        if constexpr (XS) {
+          if (m < M) xv = xs4[row];
+        } else {
+          if (m < M) xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K + 8 * row));
+        }
         x_pairs(xv, bp[rq][n]);
         if constexpr (FAST) {  // x / 16 in the slots where A holds 1024 + 16 q (exact)
           asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(bp[rq][n][1]) : "r"(0x2C002C00u));
@@ -421,10 +445,11 @@ constexpr int kMaxStages = 64;
 struct GemvPlan {
   int grid, base, rem, stages, gps;
   size_t smem;
+  bool xs;  // x staged per warp in shared memory (M == 1)
 };
 
 // Column-slab split over the SMs and shared-memory ring size for one shape.
-static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p, int sms) {
+static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p, int sms, bool xs = false) {
   const int budget = nt == 1 ? kSmemBudgetNT1 : kSmemBudgetNT2;
   // one CTA per SM; each owns a slab of <= 128 columns (8-column granules)
   const int tiles8 = N / 8;
@@ -441,7 +466,7 @@ static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p, int 
   if (ngroups > 256) return false;  // TMA box dimension limit of the scale block
   const size_t sblk = ((size_t)ngroups * max_sw * 2 + 127) / 128 * 128;
   const size_t slot = (size_t)rows * max_sw * 4;
-  const size_t fixed = sblk * (zeros ? 2 : 1);
+  const size_t fixed = sblk * (zeros ? 2 : 1) + (xs ? gemv_xs_bytes(K) : 0);
   int stages = (int)((budget - fixed - 256) / (slot + 16));
   if (stages > kMaxStages) stages = kMaxStages;
   // Consumer warp w takes groups w, w + 8, ... and waits on ring slot
@@ -473,11 +498,25 @@ static bool gemv_plan(int N, int K, int G, bool zeros, int nt, GemvPlan* p, int 
   return total <= (size_t)budget;
 }
 
+// Plan used for an M-row call: with M == 1 the x copy in shared memory is
+// taken when it leaves the ring as deep as without it.
+static bool gemv_choose(int M, int N, int K, int G, bool zeros, int sms, GemvPlan* p) {
+  const int nt = M <= 8 ? 1 : 2;
+  if (!gemv_plan(N, K, G, zeros, nt, p, sms)) return false;
+  p->xs = false;
+  GemvPlan q;
+  if (M == 1 && gemv_plan(N, K, G, zeros, nt, &q, sms, true) && q.stages == p->stages) {
+    *p = q;
+    p->xs = true;
+  }
+  return true;
+}
+
 template <int DT, int NT, int RQ, int NCH, bool ZEROS>
 static int launch_stream(const void* x, const void* w, void* out, const void* s, const void* z, int M, int N, int K,
                          int G, cudaStream_t st) {
   GemvPlan p;
-  if (!gemv_plan(N, K, G, ZEROS, NT, &p, num_sms())) return B2_ERR_UNSUPPORTED;
+  if (!gemv_choose(M, N, K, G, ZEROS, num_sms(), &p)) return B2_ERR_UNSUPPORTED;
   unsigned* err = device_error_word();
   if (!err) {
     set_error("w4_gemv: cannot resolve the device error word");
@@ -496,7 +535,9 @@ static int launch_stream(const void* x, const void* w, void* out, const void* s,
         (ZEROS && !make_tmap_2d(&maps.z[i], z, sdt, N, ngroups, (uint64_t)N * 2, wdt, ngroups)))
       return B2_ERR_INVALID;
   }
-  auto kern = w4_gemv_stream_kernel<DT, NT, RQ, NCH, ZEROS>;
+  auto kern = w4_gemv_stream_kernel<DT, NT, RQ, NCH, ZEROS, false>;
+  if constexpr (NT == 1)
+    if (p.xs) kern = w4_gemv_stream_kernel<DT, NT, RQ, NCH, ZEROS, true>;
   set_max_smem((const void*)kern, (int)p.smem);
   // Programmatic dependent launch: may overlap the previous kernel of the
   // stream; the kernel itself orders every dependent access after
@@ -635,7 +676,7 @@ extern "C" int b2_w4_gemv_plan(int64_t M, int64_t N, int64_t K, int64_t group_si
         K < (1ll << 31)))
     return B2_ERR_UNSUPPORTED;
   GemvPlan p;
-  if (!gemv_plan((int)N, (int)K, (int)group_size, zeros != 0, M <= 8 ? 1 : 2, &p, sms)) return B2_ERR_UNSUPPORTED;
+  if (!gemv_choose((int)M, (int)N, (int)K, (int)group_size, zeros != 0, sms, &p)) return B2_ERR_UNSUPPORTED;
   info[0] = p.grid;
   info[1] = p.base;
   info[2] = p.rem;
