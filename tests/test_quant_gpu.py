@@ -80,6 +80,20 @@ def test_w4_gemv_m1_fp16(cuda, N, K, G):
     _check(out, ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("G", [64, 128])
+def test_w4_gemv_m1_zeros(cuda, dtype, G):
+    """M = 1 with asymmetric zeros: the x-in-shared-memory GEMV with the zero
+    block loaded beside the scales."""
+    import b200kern as bk
+    from b200kern.synthetic import w4_inputs
+    d = w4_inputs(1, 11008, 4096, group_size=G, dtype=dtype, seed=G + 1, zeros=True)
+    out = bk.int4_matmul(d["x"].to(cuda), d["qweight"].to(cuda), d["scales"].to(cuda), d["zeros"].to(cuda),
+                         group_size=G)
+    ref = oq.int4_matmul(_np(d["x"]), d["q"].numpy(), _np(d["scales"]), _np(d["zeros"]), G)
+    _check(out, ref)
+
+
 @pytest.mark.parametrize("xscale", [1e-4, 1.0, 300.0])
 def test_w4_gemv_m1_fp16_x_range(cuda, xscale):
     """Activations from near-subnormal to large (|x| ~ 1e3): x / 16 in the
