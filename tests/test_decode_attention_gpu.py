@@ -106,6 +106,31 @@ def test_decode_paged_random_tables(cuda):
     _close(out.double().cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_decode_paged_full_and_overlong(cuda, dtype):
+    """Sequences that fill every page of their table row exactly, and one whose
+    seq_len claims more keys than its pages hold: that one is clamped to the
+    table's capacity (max_pages * page_size keys), never read past its row."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(21)
+    B, Hq, Hkv, D, ps, max_pages = 3, 8, 2, 128, 16, 6
+    cap = ps * max_pages
+    n_phys = B * max_pages + 2
+    kp = torch.randn(n_phys, ps, Hkv, D, generator=g).to(dtype)
+    vp = torch.randn(n_phys, ps, Hkv, D, generator=g).to(dtype)
+    table = torch.randperm(n_phys, generator=g)[:B * max_pages].reshape(B, max_pages).to(torch.int32)
+    lens = torch.tensor([cap, cap, cap + 50], dtype=torch.int32)
+    q = torch.randn(B, Hq, D, generator=g).to(dtype)
+    out = bk.decode_attention(q.to(cuda), kp.to(cuda), vp.to(cuda), lens.to(cuda), page_table=table.to(cuda))
+    kc = np.zeros((B, Hkv, cap, D))
+    vc = np.zeros_like(kc)
+    for b in range(B):
+        kc[b] = oatt.gather_pages(kp.double().numpy(), table[b].numpy(), cap).transpose(1, 0, 2)
+        vc[b] = oatt.gather_pages(vp.double().numpy(), table[b].numpy(), cap).transpose(1, 0, 2)
+    ref = oatt.decode(q.double().numpy(), kc, vc, np.minimum(lens.numpy(), cap))
+    _close(out.double().cpu().numpy(), ref)
+
+
 def test_gqa_decode_matches_flash_attention(cuda):
     """Decode of the last position == the last row of causal prefill attention."""
     import b200kern as bk

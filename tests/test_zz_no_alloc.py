@@ -22,20 +22,23 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2
 
 
-def _inputs(cuda, B, T, H, seed):
+_DT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+
+
+def _inputs(cuda, B, T, H, seed, dtype=torch.bfloat16):
     q, k, v, g, beta = okda.make_inputs(B, T, H, 128, seed=seed)
-    bf = lambda a: torch.tensor(a, dtype=torch.bfloat16, device=cuda).contiguous()
-    return bf(q), bf(k), bf(v), torch.tensor(g, dtype=torch.float32, device=cuda).contiguous(), bf(beta)
+    cv = lambda a: torch.tensor(a, dtype=dtype, device=cuda).contiguous()
+    return cv(q), cv(k), cv(v), torch.tensor(g, dtype=torch.float32, device=cuda).contiguous(), cv(beta)
 
 
-def _call(lib, name, q, k, v, g, beta, o, s_out, ws=None):
+def _call(lib, name, q, k, v, g, beta, o, s_out, ws=None, s0=None):
     B, T, H, D = q.shape
     stream = torch.cuda.current_stream().cuda_stream
-    args = [q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), None,
-            o.data_ptr(), s_out.data_ptr()]
+    args = [q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(),
+            None if s0 is None else s0.data_ptr(), o.data_ptr(), s_out.data_ptr()]
     if ws is not None:
         args.append(ws.data_ptr())
-    args += [B, T, H, D, D, 64, ctypes.c_float(D ** -0.5), 1, stream]
+    args += [B, T, H, D, D, 64, ctypes.c_float(D ** -0.5), _DT[q.dtype], stream]
     return getattr(lib, name)(*args)
 
 
@@ -59,6 +62,29 @@ def test_noalloc_matches_regular_entry_point_twice(cuda):
         s = torch.full((B, H, 128, 128), float("nan"), dtype=torch.float32, device=cuda)
         st = _call(lib, "b2_kda_fwd_noalloc", q, k, v, g, beta, o, s)
         assert st == 0, lib.b2_last_error()
+        torch.cuda.synchronize()
+        _close(o, o_ref)
+        _close(s, s_ref)
+
+
+def test_noalloc_initial_state_and_fp16(cuda):
+    """A non-zero fp32 initial state and fp16 operands, right after calls that
+    left other contents in the shared device array."""
+    from b200kern import _lib
+    from b200kern.kda import workspace_size
+    lib = _lib.load()
+    B, T, H = 1, 768, 2
+    q, k, v, g, beta = _inputs(cuda, B, T, H, 11, dtype=torch.float16)
+    gen = torch.Generator().manual_seed(12)
+    s0 = (torch.randn(B, H, 128, 128, generator=gen) * 0.3).to(cuda)
+    o_ref = torch.empty_like(v)
+    s_ref = torch.empty(B, H, 128, 128, dtype=torch.float32, device=cuda)
+    ws = torch.empty(workspace_size(B, T, H), dtype=torch.uint8, device=cuda)
+    assert _call(lib, "b2_kda_fwd", q, k, v, g, beta, o_ref, s_ref, ws, s0=s0) == 0, lib.b2_last_error()
+    for _ in range(2):
+        o = torch.full_like(v, float("nan"))
+        s = torch.full((B, H, 128, 128), float("nan"), dtype=torch.float32, device=cuda)
+        assert _call(lib, "b2_kda_fwd_noalloc", q, k, v, g, beta, o, s, s0=s0) == 0, lib.b2_last_error()
         torch.cuda.synchronize()
         _close(o, o_ref)
         _close(s, s_ref)

@@ -17,13 +17,19 @@ def workspace_size(B, T, H, Dk=128, Dv=128, chunk_size=64):
     return int(_lib.load().b2_kda_workspace_size(B, T, H, Dk, Dv, chunk_size))
 
 
+def kernels_per_call():
+    """Kernels one kda_chunk_fwd call launches."""
+    return 3
+
+
 def kda_chunk_fwd(q, k, v, g, beta, scale=None, initial_state=None, output_final_state=True, chunk_size=64,
-                  out=None, workspace=None):
+                  out=None, workspace=None, final_state_out=None):
     """o[B,T,H,Dv], final state [B,H,Dk,Dv] (fp32) of the gated delta rule.
 
     q, k [B,T,H,Dk], v [B,T,H,Dv] and beta [B,T,H] share one dtype (bf16,
     fp16 or fp32); g [B,T,H,Dk] fp32 log-decay; initial_state fp32 or None.
-    workspace: optional uint8 CUDA tensor of workspace_size(...) bytes."""
+    workspace: optional uint8 CUDA tensor of workspace_size(...) bytes;
+    final_state_out: optional fp32 [B,H,Dk,Dv] tensor for the final state."""
     for t in (q, k, v, g, beta):
         if not t.is_cuda:
             raise B2ShapeError("b200kern ops take CUDA tensors (there is no CPU path)")
@@ -39,7 +45,13 @@ def kda_chunk_fwd(q, k, v, g, beta, scale=None, initial_state=None, output_final
     scale = Dk ** -0.5 if scale is None else float(scale)
     q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
     o = out if out is not None else torch.empty(B, T, H, Dv, dtype=q.dtype, device=q.device)
-    s_out = torch.empty(B, H, Dk, Dv, dtype=torch.float32, device=q.device) if output_final_state else None
+    s_out = None
+    if output_final_state:
+        s_out = final_state_out
+        if s_out is None:
+            s_out = torch.empty(B, H, Dk, Dv, dtype=torch.float32, device=q.device)
+        elif s_out.dtype != torch.float32 or tuple(s_out.shape) != (B, H, Dk, Dv) or not s_out.is_contiguous():
+            raise B2ShapeError("final_state_out must be a contiguous fp32 [B, H, Dk, Dv] tensor")
     s0 = None
     if initial_state is not None:
         s0 = initial_state.to(torch.float32).contiguous()

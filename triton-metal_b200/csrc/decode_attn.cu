@@ -47,12 +47,15 @@ struct Params {
   float scale;
   const int32_t* q_pos;  // [B] or null (seq_len - 1)
   int window;            // > 0: sliding window
+  int cap;               // keys a sequence may reach: max_seq_len (<= max_pages * page_size when paged)
   const float* rope;     // [D/2] RoPE frequencies or null
 };
 
 // Key range [lo, hi) of sequence b and its query position.
 __device__ __forceinline__ void key_range(const Params& p, int b, int& lo, int& hi, int& qp) {
-  const int len = p.seq_lens[b];
+  // seq_lens[b] beyond the caller's max_seq_len is clamped to it: the splits
+  // only cover max_seq_len keys and a paged row only max_pages pages.
+  const int len = min(p.seq_lens[b], p.cap);
   qp = p.q_pos ? p.q_pos[b] : len - 1;
   lo = 0;
   hi = len;
@@ -584,6 +587,9 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
   B2_CHECK_ARG(D <= dec::kMaxD, B2_ERR_UNSUPPORTED, "decode_attn: D=%lld > %d", (long long)D, dec::kMaxD);
   B2_CHECK_ARG(page_size == 0 || (page_table && page_size > 0 && max_pages > 0), B2_ERR_INVALID,
                "decode_attn: paged cache needs page_table, page_size, max_pages");
+  B2_CHECK_ARG(page_size == 0 || max_seq_len <= page_size * max_pages, B2_ERR_INVALID,
+               "decode_attn: max_seq_len %lld exceeds the page table's capacity %lld x %lld",
+               (long long)max_seq_len, (long long)max_pages, (long long)page_size);
   B2_CHECK_ARG((q_dtype == B2_F32 || q_dtype == B2_F16 || q_dtype == B2_BF16) &&
                    (kv_dtype == B2_F32 || kv_dtype == B2_F16 || kv_dtype == B2_BF16),
                B2_ERR_DTYPE, "decode_attn: dtypes %d / %d", q_dtype, kv_dtype);
@@ -607,6 +613,7 @@ extern "C" int b2_decode_attn(const void* q, const void* k, const void* v, void*
   p.scale = scale;
   p.q_pos = q_pos;
   p.window = (int)(window > 0 ? window : 0);
+  p.cap = (int)max_seq_len;
   p.rope = rope_freqs;
   B2_CHECK_ARG(!rope_freqs || D % 2 == 0, B2_ERR_INVALID, "decode_attn: RoPE needs an even head dim");
   // with a window every sequence has at most `window` keys: split that

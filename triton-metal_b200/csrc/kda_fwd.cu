@@ -698,8 +698,14 @@ kda_output_kernel(const float* __restrict__ ws, T* __restrict__ o, int B, int Tl
 using namespace b2;
 
 extern "C" size_t b2_kda_workspace_size(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int64_t chunk) {
+  // 0 for every shape b2_kda_fwd rejects, and for sizes that do not fit a size_t
   if (B <= 0 || T <= 0 || H <= 0 || chunk != kda::C || T % chunk) return 0;
-  return (size_t)B * H * (T / chunk) * kda::kWsBlock * sizeof(float);
+  if (Dk != kda::DK || Dv != kda::DV || B * H > 65535) return 0;
+  const size_t per = (size_t)kda::kWsBlock * sizeof(float);
+  const size_t blocks = (size_t)(B * H);
+  const size_t chunks = (size_t)(T / chunk);
+  if (chunks > SIZE_MAX / per / blocks) return 0;
+  return blocks * chunks * per;
 }
 
 extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const float* g, const void* beta,
@@ -751,7 +757,10 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
 //
 // * The first call on a device resolves the array's device address with
 //   cudaGetSymbolAddress (with that device current) and caches it; make that
-//   first call before any stream capture.
+//   first call before any stream capture.  The cache is keyed by device
+//   ordinal and assumes the runtime's primary context on that device: after
+//   cudaDeviceReset, or from a different driver context, the cached address
+//   is stale (call b2_kda_fwd with your own workspace there).
 // * Problems whose workspace exceeds kNoAllocScratchBytes are rejected with
 //   B2_ERR_INVALID (use b2_kda_fwd with a caller-provided workspace instead).
 // * Every call shares the one array, which keeps the previous call's

@@ -406,8 +406,18 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
 
-  // every stage (and the scale block) was waited for -> smem is free again
-  asm volatile("bar.sync 1, %0;" ::"n"(NCONS * 32));
+  // Every stage (and the scale block) was waited for -> smem is free again,
+  // unless a bounded wait ran out in some consumer warp: then copies may still
+  // land in the ring, so no warp reuses it and no output is written (the
+  // error word already records the timeout).  The barrier ORs the warps' flags.
+  uint32_t any_dead;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.eq.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(any_dead)
+      : "r"((uint32_t)alive), "n"(NCONS * 32)
+      : "memory");
+  if (any_dead) return;
   constexpr int CW = kMaxColTiles * 8;           // max slab width
   float* red = reinterpret_cast<float*>(smem);  // [stage lane][NT*8][CW]
   constexpr int RS = NT * 8 * CW;
