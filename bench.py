@@ -209,14 +209,14 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 def run_samples(fn, units_per_call, warmup, steps=None, budget_s=None):
     """Call fn(i) `warmup` times untimed, then `steps` times (or until
-    budget_s elapses); fn returns the units it covered, or None for
-    units_per_call.  Returns (units per second, calls, seconds)."""
+    budget_s elapses); fn returns the units it covered as a float, or
+    anything else for units_per_call.  Returns (units per second, calls, seconds)."""
     for i in range(warmup):
         fn(i)
     n, done, t0 = 0, 0.0, time.perf_counter()
     while True:
         r = fn(warmup + n)
-        done += units_per_call if r is None else r
+        done += r if isinstance(r, float) else units_per_call
         n += 1
         el = time.perf_counter() - t0
         if steps is not None and n >= steps:

@@ -39,10 +39,27 @@ def test_workloads_declare_unit_and_bound(bench):
 
 
 def test_traffic_figures_name_workloads(bench):
-    names = {getattr(cls, "name", k) for k, cls in bench.WORKLOADS.items()}
-    for key, val in bench.NCU_TRAFFIC.items():
-        assert key in names, key
-        assert val is None or val > 0
+    """Every `traffic[...]` figure in profiles/*.md names a bench workload."""
+    names = set(bench.WORKLOADS)
+    for key, val in bench.ncu_traffic().items():
+        assert key.split()[0] in names, key
+        assert val > 0
+
+
+def test_run_samples_counts_returned_units(bench):
+    calls = []
+    rate, n, el = bench.run_samples(lambda i: calls.append(i) or 2.0, None, warmup=2, steps=5)
+    assert n == 5 and len(calls) == 7 and calls[:2] == [0, 1]
+    assert rate == pytest.approx(10.0 / el)
+
+
+def test_reference_arm_config_matches_ours(bench):
+    """Both arms print config_of(workload) built from the same constructor
+    (the reference arm builds it without device tensors)."""
+    wl = bench.make_workload("fa_c0", 0, device=False)
+    assert bench.config_of(wl) == {"workload": "fa_c0 B=2 H=8 S=1024 D=64 causal=True fp32 scale=1/8"}
+    wl = bench.make_workload("w4a16_gemv", 0, 1, device=False)
+    assert bench.config_of(wl) == {"workload": "w4a16_gemv M=1 K=4096 N=11008 G=128"}
 
 
 def test_fa_window_visible_pairs(bench):

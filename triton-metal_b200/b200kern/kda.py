@@ -19,7 +19,7 @@ def workspace_size(B, T, H, Dk=128, Dv=128, chunk_size=64):
 
 def kernels_per_call():
     """Kernels one kda_chunk_fwd call launches."""
-    return 3
+    return 2
 
 
 def kda_chunk_fwd(q, k, v, g, beta, scale=None, initial_state=None, output_final_state=True, chunk_size=64,

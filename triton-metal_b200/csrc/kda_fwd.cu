@@ -22,68 +22,35 @@
 // exp(G_i - G_j) is split at r = the last row of the j block, so both
 // exp(G_i - G_r) and exp(G_r - G_j) are <= 1 off the diagonal (and the
 // diagonal blocks span at most 3 steps).
-// Kernel B (one CTA per (b, h, 32 columns of Dv)) carries the fp32 state
+// Kernel B (one CTA per (b, h, 64 columns of Dv)) carries the fp32 state
 // through the chunks in order on fp16 tensor cores (columns of the state are
-// independent: the transition acts on the Dk side only), storing V' and each
-// chunk's entering state; kernel C (parallel over chunks) forms the outputs.
+// independent: the transition acts on the Dk side only) and forms each
+// chunk's outputs in the same pass, so neither V' nor the per-chunk state
+// ever leaves the SM.
 #include "b2_common.cuh"
+#include "tc_common.cuh"
 
 namespace b2 {
 namespace kda {
 
 constexpr int C = 64, DK = 128, DV = 128;
 
-// Workspace block per (b, h, chunk), floats
+// Workspace block per (b, h, chunk), in floats: fp16 W, U, scale Q e^G and
+// K e^{G_last - G} [64][128], fp16 A_qk [64][64], fp32 e^{G_last} [128]
+// (74,240 bytes).  The fp16 tiles only feed 10-bit-mantissa MMA operands and
+// are O(1); the state itself is carried in fp32 registers.
 constexpr size_t kWsW = 0;
-constexpr size_t kWsU = kWsW + (size_t)C * DK;
-constexpr size_t kWsQg = kWsU + (size_t)C * DV;
-constexpr size_t kWsKr = kWsQg + (size_t)C * DK;
-constexpr size_t kWsAq = kWsKr + (size_t)C * DK;
-constexpr size_t kWsGl = kWsAq + (size_t)C * C;
-constexpr size_t kWsVp = kWsGl + DK;                  // V' = U - W S (state pass -> output)
-constexpr size_t kWsS = kWsVp + (size_t)C * DV;       // state entering the chunk
-constexpr size_t kWsBlock = kWsS + (size_t)DK * DV;
-// W, U, Kr (state pass) and Qg, A_qk, V', S_c (output pass) feed only tf32
-// MMAs, whose 10-bit mantissa fp16 matches, and are O(1): they are stored as
-// fp16 in the first half of their fp32-sized regions, halving the workspace
-// traffic.  The state itself is carried in fp32 registers.
+constexpr size_t kWsU = kWsW + (size_t)C * DK / 2;
+constexpr size_t kWsQg = kWsU + (size_t)C * DV / 2;
+constexpr size_t kWsKr = kWsQg + (size_t)C * DK / 2;
+constexpr size_t kWsAq = kWsKr + (size_t)C * DK / 2;
+constexpr size_t kWsGl = kWsAq + (size_t)C * C / 2;
+constexpr size_t kWsBlock = kWsGl + DK;
 __device__ __forceinline__ __half* ws_h(float* blk, size_t off) { return reinterpret_cast<__half*>(blk + off); }
 __device__ __forceinline__ const __half* ws_h(const float* blk, size_t off) {
   return reinterpret_cast<const __half*>(blk + off);
 }
-__device__ __forceinline__ uint32_t tf32(float x);
-__device__ __forceinline__ uint32_t tf32h(__half x) { return tf32(__half2float(x)); }  // exact
 
-template <typename T>
-__device__ __forceinline__ float ld(const T* p) {
-  if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float*>(p);
-  else return to_f32<T>(*p);
-}
-// 4 consecutive elements (16 bytes for fp32, 8 for 16-bit types) as floats
-template <typename T>
-__device__ __forceinline__ float4 ld4(const T* p) {
-  if constexpr (sizeof(T) == 4) {
-    return *reinterpret_cast<const float4*>(p);
-  } else {
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
-    const T* h = reinterpret_cast<const T*>(&u);
-    return make_float4(to_f32<T>(h[0]), to_f32<T>(h[1]), to_f32<T>(h[2]), to_f32<T>(h[3]));
-  }
-}
-
-// ---- tf32 warp MMA (m16n8k8), fp32 accumulate -------------------------------
-__device__ __forceinline__ uint32_t tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
@@ -92,237 +59,393 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ---------------------------------------------------------------------------
-// Kernel A: intra-chunk WY/UT transform, one CTA per (b, h, chunk), 8 warps.
-//  1. load K, scale*Q, g (cumsum -> G), V, beta
-//  2. A_kk, A_qk on 16 x 16 blocks:
-//     - off-diagonal blocks (I > J) as tf32 MMAs of bounded operands, with the
-//       first row r = 16 I of block I as exponent reference:
-//         K~_i = K_i e^{G_i - G_r} (i in I),  K^_j = K_j e^{G_r - G_j} (j < r)
-//       (both <= 1 because G is non-increasing);
-//     - diagonal blocks exactly in fp32 on CUDA cores (4 x 4 sub-blocks split
-//       at their own reference rows, 4 threads per sub-block over d).
-//  3. T = (I + A_kk)^-1 blockwise: diagonal 16 x 16 blocks by per-column
-//     forward substitution in registers, then T_IJ = -T_II sum_M A_IM T_MJ.
-//  4. W = T (beta K e^G), U = T (beta V) as tf32 MMAs.
+// Kernel A: intra-chunk WY/UT transform on the 5th-gen tensor cores, one CTA
+// per (b, h, chunk), 256 threads.  Thread (dp, I) owns the column pair
+// d = 2 dp, 2 dp + 1 of the 16 rows of block I (rows 16 I .. 16 I + 15).
+//  1. g -> G = in-chunk cumsum (block prefix + block offsets through smem).
+//  2. Every exponential is split at per-block reference rows so that each
+//     factor stays in range; with r0 = 16 I, mid = 16 I + 7 and nx = the
+//     first row of the next block (row 63 for the last block):
+//        i side (rows i of block I)      j side (rows j of block I)
+//        Loff_i  = k_i e^{G_i - G_r0}    Khd_j = k_j e^{G_nx - G_j} e^{G_mid - G_nx}
+//        Ldiag_i = Loff_i e^{G_r0 - G_mid}
+//        Khoff^(I')_j = k_j e^{G_nx - G_j} e^{G_r0(I') - G_nx}   (blocks I' > I)
+//     so A_kk[i][j] / beta_i = Loff_i . Khoff^(I(i))_j (j in an earlier block)
+//     and = Ldiag_i . Khd_j (same block); likewise A_qk with scale q for k on
+//     the i side.  Off-diagonal factors are all <= 1.  On the diagonal the
+//     factors reach e^{+-gap}, gap = max_d (G_r0 - G_nx); blocks with
+//     gap > 80 (fp32 / bf16 range) are recomputed exactly on CUDA cores.
+//  3. The bf16 operands go to shared memory in the 128-byte-swizzled K-major
+//     layout and two tcgen05.mma (M = N = 128, K = 128) produce every lower
+//     block of A_kk and A_qk in TMEM: A rows = j side (block rows 3 and 2,
+//     then 1 and 0), B rows = i side.
+//  4. T = (I + A_kk)^-1 on CUDA cores (fp32): diagonal 16 x 16 blocks by
+//     column substitution, then T_IJ = -T_II sum_M A_IM T_MJ level by level.
+//  5. W^T = (beta K e^G)^T T^T and U^T = (beta V)^T T^T as two tcgen05.mma
+//     (M = 128 = Dk / Dv, N = 64, K = 64), bf16 operands, fp32 in TMEM.
+//  6. W, U, A_qk, scale Q e^G, K e^{G_last - G} (fp16) and e^{G_last} go to
+//     the workspace block of this chunk for kernel B.
 // ---------------------------------------------------------------------------
-constexpr int LD = DK + 8;   // 136: fragment reads (row g, col t) and (row t, col g) conflict-free
-constexpr int LT = C + 4;    // 68
-constexpr int kA2K = 0;
-constexpr int kA2Q = kA2K + C * LD;   // later: beta K e^G
-constexpr int kA2G = kA2Q + C * LD;
-constexpr int kA2V = kA2G + C * LD;   // later: beta V
-constexpr int kA2A = kA2V + C * LD;
-constexpr int kA2Aq = kA2A + C * LT;
-constexpr int kA2T = kA2Aq + C * LT;
-constexpr int kA2Beta = kA2T + C * LT;
-constexpr int kA2Floats = kA2Beta + C;
-constexpr size_t kA2Smem = (size_t)kA2Floats * 4;
-constexpr int kA2Threads = 512;  // 16 warps: one CTA per SM (shared memory), every phase split finer
+namespace prep {
+constexpr int kThreads = 256;
+constexpr int LT = C + 4;                     // fp32 row stride of A_kk / A_qk / T
+constexpr uint32_t kOpBytes = 128 * 128 * 2;  // one 128-row, K = 128 bf16 operand
+constexpr uint32_t kAA = 0;                   // j side of block rows 3, 2
+constexpr uint32_t kAB = kAA + kOpBytes;      // j side of block rows 1, 0
+constexpr uint32_t kBA = kAB + kOpBytes;      // i side of block rows 3, 2
+constexpr uint32_t kBB = kBA + kOpBytes;      // i side of block rows 1, 0
+constexpr uint32_t kAW = kBB + kOpBytes;      // (beta K e^G)^T: 128 rows (dk) x K = 64 (t)
+constexpr uint32_t kAU = kAW + 128 * 64 * 2;  // (beta V)^T
+constexpr uint32_t kSG = kAU + 128 * 64 * 2;  // G fp32 [64][128]
+constexpr uint32_t kST = kSG + C * DK * 4;    // T fp32 [64][LT]
+constexpr uint32_t kTot = kST + C * LT * 4;   // block totals of g [4][128]
+constexpr uint32_t kBeta = kTot + 4 * DK * 4; // beta [64]
+constexpr uint32_t kGap = kBeta + C * 4;      // per block max exponent gap (fp32 bits) [4]
+constexpr uint32_t kBar = kGap + 16;          // 2 mbarriers
+constexpr uint32_t kHold = kBar + 16;         // TMEM base address
+constexpr uint32_t kBytes = kHold + 16;
+constexpr size_t kSmem = kBytes + 1024;       // + alignment of the swizzled tiles
+// aliases, valid once the A_kk MMAs have completed
+constexpr uint32_t kSA = kAA;                 // A_kk fp32 [64][LT]
+constexpr uint32_t kSAq = kAA + C * LT * 4;   // A_qk fp32 [64][LT]
+constexpr uint32_t kBT = kBA;                 // T bf16, 64 rows (t) x K = 64 (j)
+constexpr uint32_t kTmemCols = 256;
+constexpr float kGapMax = 80.f;
+static_assert(kSAq + C * LT * 4 <= kBA, "A_kk / A_qk scratch must fit in the two j-side operand tiles");
+
+// byte offset of bf16 element (row, k) in a K-major 128B-swizzled operand whose
+// K-blocks (64 elements) each hold `rows` rows
+__device__ __forceinline__ uint32_t sw_off(int row, int k, int rows) {
+  return (uint32_t)((k >> 6) * rows * 128 + row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
+}
+__device__ __forceinline__ uint32_t bf2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ void st_u32(uint8_t* base, uint32_t off, uint32_t v) {
+  *reinterpret_cast<uint32_t*>(base + off) = v;
+}
+template <typename T>
+__device__ __forceinline__ float2 ld2(const T* p) {
+  if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float2*>(p);
+  else return make_float2(to_f32<T>(p[0]), to_f32<T>(p[1]));
+}
+__device__ __forceinline__ float fexp(float x) { return __expf(x); }
+}  // namespace prep
 
 template <typename T>
-__global__ void __launch_bounds__(kA2Threads, 1)
-kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                 const float* __restrict__ g, const T* __restrict__ beta, float* __restrict__ ws, int B, int Tlen,
-                 int H, float scale) {
-  extern __shared__ __align__(16) float sm[];
-  float* sK = sm + kA2K;
-  float* sQ = sm + kA2Q;
-  float* sG = sm + kA2G;
-  float* sV = sm + kA2V;
-  float* sA = sm + kA2A;
-  float* sAq = sm + kA2Aq;
-  float* sT = sm + kA2T;
-  float* sBeta = sm + kA2Beta;
+__global__ void __launch_bounds__(prep::kThreads, 1)
+kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                const float* __restrict__ g, const T* __restrict__ beta, float* __restrict__ ws, int B, int Tlen,
+                int H, float scale, unsigned* __restrict__ err) {
+  using namespace prep;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  float* sG = reinterpret_cast<float*>(sm + kSG);
+  float* sT = reinterpret_cast<float*>(sm + kST);
+  float* sTot = reinterpret_cast<float*>(sm + kTot);
+  float* sBeta = reinterpret_cast<float*>(sm + kBeta);
+  unsigned* sGap = reinterpret_cast<unsigned*>(sm + kGap);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBar);
+  uint32_t* hold = reinterpret_cast<uint32_t*>(sm + kHold);
   const int nc = Tlen / C;
   const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, tq = lane & 3;  // MMA fragment coordinates
-  const int64_t row0 = ((int64_t)b * Tlen + (int64_t)chunk * C) * H + h;
+  const int dp = tid & 63, d0 = 2 * dp, I = tid >> 6, r0 = 16 * I;
+  const int64_t row0 = ((int64_t)b * Tlen + (int64_t)chunk * C) * H + h;  // (b, t = chunk start, h)
   float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
 
-  // ---- 1. load: g by cp.async; q, k, v as 4 consecutive d per thread, every
-  // global load issued before the first shared store (latency overlapped) ----
-  constexpr int kNL = C * DK / 4 / kA2Threads;  // vectors per thread per tensor
-  for (int i = 0; i < kNL; ++i) {
-    const int e = tid + i * kA2Threads, t = e / (DK / 4), d = 4 * (e % (DK / 4));
-    cp_async16(sG + t * LD + d, g + (row0 + (int64_t)t * H) * DK + d);
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
   }
-  cp_async_commit();
+  if (tid < 4) sGap[tid] = 0u;
+  if (warp == 0) {
+    tc::tmem_alloc(hold, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  if (tid < C) sBeta[tid] = to_f32<T>(beta[row0 + (int64_t)tid * H]);
+
+  // ---- 1. G: prefix inside the block, then the preceding blocks' totals ----
+  float2 G[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) G[r] = *reinterpret_cast<const float2*>(g + (row0 + (int64_t)(r0 + r) * H) * DK + d0);
+#pragma unroll
+  for (int r = 1; r < 16; ++r) {
+    G[r].x += G[r - 1].x;
+    G[r].y += G[r - 1].y;
+  }
+  *reinterpret_cast<float2*>(sTot + I * DK + d0) = G[15];
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *hold;
   {
-    float4 kk[kNL], qq[kNL], vv[kNL];
-#pragma unroll
-    for (int i = 0; i < kNL; ++i) {
-      const int e = tid + i * kA2Threads, t = e / (DK / 4), d = 4 * (e % (DK / 4));
-      const int64_t off = (row0 + (int64_t)t * H) * DK + d;
-      kk[i] = ld4(k + off);
-      qq[i] = ld4(q + off);
-      vv[i] = ld4(v + (row0 + (int64_t)t * H) * DV + d);
+    float2 off = make_float2(0.f, 0.f);
+    for (int J = 0; J < I; ++J) {
+      const float2 tj = *reinterpret_cast<const float2*>(sTot + J * DK + d0);
+      off.x += tj.x;
+      off.y += tj.y;
     }
 #pragma unroll
-    for (int i = 0; i < kNL; ++i) {
-      const int e = tid + i * kA2Threads, t = e / (DK / 4), d = 4 * (e % (DK / 4));
-      *reinterpret_cast<float4*>(sK + t * LD + d) = kk[i];
-      *reinterpret_cast<float4*>(sQ + t * LD + d) =
-          make_float4(qq[i].x * scale, qq[i].y * scale, qq[i].z * scale, qq[i].w * scale);
-      *reinterpret_cast<float4*>(sV + t * LD + d) = vv[i];
+    for (int r = 0; r < 16; ++r) {
+      G[r].x += off.x;
+      G[r].y += off.y;
+      *reinterpret_cast<float2*>(sG + (r0 + r) * DK + d0) = G[r];
     }
   }
-  cp_async_wait<0>();
-  if (tid < C) sBeta[tid] = ld(beta + row0 + (int64_t)tid * H);
-  for (int e = tid; e < C * LT; e += kA2Threads) {
+  __syncthreads();
+
+  // ---- 2. per-column constants of this block ----
+  const float2 Gr0 = G[0], Gmid = G[7];
+  const float2 Gnx = I < 3 ? *reinterpret_cast<const float2*>(sG + (r0 + 16) * DK + d0) : G[15];
+  const float2 Gl = *reinterpret_cast<const float2*>(sG + (C - 1) * DK + d0);
+  {
+    float gap = fmaxf(Gr0.x - Gnx.x, Gr0.y - Gnx.y);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) gap = fmaxf(gap, __shfl_xor_sync(0xffffffffu, gap, o));
+    if (lane == 0) atomicMax(&sGap[I], __float_as_uint(fmaxf(gap, 0.f)));
+  }
+  const float2 cA = make_float2(fexp(Gr0.x - Gmid.x), fexp(Gr0.y - Gmid.y));
+  const float2 cB = make_float2(fexp(Gmid.x - Gnx.x), fexp(Gmid.y - Gnx.y));
+  const float2 eG0 = make_float2(fexp(Gr0.x), fexp(Gr0.y));
+  const float2 cKr = make_float2(fexp(Gl.x - Gnx.x), fexp(Gl.y - Gnx.y));
+  float2 cOff[3];  // e^{G_r0(I') - G_nx} for I' = I + 1 .. 3
+#pragma unroll
+  for (int u = 0; u < 3; ++u) {
+    const int Ip = I + 1 + u;
+    if (Ip < 4) {
+      const float2 gr = *reinterpret_cast<const float2*>(sG + 16 * Ip * DK + d0);
+      cOff[u] = make_float2(fexp(gr.x - Gnx.x), fexp(gr.y - Gnx.y));
+    } else {
+      cOff[u] = make_float2(0.f, 0.f);
+    }
+  }
+
+  // ---- 3. operands: rows of this block for the A_kk / A_qk MMAs, the W / U
+  // operands, and scale Q e^G, K e^{G_last - G} straight to the workspace ----
+  uint8_t* opA = sm + (I >= 2 ? kAA : kAB);
+  uint8_t* opB = sm + (I >= 2 ? kBA : kBB);
+  // i-side rows of this block in its B operand (block rows 3 / 1 at 0, 2 / 0 at 64)
+  const int ib = (I == 3 || I == 1) ? 0 : 64;
+  // j-side diagonal rows of this block in its A operand
+  const int jd = I == 3 ? 48 : (I == 2 ? 96 : (I == 1 ? 16 : 32));
+  __half* wsQg = ws_h(blk, kWsQg);
+  __half* wsKr = ws_h(blk, kWsKr);
+  float2 wk[16];  // beta K e^G for the W operand, this thread's rows
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    const int t = r0 + r;
+    const int64_t gi = (row0 + (int64_t)t * H) * DK + d0;
+    const float2 kk = ld2(k + gi);
+    float2 sq = ld2(q + gi);
+    sq.x *= scale;
+    sq.y *= scale;
+    const float2 e0 = make_float2(fexp(G[r].x - Gr0.x), fexp(G[r].y - Gr0.y));
+    const float2 ej = make_float2(fexp(Gnx.x - G[r].x), fexp(Gnx.y - G[r].y));
+    const float2 lo = make_float2(kk.x * e0.x, kk.y * e0.y);
+    const float2 lq = make_float2(sq.x * e0.x, sq.y * e0.y);
+    const float2 kj = make_float2(kk.x * ej.x, kk.y * ej.y);
+    // i side: Loff, Lqoff (block rows >= 1), Ldiag, Lqdiag
+    if (I >= 1) {
+      st_u32(opB, sw_off(ib + r, d0, 128), bf2(lo.x, lo.y));
+      st_u32(opB, sw_off(ib + 16 + r, d0, 128), bf2(lq.x, lq.y));
+      st_u32(opB, sw_off(ib + 32 + r, d0, 128), bf2(lo.x * cA.x, lo.y * cA.y));
+      st_u32(opB, sw_off(ib + 48 + r, d0, 128), bf2(lq.x * cA.x, lq.y * cA.y));
+    } else {
+      st_u32(opB, sw_off(64 + r, d0, 128), bf2(lo.x * cA.x, lo.y * cA.y));
+      st_u32(opB, sw_off(80 + r, d0, 128), bf2(lq.x * cA.x, lq.y * cA.y));
+    }
+    // j side: diagonal block, then every later block row I' (off-diagonal)
+    st_u32(opA, sw_off(jd + r, d0, 128), bf2(kj.x * cB.x, kj.y * cB.y));
+#pragma unroll
+    for (int u = 0; u < 3; ++u) {
+      const int Ip = I + 1 + u;
+      if (Ip >= 4) break;
+      const uint32_t v2 = bf2(kj.x * cOff[u].x, kj.y * cOff[u].y);
+      if (Ip == 3) st_u32(sm + kAA, sw_off(t, d0, 128), v2);
+      else if (Ip == 2) st_u32(sm + kAA, sw_off(64 + t, d0, 128), v2);
+      else st_u32(sm + kAB, sw_off(t, d0, 128), v2);
+    }
+    // workspace outputs of this row
+    *reinterpret_cast<__half2*>(wsQg + t * DK + d0) = __floats2half2_rn(lq.x * eG0.x, lq.y * eG0.y);
+    *reinterpret_cast<__half2*>(wsKr + t * DK + d0) = __floats2half2_rn(kj.x * cKr.x, kj.y * cKr.y);
+    const float bt = sBeta[t];
+    wk[r] = make_float2(bt * lo.x * eG0.x, bt * lo.y * eG0.y);
+  }
+  // W / U operands: rows d, K = t; this thread's 16 t of rows d0, d0 + 1 are
+  // two 16-byte chunks each
+  {
+    uint32_t p0[8], p1[8];
+#pragma unroll
+    for (int r = 0; r < 16; r += 2) {
+      p0[r / 2] = bf2(wk[r].x, wk[r + 1].x);
+      p1[r / 2] = bf2(wk[r].y, wk[r + 1].y);
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      *reinterpret_cast<uint4*>(sm + kAW + sw_off(d0, r0 + 8 * c, 128)) =
+          make_uint4(p0[4 * c], p0[4 * c + 1], p0[4 * c + 2], p0[4 * c + 3]);
+      *reinterpret_cast<uint4*>(sm + kAW + sw_off(d0 + 1, r0 + 8 * c, 128)) =
+          make_uint4(p1[4 * c], p1[4 * c + 1], p1[4 * c + 2], p1[4 * c + 3]);
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float bt = sBeta[r0 + r];
+      const float2 vv = ld2(v + (row0 + (int64_t)(r0 + r) * H) * DV + d0);
+      wk[r] = make_float2(bt * vv.x, bt * vv.y);
+    }
+#pragma unroll
+    for (int r = 0; r < 16; r += 2) {
+      p0[r / 2] = bf2(wk[r].x, wk[r + 1].x);
+      p1[r / 2] = bf2(wk[r].y, wk[r + 1].y);
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      *reinterpret_cast<uint4*>(sm + kAU + sw_off(d0, r0 + 8 * c, 128)) =
+          make_uint4(p0[4 * c], p0[4 * c + 1], p0[4 * c + 2], p0[4 * c + 3]);
+      *reinterpret_cast<uint4*>(sm + kAU + sw_off(d0 + 1, r0 + 8 * c, 128)) =
+          make_uint4(p1[4 * c], p1[4 * c + 1], p1[4 * c + 2], p1[4 * c + 3]);
+    }
+  }
+  if (tid < DK / 2) {  // e^{G_last}: block 3 holds row 63
+    // (any thread has Gl for its pair)
+    *reinterpret_cast<float2*>(blk + kWsGl + d0) = make_float2(fexp(Gl.x), fexp(Gl.y));
+  }
+  tc::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+
+  // ---- 4. A_kk / A_qk MMAs (one thread) ----
+  if (tid == 0) {
+    tc::fence_after_sync();
+    constexpr uint32_t idesc = tc::idesc_f16(128, 128, true);
+#pragma unroll
+    for (int s = 0; s < DK / 16; ++s) {
+      const uint32_t kb = (uint32_t)(s >> 2) * kOpBytes / 2, ko = 2u * (s & 3);
+      tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(sm + kAA + kb) + ko, tc::desc_kmajor_sw128(sm + kBA + kb) + ko,
+                     idesc, s != 0);
+    }
+#pragma unroll
+    for (int s = 0; s < DK / 16; ++s) {
+      const uint32_t kb = (uint32_t)(s >> 2) * kOpBytes / 2, ko = 2u * (s & 3);
+      tc::mma_f16_ss(tmem + 128, tc::desc_kmajor_sw128(sm + kAB + kb) + ko,
+                     tc::desc_kmajor_sw128(sm + kBB + kb) + ko, idesc, s != 0);
+    }
+    tc::commit(&bar[0]);
+  }
+  bool alive = mbar_wait(&bar[0], 0, err, 0xB2300001u);
+  tc::fence_after_sync();
+  // A_kk / A_qk scratch (aliases the j-side tiles the MMAs just read)
+  float* sA = reinterpret_cast<float*>(sm + kSA);
+  float* sAq = reinterpret_cast<float*>(sm + kSAq);
+  for (int e = tid; e < C * LT; e += kThreads) {
     sA[e] = 0.f;
     sAq[e] = 0.f;
   }
   __syncthreads();
-  if (tid < DK) {
-    float acc = 0.f;
-    for (int t = 0; t < C; ++t) {
-      acc += sG[t * LD + tid];
-      sG[t * LD + tid] = acc;
+
+  // ---- 5. TMEM -> A_kk (times beta_i), A_qk (lower parts only) ----
+  if (alive) {
+    const int qd = warp & 3, half = warp >> 2;
+    const int L = 32 * qd + lane;  // TMEM lane = A-operand row
+    uint32_t vals[64];
+    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+    if (half == 0) {
+      // block rows 3 (lanes 0..63) and 2 (lanes 64..111)
+      const uint32_t cbase = qd < 2 ? 0u : 64u;
+      uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals);
+      uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals + 32);
+      tc::tmem_ld_32x32b_x32(tmem + lane_off + cbase, v0);
+      tc::tmem_ld_32x32b_x32(tmem + lane_off + cbase + 32, v1);
+      tc::tmem_ld_wait();
+      const int Ib = qd < 2 ? 3 : 2;
+      const int j = qd < 2 ? L : L - 64;
+      const int ri = 16 * Ib;  // first row of the block row
+      if (j < ri) {            // off-diagonal: columns 0..15 A_kk, 16..31 A_qk
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          sA[(ri + i) * LT + j] = __uint_as_float(vals[i]) * sBeta[ri + i];
+          sAq[(ri + i) * LT + j] = __uint_as_float(vals[16 + i]);
+        }
+      } else if (j < ri + 16) {  // diagonal: columns 32..47 A_kk, 48..63 A_qk
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (j < ri + i) sA[(ri + i) * LT + j] = __uint_as_float(vals[32 + i]) * sBeta[ri + i];
+          if (j <= ri + i) sAq[(ri + i) * LT + j] = __uint_as_float(vals[48 + i]);
+        }
+      }
+    } else if (qd < 2) {
+      // block rows 1 (lanes 0..31) and 0 (lanes 32..47), TMEM columns 128..
+      uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals);
+      uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals + 32);
+      tc::tmem_ld_32x32b_x32(tmem + lane_off + 128 + (qd == 0 ? 0u : 64u), v0);
+      tc::tmem_ld_32x32b_x32(tmem + lane_off + 128 + (qd == 0 ? 32u : 96u), v1);
+      tc::tmem_ld_wait();
+      if (qd == 0) {
+        const int j = L;
+        if (j < 16) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            sA[(16 + i) * LT + j] = __uint_as_float(vals[i]) * sBeta[16 + i];
+            sAq[(16 + i) * LT + j] = __uint_as_float(vals[16 + i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (j < 16 + i) sA[(16 + i) * LT + j] = __uint_as_float(vals[32 + i]) * sBeta[16 + i];
+            if (j <= 16 + i) sAq[(16 + i) * LT + j] = __uint_as_float(vals[48 + i]);
+          }
+        }
+      } else if (L < 48) {
+        const int j = L - 32;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (j < i) sA[i * LT + j] = __uint_as_float(vals[i]) * sBeta[i];
+          if (j <= i) sAq[i * LT + j] = __uint_as_float(vals[16 + i]);
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  // diagonal blocks whose exponent gap is beyond the bf16 / fp32 range of the
+  // split factors: exact fp32 on CUDA cores (pairs j <= i of the block)
+  for (int Ib = 0; Ib < 4; ++Ib) {
+    if (__uint_as_float(sGap[Ib]) <= kGapMax) continue;
+    for (int p = tid; p < 136; p += kThreads) {
+      int i = 0, rem = p;
+      while (rem > i) {
+        rem -= i + 1;
+        ++i;
+      }
+      const int ri = 16 * Ib + i, rj = 16 * Ib + rem;
+      const T* ki = k + (row0 + (int64_t)ri * H) * DK;
+      const T* qi = q + (row0 + (int64_t)ri * H) * DK;
+      const T* kj = k + (row0 + (int64_t)rj * H) * DK;
+      float akk = 0.f, aqk = 0.f;
+      for (int d = 0; d < DK; ++d) {
+        const float e = fexp(sG[ri * DK + d] - sG[rj * DK + d]);
+        const float kjd = to_f32<T>(kj[d]) * e;
+        akk += to_f32<T>(ki[d]) * kjd;
+        aqk += to_f32<T>(qi[d]) * kjd;
+      }
+      if (rj < ri) sA[ri * LT + rj] = akk * sBeta[ri];
+      sAq[ri * LT + rj] = aqk * scale;
     }
   }
   __syncthreads();
 
-  // ---- 2a. diagonal 16 x 16 blocks, exact: 4 blocks x 10 lower 4x4 sub-blocks x 8 d-splits
-  // (warps 0-9) ----
-  if (tid < 320) {
-    const int task = tid >> 3, split = tid & 7;
-    const int D = task / 10;
-    int a = 0, rem = task % 10;
-    while (rem > a) {
-      rem -= a + 1;
-      ++a;
-    }
-    const int bsub = rem;  // sub-block (a, bsub), bsub <= a
-    const int ib = 16 * D + 4 * a, jb = 16 * D + 4 * bsub;
-    const int r = jb + 3;  // reference: last row of the j sub-block
-    float akk[4][4], aqk[4][4];
-#pragma unroll
-    for (int x = 0; x < 4; ++x)
-#pragma unroll
-      for (int y = 0; y < 4; ++y) akk[x][y] = aqk[x][y] = 0.f;
-    // d visits split + 8 m in an order rotated by the task's slot in the warp:
-    // the 4 tasks of a warp start on rows that are multiples of 4 apart
-    // (= the same bank at row stride 136), so unrotated they would read the
-    // same bank; rotated, the 32 lanes cover 32 banks at every step
-    const int rot = (tid >> 3) & 3;
-    for (int it = 0; it < DK / 8; ++it) {
-      const int d = split + 8 * ((it + rot) & (DK / 8 - 1));
-      const float gr = sG[r * LD + d];
-      float ki[4], qi[4], kj[4];
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const float ei = __expf(sG[(ib + x) * LD + d] - gr);
-        ki[x] = sK[(ib + x) * LD + d] * ei;
-        qi[x] = sQ[(ib + x) * LD + d] * ei;
-        kj[x] = sK[(jb + x) * LD + d] * __expf(gr - sG[(jb + x) * LD + d]);
-      }
-#pragma unroll
-      for (int x = 0; x < 4; ++x)
-#pragma unroll
-        for (int y = 0; y < 4; ++y) {
-          akk[x][y] += ki[x] * kj[y];
-          aqk[x][y] += qi[x] * kj[y];
-        }
-    }
-#pragma unroll
-    for (int x = 0; x < 4; ++x)
-#pragma unroll
-      for (int y = 0; y < 4; ++y) {
-        akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 1);
-        akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 2);
-        akk[x][y] += __shfl_xor_sync(0xffffffffu, akk[x][y], 4);
-        aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 1);
-        aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 2);
-        aqk[x][y] += __shfl_xor_sync(0xffffffffu, aqk[x][y], 4);
-      }
-    if (split == 0) {
-#pragma unroll
-      for (int x = 0; x < 4; ++x)
-#pragma unroll
-        for (int y = 0; y < 4; ++y) {
-          const int i = ib + x, j = jb + y;
-          if (j < i) sA[i * LT + j] = akk[x][y] * sBeta[i];
-          if (j <= i) sAq[i * LT + j] = aqk[x][y];
-        }
-    }
-  }
-  // ---- 2b. off-diagonal 16 x 16 blocks on tensor cores: 12 (I, n-tile) tasks,
-  // run by warps 10-15 (2 each) while warps 0-9 do the diagonal blocks above
-  // (disjoint outputs, shared read-only inputs) ----
-  for (int task = warp - 10; warp >= 10 && task < 12; task += 6) {
-    const int I = task < 2 ? 1 : (task < 6 ? 2 : 3);
-    const int nt = task - (I == 1 ? 0 : (I == 2 ? 2 : 6));  // n-tile of 8 columns j in [0, 16 I)
-    const int r = 16 * I;
-    float ckk[4] = {0.f, 0.f, 0.f, 0.f}, cqk[4] = {0.f, 0.f, 0.f, 0.f};
-    const int i0 = r + gq, i1 = r + gq + 8, j = 8 * nt + gq;
-#pragma unroll 4
-    for (int ks = 0; ks < DK / 8; ++ks) {
-      const int d0 = 8 * ks + tq, d1 = d0 + 4;
-      const float gr0 = sG[r * LD + d0], gr1 = sG[r * LD + d1];
-      const float e00 = __expf(sG[i0 * LD + d0] - gr0), e10 = __expf(sG[i1 * LD + d0] - gr0);
-      const float e01 = __expf(sG[i0 * LD + d1] - gr1), e11 = __expf(sG[i1 * LD + d1] - gr1);
-      const uint32_t ak0 = tf32(sK[i0 * LD + d0] * e00), ak1 = tf32(sK[i1 * LD + d0] * e10);
-      const uint32_t ak2 = tf32(sK[i0 * LD + d1] * e01), ak3 = tf32(sK[i1 * LD + d1] * e11);
-      const uint32_t aq0 = tf32(sQ[i0 * LD + d0] * e00), aq1 = tf32(sQ[i1 * LD + d0] * e10);
-      const uint32_t aq2 = tf32(sQ[i0 * LD + d1] * e01), aq3 = tf32(sQ[i1 * LD + d1] * e11);
-      const uint32_t b0 = tf32(sK[j * LD + d0] * __expf(gr0 - sG[j * LD + d0]));
-      const uint32_t b1 = tf32(sK[j * LD + d1] * __expf(gr1 - sG[j * LD + d1]));
-      mma_tf32(ckk, ak0, ak1, ak2, ak3, b0, b1);
-      mma_tf32(cqk, aq0, aq1, aq2, aq3, b0, b1);
-    }
-    // c0,c1: row i0, cols 8nt+2tq (+1); c2,c3: row i1
-    const int jc = 8 * nt + 2 * tq;
-    sA[i0 * LT + jc] = ckk[0] * sBeta[i0];
-    sA[i0 * LT + jc + 1] = ckk[1] * sBeta[i0];
-    sA[i1 * LT + jc] = ckk[2] * sBeta[i1];
-    sA[i1 * LT + jc + 1] = ckk[3] * sBeta[i1];
-    sAq[i0 * LT + jc] = cqk[0];
-    sAq[i0 * LT + jc + 1] = cqk[1];
-    sAq[i1 * LT + jc] = cqk[2];
-    sAq[i1 * LT + jc + 1] = cqk[3];
-  }
-  __syncthreads();
-
-  // ---- 3a. outputs that need raw Q / K; then beta K e^G into sQ, beta V into sV ----
+  // ---- 6. A_qk -> workspace (fp16, zeros above the diagonal) ----
   {
-    const float* glr = sG + (C - 1) * LD;
-    for (int e = tid; e < C * DK / 4; e += kA2Threads) {
-      const int t = e / (DK / 4), d = 4 * (e % (DK / 4));
-      const float bt = sBeta[t];
-      const float4 gi = *reinterpret_cast<const float4*>(sG + t * LD + d);
-      const float4 kk = *reinterpret_cast<const float4*>(sK + t * LD + d);
-      const float4 qq = *reinterpret_cast<const float4*>(sQ + t * LD + d);
-      const float4 gl = *reinterpret_cast<const float4*>(glr + d);
-      float4 vv = *reinterpret_cast<const float4*>(sV + t * LD + d);
-      const float4 eg = make_float4(__expf(gi.x), __expf(gi.y), __expf(gi.z), __expf(gi.w));
-      {
-        __half2 lo = __floats2half2_rn(qq.x * eg.x, qq.y * eg.y), hi = __floats2half2_rn(qq.z * eg.z, qq.w * eg.w);
-        *reinterpret_cast<uint2*>(ws_h(blk, kWsQg) + t * DK + d) =
-            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-      }
-      {
-        __half2 lo = __floats2half2_rn(kk.x * __expf(gl.x - gi.x), kk.y * __expf(gl.y - gi.y));
-        __half2 hi = __floats2half2_rn(kk.z * __expf(gl.z - gi.z), kk.w * __expf(gl.w - gi.w));
-        *reinterpret_cast<uint2*>(ws_h(blk, kWsKr) + t * DK + d) =
-            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-      }
-      *reinterpret_cast<float4*>(sQ + t * LD + d) =
-          make_float4(bt * kk.x * eg.x, bt * kk.y * eg.y, bt * kk.z * eg.z, bt * kk.w * eg.w);
-      vv.x *= bt;
-      vv.y *= bt;
-      vv.z *= bt;
-      vv.w *= bt;
-      *reinterpret_cast<float4*>(sV + t * LD + d) = vv;
-    }
-    for (int e = tid; e < C * C / 2; e += kA2Threads) {
+    __half* wsAq = ws_h(blk, kWsAq);
+    for (int e = tid; e < C * C / 2; e += kThreads) {
       const int r = (2 * e) / C, c2 = (2 * e) % C;
-      *reinterpret_cast<__half2*>(ws_h(blk, kWsAq) + 2 * e) =
-          __floats2half2_rn(sAq[r * LT + c2], sAq[r * LT + c2 + 1]);
+      *reinterpret_cast<__half2*>(wsAq + 2 * e) = __floats2half2_rn(sAq[r * LT + c2], sAq[r * LT + c2 + 1]);
     }
-    if (tid < DK) blk[kWsGl + tid] = __expf(glr[tid]);
   }
-  // ---- 3b. diagonal blocks of T: column j of block D solved in registers ----
+  // ---- 7. T = (I + A_kk)^-1: diagonal 16 x 16 blocks, column by column ----
   if (tid < C) {
     const int D = tid >> 4, jj = tid & 15, base = 16 * D;
     float col[16];
@@ -337,360 +460,316 @@ kda_intra_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __re
 #pragma unroll
     for (int i = 0; i < 16; ++i) sT[(base + i) * LT + base + jj] = col[i];
   }
-  for (int e = tid; e < C * C; e += kA2Threads) {  // zero T above the diagonal blocks
-    const int i = e / C, jcol = e % C;
-    if ((jcol >> 4) > (i >> 4)) sT[i * LT + jcol] = 0.f;
+  for (int e = tid; e < C * C; e += kThreads) {  // zero T above the diagonal blocks
+    const int i = e / C, jc = e % C;
+    if ((jc >> 4) > (i >> 4)) sT[i * LT + jc] = 0.f;
   }
   __syncthreads();
-  // ---- 3c. off-diagonal blocks of T, level by level: T_IJ = -T_II X_IJ, X_IJ = sum_{M=J}^{I-1} A_IM T_MJ ----
-  for (int I = 1; I < 4; ++I) {
-    float xv[3] = {0.f, 0.f, 0.f};
-    const int nel = 256 * I;  // I blocks J = 0..I-1 of 16 x 16
-    // X into sAq's rows of block I (A_qk is no longer needed)
-    for (int e = tid; e < nel; e += kA2Threads) {
+  // off-diagonal blocks level by level: X_IJ = sum_{M=J}^{I-1} A_IM T_MJ (into
+  // sAq, no longer needed), T_IJ = -T_II X_IJ
+  for (int Ib = 1; Ib < 4; ++Ib) {
+    const int nel = 256 * Ib;
+    for (int e = tid; e < nel; e += kThreads) {
       const int J = e >> 8, ii = (e >> 4) & 15, jj = e & 15;
       float s = 0.f;
-      for (int m = 16 * J; m < 16 * I; ++m) s += sA[(16 * I + ii) * LT + m] * sT[m * LT + 16 * J + jj];
-      sAq[(16 * I + ii) * LT + 16 * J + jj] = s;
+      for (int m = 16 * J; m < 16 * Ib; ++m) s += sA[(16 * Ib + ii) * LT + m] * sT[m * LT + 16 * J + jj];
+      sAq[(16 * Ib + ii) * LT + 16 * J + jj] = s;
     }
-    (void)xv;
     __syncthreads();
-    for (int e = tid; e < nel; e += kA2Threads) {
+    for (int e = tid; e < nel; e += kThreads) {
       const int J = e >> 8, ii = (e >> 4) & 15, jj = e & 15;
       float s = 0.f;
-      for (int m = 0; m <= ii; ++m) s += sT[(16 * I + ii) * LT + 16 * I + m] * sAq[(16 * I + m) * LT + 16 * J + jj];
-      sT[(16 * I + ii) * LT + 16 * J + jj] = -s;
+      for (int m = 0; m <= ii; ++m) s += sT[(16 * Ib + ii) * LT + 16 * Ib + m] * sAq[(16 * Ib + m) * LT + 16 * J + jj];
+      sT[(16 * Ib + ii) * LT + 16 * J + jj] = -s;
     }
     __syncthreads();
   }
-
-  // ---- 4. W = T (beta K e^G), U = T (beta V): warp -> (m-tile w%4, column quarter w/4) ----
+  // ---- 8. T (bf16) as the B operand: rows t, K = j ----
   {
-    const int mt = warp & 3, nh = warp >> 2;
-    const int r0 = 16 * mt, c0 = 32 * nh;
-    float w[4][4], u[4][4];
+    const int t = tid >> 2, c0 = 16 * (tid & 3);
+    uint32_t pk[8];
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int i = 0; i < 8; ++i) pk[i] = bf2(sT[t * LT + c0 + 2 * i], sT[t * LT + c0 + 2 * i + 1]);
+    *reinterpret_cast<uint4*>(sm + kBT + sw_off(t, c0, 64)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    *reinterpret_cast<uint4*>(sm + kBT + sw_off(t, c0 + 8, 64)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
+  tc::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (tid == 0 && alive) {
+    tc::fence_after_sync();
+    constexpr uint32_t idesc = tc::idesc_f16(128, 64, true);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) w[n][e] = u[n][e] = 0.f;
-    const int ksteps = 2 * mt + 2;  // T is lower triangular
-    for (int ks = 0; ks < ksteps; ++ks) {
-      const int k0 = 8 * ks;
-      const uint32_t a0 = tf32(sT[(r0 + gq) * LT + k0 + tq]), a1 = tf32(sT[(r0 + gq + 8) * LT + k0 + tq]);
-      const uint32_t a2 = tf32(sT[(r0 + gq) * LT + k0 + tq + 4]), a3 = tf32(sT[(r0 + gq + 8) * LT + k0 + tq + 4]);
+    for (int s = 0; s < C / 16; ++s)
+      tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(sm + kAW) + 2u * s, tc::desc_kmajor_sw128(sm + kBT) + 2u * s,
+                     idesc, s != 0);
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        const int col = c0 + 8 * n + gq;
-        mma_tf32(w[n], a0, a1, a2, a3, tf32(sQ[(k0 + tq) * LD + col]), tf32(sQ[(k0 + tq + 4) * LD + col]));
-        mma_tf32(u[n], a0, a1, a2, a3, tf32(sV[(k0 + tq) * LD + col]), tf32(sV[(k0 + tq + 4) * LD + col]));
-      }
+    for (int s = 0; s < C / 16; ++s)
+      tc::mma_f16_ss(tmem + 64, tc::desc_kmajor_sw128(sm + kAU) + 2u * s, tc::desc_kmajor_sw128(sm + kBT) + 2u * s,
+                     idesc, s != 0);
+    tc::commit(&bar[1]);
+  }
+  if (alive) alive = mbar_wait(&bar[1], 0, err, 0xB2300002u);
+  tc::fence_after_sync();
+  // ---- 9. W^T, U^T (TMEM lane = dk / dv, column = t) -> W, U [t][d] fp16 ----
+  if (alive) {
+    const int qd = warp & 3, half = warp >> 2;
+    const int d = 32 * qd + lane;
+    uint32_t va[32];
+    __half* dst = ws_h(blk, half ? kWsU : kWsW);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(qd * 32) << 16) + 64u * half + 32u * c, va);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) dst[(32 * c + i) * DK + d] = __float2half_rn(__uint_as_float(va[i]));
     }
-#pragma unroll
-    for (int n = 0; n < 4; ++n) {
-      const int col = c0 + 8 * n + 2 * tq;
-      const int ra = r0 + gq, rb = r0 + gq + 8;
-      *reinterpret_cast<__half2*>(ws_h(blk, kWsW) + ra * DK + col) = __floats2half2_rn(w[n][0], w[n][1]);
-      *reinterpret_cast<__half2*>(ws_h(blk, kWsW) + rb * DK + col) = __floats2half2_rn(w[n][2], w[n][3]);
-      *reinterpret_cast<__half2*>(ws_h(blk, kWsU) + ra * DV + col) = __floats2half2_rn(u[n][0], u[n][1]);
-      *reinterpret_cast<__half2*>(ws_h(blk, kWsU) + rb * DV + col) = __floats2half2_rn(u[n][2], u[n][3]);
-    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
 // ---------------------------------------------------------------------------
-// Kernel B: sequential state pass, one CTA per (b, h, 32 state columns).
-// Per chunk (fp16 m16n8k16 MMAs with fp32 accumulate; the fp32 state lives in
-// registers, its fp16 operand copy S^T in shared memory):
-//   V' = U - W S          (64 x 32, K = 128)
-//   S  = e^{G_last} o S + Kr^T V'   (128 x 32, K = 64; Kr^T by ldmatrix.trans)
-// S and V' enter the MMAs rounded to fp16, the 10-bit mantissa tf32 gave.
-// and stores V' and the state entering the chunk for kernel C.  The next
-// chunk's W, Kr and U slice stream in with cp.async while this one computes.
+// Kernel B: fused state recurrence + outputs, one CTA per (b, h, 64 state
+// columns), 4 warps; warp w owns the 16 state columns dv0 = v0 + 16 w ..
+// dv0 + 15 for the whole sequence.  Columns of the state are independent (the
+// transition acts on the Dk side only), so a warp never waits for another
+// warp's state.  Everything runs on the transposed state S^T [Dv, Dk], held
+// in fp32 m16n8 accumulator fragments, whose fp16 copies are the A operands
+// of the next MMAs directly from registers:
+//   V'^T = U^T - S^T W^T                 (16 x 64, K = 128)
+//   O^T  = S^T Qg^T + V'^T A_qk^T        (16 x 64, K = 128 and K = 64, causal)
+//   S^T  = S^T o e^{G_last} + V'^T Kr    (16 x 128, K = 64)
+// W, Kr, Qg, A_qk, this CTA's U columns and e^{G_last} stream through a
+// two-stage cp.async ring; the B operands come out of it by ldmatrix (Kr
+// transposed).  S^T and V'^T enter the MMAs rounded to fp16 (10-bit
+// mantissa); the state itself stays fp32.  O leaves through a shared-memory
+// tile so that each output row is one coalesced store.
 // ---------------------------------------------------------------------------
-constexpr int SV = 32;        // state columns per CTA
-constexpr int kB2Threads = 128;
-constexpr int LW = DK + 8;    // sW row stride (halves): A-fragment reads (row g, col t), word stride 68
-constexpr int LKR = DK + 8;   // sKr row stride (halves): transposed A reads (row t, col g)
-constexpr int LU = SV + 8;    // sU row stride (halves)
-constexpr int LS = DK + 8;    // sSt row stride (halves): S^T, one row per state column
-constexpr int LVT = C + 8;    // sVt row stride (halves): V'^T
-constexpr int kB2StageBytes = (C * LW + C * LKR + C * LU) * 2;  // fp16 W, Kr, U slice
-constexpr int kB2SBytes = 2 * kB2StageBytes;                    // S^T after the two stages
-constexpr int kB2VtBytes = kB2SBytes + SV * LS * 2;
-constexpr size_t kB2Smem = (size_t)kB2VtBytes + SV * LVT * 2;
+constexpr int RW = 4;                 // warps per CTA
+constexpr int RV = 16 * RW;           // state columns per CTA
+constexpr int kRThreads = 32 * RW;
+constexpr int LR = DK + 8;            // halves: W, Kr, Qg rows (ldmatrix rows on distinct banks)
+constexpr int LA = C + 8;             // halves: A_qk rows
+constexpr int LUS = RV + 8;           // halves: U slice rows
+constexpr int kRW = 0;                // stage offsets in halves
+constexpr int kRKr = kRW + C * LR;
+constexpr int kRQg = kRKr + C * LR;
+constexpr int kRAq = kRQg + C * LR;
+constexpr int kRU = kRAq + C * LA;
+constexpr int kRStageHalves = kRU + C * LUS;
+constexpr int kRStageBytes = kRStageHalves * 2 + DK * 4;  // + e^{G_last} (fp32)
+constexpr int LO = RV + 4;                                // floats: output staging rows
+constexpr size_t kRSmem = 2 * (size_t)kRStageBytes + (size_t)C * LO * 4;
+static_assert(kRStageBytes % 16 == 0, "stage alignment");
 
-__device__ __forceinline__ void b2_load_stage(unsigned char* st, const float* blk, int v0, int tid) {
-  __half* sW = reinterpret_cast<__half*>(st);
-  __half* sKr = sW + C * LW;
-  __half* sU = sKr + C * LKR;
-  for (int e = tid; e < C * DK / 8; e += kB2Threads) {
+__device__ __forceinline__ void r_load_stage(unsigned char* st, const float* blk, int v0, int tid) {
+  __half* s = reinterpret_cast<__half*>(st);
+  float* sGl = reinterpret_cast<float*>(st + kRStageHalves * 2);
+  for (int e = tid; e < C * DK / 8; e += kRThreads) {
     const int r = e / (DK / 8), c8 = e % (DK / 8);
-    cp_async16(sW + r * LW + 8 * c8, ws_h(blk, kWsW) + r * DK + 8 * c8);
-    cp_async16(sKr + r * LKR + 8 * c8, ws_h(blk, kWsKr) + r * DK + 8 * c8);
+    cp_async16(s + kRW + r * LR + 8 * c8, ws_h(blk, kWsW) + r * DK + 8 * c8);
+    cp_async16(s + kRKr + r * LR + 8 * c8, ws_h(blk, kWsKr) + r * DK + 8 * c8);
+    cp_async16(s + kRQg + r * LR + 8 * c8, ws_h(blk, kWsQg) + r * DK + 8 * c8);
   }
-  for (int e = tid; e < C * SV / 8; e += kB2Threads) {
-    const int r = e / (SV / 8), c8 = e % (SV / 8);
-    cp_async16(sU + r * LU + 8 * c8, ws_h(blk, kWsU) + r * DV + v0 + 8 * c8);
+  for (int e = tid; e < C * C / 8; e += kRThreads) {
+    const int r = e / (C / 8), c8 = e % (C / 8);
+    cp_async16(s + kRAq + r * LA + 8 * c8, ws_h(blk, kWsAq) + r * C + 8 * c8);
   }
+  for (int e = tid; e < C * RV / 8; e += kRThreads) {
+    const int r = e / (RV / 8), c8 = e % (RV / 8);
+    cp_async16(s + kRU + r * LUS + 8 * c8, ws_h(blk, kWsU) + r * DV + v0 + 8 * c8);
+  }
+  if (tid < DK / 4) cp_async16(sGl + 4 * tid, blk + kWsGl + 4 * tid);
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack_h2(uint32_t u) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
 
-__global__ void __launch_bounds__(kB2Threads, 1)
-kda_state_kernel(float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ s_out, int B, int Tlen,
-                 int H) {
+template <typename T>
+__device__ __forceinline__ void store4(T* dst, float4 v) {
+  if constexpr (sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(dst) = v;
+  } else {
+    T h[4] = {from_f32<T>(v.x), from_f32<T>(v.y), from_f32<T>(v.z), from_f32<T>(v.w)};
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(h);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRThreads, 1)
+kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ s_out,
+                 T* __restrict__ o, int B, int Tlen, int H) {
   extern __shared__ __align__(16) unsigned char smb[];
-  __half* sSt = reinterpret_cast<__half*>(smb + kB2SBytes);   // S^T, fp16 operand copy
-  __half* sVt = reinterpret_cast<__half*>(smb + kB2VtBytes);  // V'^T, fp16 operand copy
+  float* sO = reinterpret_cast<float*>(smb + 2 * kRStageBytes);
   const int nc = Tlen / C;
-  const int v0 = blockIdx.x * SV, h = blockIdx.y, b = blockIdx.z;
+  const int v0 = blockIdx.x * RV, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
-  float* head = ws + ((size_t)b * H + h) * nc * kWsBlock;
+  const int g = lane >> 2, tq = lane & 3, mat = lane >> 3, r8 = lane & 7;
+  const int dv0 = v0 + 16 * warp;
+  const float* head = ws + ((size_t)b * H + h) * nc * kWsBlock;
+  const size_t sbase = ((size_t)b * H + h) * DK * DV;
 
-  b2_load_stage(smb, head, v0, tid);
+  r_load_stage(smb, head, v0, tid);
   cp_async_commit();
 
-  // state rows of this warp: m-tiles 2w, 2w+1 (dk rows 32w .. 32w+31), all 32 columns, fp32
-  float acc[2][4][4];
+  // S^T fragments: n-tile nt covers dk 8 nt .. 8 nt + 7; e: (dv g | g + 8) x (dk 2 tq | 2 tq + 1)
+  float S[16][4];
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
+  for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
-        const float v = s0 ? s0[(((size_t)b * H + h) * DK + row) * DV + v0 + col] : 0.f;
-        acc[mt][nt][e] = v;
-        sSt[col * LS + row] = __float2half_rn(v);
-      }
+    for (int e = 0; e < 4; ++e) {
+      const int dk = 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
+      S[nt][e] = s0 ? s0[sbase + (size_t)dk * DV + dv] : 0.f;
+    }
 
   for (int c = 0; c < nc; ++c) {
-    float* blk = head + (size_t)c * kWsBlock;
-    unsigned char* st = smb + (c & 1) * kB2StageBytes;
+    const unsigned char* st = smb + (c & 1) * kRStageBytes;
     if (c + 1 < nc) {
-      b2_load_stage(smb + ((c + 1) & 1) * kB2StageBytes, blk + kWsBlock, v0, tid);
+      r_load_stage(smb + ((c + 1) & 1) * kRStageBytes, head + (size_t)(c + 1) * kWsBlock, v0, tid);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();  // stage c and S^T visible to all
-    const __half* sW = reinterpret_cast<const __half*>(st);
-    const __half* sKr = sW + C * LW;
-    const __half* sU = sKr + C * LKR;
+    __syncthreads();  // stage c visible to every warp
+    const __half* sW = reinterpret_cast<const __half*>(st) + kRW;
+    const __half* sKr = reinterpret_cast<const __half*>(st) + kRKr;
+    const __half* sQg = reinterpret_cast<const __half*>(st) + kRQg;
+    const __half* sAq = reinterpret_cast<const __half*>(st) + kRAq;
+    const __half* sU = reinterpret_cast<const __half*>(st) + kRU;
+    const float* sGl = reinterpret_cast<const float*>(st + kRStageHalves * 2);
 
-    // state entering this chunk -> workspace (read by kernel C)
+    // S^T as fp16 A fragments, one per 16-wide dk step
+    uint32_t sa[8][4];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = v0 + 8 * nt + 2 * t;
-          *reinterpret_cast<__half2*>(ws_h(blk, kWsS) + row * DV + col) =
-              __floats2half2_rn(acc[mt][nt][e], acc[mt][nt][e + 1]);
-        }
-
-    // V' = U - W S (fp16 MMAs m16n8k16, fp32 accumulate): warp w owns chunk rows 16w .. 16w+15
-    {
-      float p[4][4];
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) p[nt][e] = 0.f;
-      const int r0 = 16 * warp;
-#pragma unroll 2
-      for (int ks = 0; ks < DK / 16; ++ks) {
-        const int k0 = 16 * ks;
-        uint32_t a[4];
-        a[0] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g) * LW + k0 + 2 * t);
-        a[1] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g + 8) * LW + k0 + 2 * t);
-        a[2] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g) * LW + k0 + 2 * t + 8);
-        a[3] = *reinterpret_cast<const uint32_t*>(sW + (r0 + g + 8) * LW + k0 + 2 * t + 8);
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          uint32_t bb[2];
-          bb[0] = *reinterpret_cast<const uint32_t*>(sSt + (8 * nt + g) * LS + k0 + 2 * t);
-          bb[1] = *reinterpret_cast<const uint32_t*>(sSt + (8 * nt + g) * LS + k0 + 2 * t + 8);
-          mma_16816<B2_F16>(p[nt], a, bb);
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int row = r0 + g + 8 * (e >> 1), col = 8 * nt + 2 * t;
-          const float2 u = __half22float2(*reinterpret_cast<const __half2*>(sU + row * LU + col));
-          const float v0f = u.x - p[nt][e], v1f = u.y - p[nt][e + 1];
-          sVt[col * LVT + row] = __float2half_rn(v0f);
-          sVt[(col + 1) * LVT + row] = __float2half_rn(v1f);
-          *reinterpret_cast<__half2*>(ws_h(blk, kWsVp) + row * DV + v0 + col) = __floats2half2_rn(v0f, v1f);
-        }
+    for (int kk = 0; kk < 8; ++kk) {
+      sa[kk][0] = pack_h2(S[2 * kk][0], S[2 * kk][1]);
+      sa[kk][1] = pack_h2(S[2 * kk][2], S[2 * kk][3]);
+      sa[kk][2] = pack_h2(S[2 * kk + 1][0], S[2 * kk + 1][1]);
+      sa[kk][3] = pack_h2(S[2 * kk + 1][2], S[2 * kk + 1][3]);
     }
-    __syncthreads();  // V'^T complete; every warp finished reading S^T
-
-    // S = e^{G_last} o S + Kr^T V' (A = Kr^T by ldmatrix.trans, B = V'^T rows)
-    {
-      const float* glp = blk + kWsGl;
+    // acc = S^T W^T - U^T (= -V'^T), starting from -U^T read as C fragments
+    float vp[8][4], oa[8][4];
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const float gl0 = glp[32 * warp + 16 * mt + g], gl1 = glp[32 * warp + 16 * mt + g + 8];
+    for (int p = 0; p < 4; ++p) {
+      uint32_t u[4];
+      ldsm_x4_trans(smem_u32(sU + (8 * (2 * p + (mat >> 1)) + r8) * LUS + 16 * warp + ((mat & 1) << 3)), u);
+      const float2 a0 = unpack_h2(u[0]), a1 = unpack_h2(u[1]), a2 = unpack_h2(u[2]), a3 = unpack_h2(u[3]);
+      vp[2 * p][0] = -a0.x;
+      vp[2 * p][1] = -a0.y;
+      vp[2 * p][2] = -a1.x;
+      vp[2 * p][3] = -a1.y;
+      vp[2 * p + 1][0] = -a2.x;
+      vp[2 * p + 1][1] = -a2.y;
+      vp[2 * p + 1][2] = -a3.x;
+      vp[2 * p + 1][3] = -a3.y;
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          acc[mt][nt][0] *= gl0;
-          acc[mt][nt][1] *= gl0;
-          acc[mt][nt][2] *= gl1;
-          acc[mt][nt][3] *= gl1;
-        }
-      }
-      const int mat = lane >> 3;
-#pragma unroll
-      for (int ks = 0; ks < C / 16; ++ks) {
-        const int k0 = 16 * ks;
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          const int m0 = 32 * warp + 16 * mt;  // dk rows; A[m][k] = Kr[k][m]
-          uint32_t a[4];
-          ldsm_x4_trans(smem_u32(sKr + (k0 + (lane & 7) + ((mat >> 1) << 3)) * LKR + m0 + ((mat & 1) << 3)), a);
-#pragma unroll
-          for (int nt = 0; nt < 4; ++nt) {
-            uint32_t bb[2];
-            bb[0] = *reinterpret_cast<const uint32_t*>(sVt + (8 * nt + g) * LVT + k0 + 2 * t);
-            bb[1] = *reinterpret_cast<const uint32_t*>(sVt + (8 * nt + g) * LVT + k0 + 2 * t + 8);
-            mma_16816<B2_F16>(acc[mt][nt], a, bb);
-          }
-        }
-      }
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
-            sSt[col * LS + row] = __float2half_rn(acc[mt][nt][e]);
-          }
+      for (int e = 0; e < 4; ++e) oa[2 * p][e] = oa[2 * p + 1][e] = 0.f;
     }
-    __syncthreads();  // new S^T visible; stage c may be overwritten by the next prefetch
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
+        uint32_t bw[4], bq[4];
+        ldsm_x4(smem_u32(sW + row * LR + col), bw);
+        const uint32_t w0[2] = {bw[0], bw[1]}, w1[2] = {bw[2], bw[3]};
+        mma_16816<B2_F16>(vp[2 * np], sa[kk], w0);
+        mma_16816<B2_F16>(vp[2 * np + 1], sa[kk], w1);
+        ldsm_x4(smem_u32(sQg + row * LR + col), bq);
+        const uint32_t q0[2] = {bq[0], bq[1]}, q1[2] = {bq[2], bq[3]};
+        mma_16816<B2_F16>(oa[2 * np], sa[kk], q0);
+        mma_16816<B2_F16>(oa[2 * np + 1], sa[kk], q1);
+      }
+    }
+    // V'^T = -acc as fp16 A fragments over the chunk's 4 16-step blocks
+    uint32_t va[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      va[kk][0] = pack_h2(-vp[2 * kk][0], -vp[2 * kk][1]);
+      va[kk][1] = pack_h2(-vp[2 * kk][2], -vp[2 * kk][3]);
+      va[kk][2] = pack_h2(-vp[2 * kk + 1][0], -vp[2 * kk + 1][1]);
+      va[kk][3] = pack_h2(-vp[2 * kk + 1][2], -vp[2 * kk + 1][3]);
+    }
+    // O^T += V'^T A_qk^T: A_qk[i][j] = 0 for j > i, so key block kk only
+    // reaches query blocks np >= kk
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        if (np < kk) continue;
+        const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
+        uint32_t ba[4];
+        ldsm_x4(smem_u32(sAq + row * LA + col), ba);
+        const uint32_t a0[2] = {ba[0], ba[1]}, a1[2] = {ba[2], ba[3]};
+        mma_16816<B2_F16>(oa[2 * np], va[kk], a0);
+        mma_16816<B2_F16>(oa[2 * np + 1], va[kk], a1);
+      }
+    }
+    // S^T = S^T o e^{G_last} (per dk column) + V'^T Kr
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const float2 gl = *reinterpret_cast<const float2*>(sGl + 8 * nt + 2 * tq);
+      S[nt][0] *= gl.x;
+      S[nt][1] *= gl.y;
+      S[nt][2] *= gl.x;
+      S[nt][3] *= gl.y;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        uint32_t bk[4];
+        ldsm_x4_trans(smem_u32(sKr + (16 * kk + r8 + ((mat & 1) << 3)) * LR + 16 * np + ((mat >> 1) << 3)), bk);
+        const uint32_t k0[2] = {bk[0], bk[1]}, k1[2] = {bk[2], bk[3]};
+        mma_16816<B2_F16>(S[2 * np], va[kk], k0);
+        mma_16816<B2_F16>(S[2 * np + 1], va[kk], k1);
+      }
+    }
+    // O^T -> staging tile [t][dv], then coalesced rows of o
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = 8 * nt + 2 * tq + (e & 1), dvl = 16 * warp + g + 8 * (e >> 1);
+        sO[t * LO + dvl] = oa[nt][e];
+      }
+    __syncthreads();  // staging complete; every warp is done with stage c
+    for (int e = tid; e < C * RV / 4; e += kRThreads) {
+      const int t = e / (RV / 4), c4 = e % (RV / 4);
+      const float4 val = *reinterpret_cast<const float4*>(sO + t * LO + 4 * c4);
+      store4<T>(o + (((int64_t)b * Tlen + (int64_t)c * C + t) * H + h) * DV + v0 + 4 * c4, val);
+    }
   }
   if (s_out) {
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = 32 * warp + 16 * mt + g + 8 * (e >> 1), col = 8 * nt + 2 * t + (e & 1);
-          s_out[(((size_t)b * H + h) * DK + row) * DV + v0 + col] = acc[mt][nt][e];
-        }
+      for (int e = 0; e < 4; ++e) {
+        const int dk = 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
+        s_out[sbase + (size_t)dk * DV + dv] = S[nt][e];
+      }
   }
-}
-
-// ---------------------------------------------------------------------------
-// Kernel C: outputs, one CTA per (b, h, chunk), fully parallel:
-//   O = (scale Q o e^G) S_c + A_qk V'     (64 x 128; fp16 MMAs on the fp16 operands)
-// ---------------------------------------------------------------------------
-constexpr int kCThreads = 128;
-constexpr int LQ = DK + 8;   // halves; A reads (row g, col t): word stride 68 = 4 banks apart
-constexpr int LAQ = C + 8;   // halves; word stride 36
-constexpr int LBS = DV + 8;  // halves; B reads (row t, col g)
-constexpr int kCQ = 0;
-constexpr int kCA = kCQ + C * LQ;
-constexpr int kCS = kCA + C * LAQ;
-constexpr int kCV = kCS + DK * LBS;
-constexpr int kCHalves = kCV + C * LBS;
-constexpr size_t kCSmem = (size_t)kCHalves * 2;
-
-template <typename T>
-__global__ void __launch_bounds__(kCThreads, 2)
-kda_output_kernel(const float* __restrict__ ws, T* __restrict__ o, int B, int Tlen, int H) {
-  extern __shared__ __align__(16) __half smh[];
-  __half* sQ = smh + kCQ;
-  __half* sA = smh + kCA;
-  __half* sS = smh + kCS;
-  __half* sV = smh + kCV;
-  const int nc = Tlen / C;
-  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const float* blk = ws + (((size_t)b * H + h) * nc + chunk) * kWsBlock;
-  for (int e = tid; e < C * DK / 8; e += kCThreads) {
-    const int r = e / (DK / 8), c8 = e % (DK / 8);
-    cp_async16(sQ + r * LQ + 8 * c8, ws_h(blk, kWsQg) + r * DK + 8 * c8);
-    cp_async16(sV + r * LBS + 8 * c8, ws_h(blk, kWsVp) + r * DV + 8 * c8);
-  }
-  for (int e = tid; e < DK * DV / 8; e += kCThreads) {
-    const int r = e / (DV / 8), c8 = e % (DV / 8);
-    cp_async16(sS + r * LBS + 8 * c8, ws_h(blk, kWsS) + r * DV + 8 * c8);
-  }
-  for (int e = tid; e < C * C / 8; e += kCThreads) {
-    const int r = e / (C / 8), c8 = e % (C / 8);
-    cp_async16(sA + r * LAQ + 8 * c8, ws_h(blk, kWsAq) + r * C + 8 * c8);
-  }
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
-  // warp w: chunk rows 16w .. 16w+15, all 128 output columns (16 n-tiles)
-  const int r0 = 16 * warp;
-  float acc[16][4];
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-  // fp16 m16n8k16 MMAs: A fragments (row-major Qg, A_qk) by 32-bit loads, B
-  // fragments of the row-major [k][n] tiles (S_c, V') by ldmatrix.trans,
-  // matrices (k lo, n lo), (k hi, n lo), (k lo, n hi), (k hi, n hi)
-  const int mat = lane >> 3;
-  const int brow = (lane & 7) + ((mat & 1) << 3), bcol = (mat >> 1) << 3;
-#pragma unroll 2
-  for (int ks = 0; ks < DK / 16; ++ks) {
-    const int k0 = 16 * ks;
-    uint32_t a[4];
-    a[0] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g) * LQ + k0 + 2 * t);
-    a[1] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g + 8) * LQ + k0 + 2 * t);
-    a[2] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g) * LQ + k0 + 2 * t + 8);
-    a[3] = *reinterpret_cast<const uint32_t*>(sQ + (r0 + g + 8) * LQ + k0 + 2 * t + 8);
-#pragma unroll
-    for (int np = 0; np < 8; ++np) {
-      uint32_t bf[4];
-      ldsm_x4_trans(smem_u32(sS + (k0 + brow) * LBS + 16 * np + bcol), bf);
-      const uint32_t b0[2] = {bf[0], bf[1]}, b1[2] = {bf[2], bf[3]};
-      mma_16816<B2_F16>(acc[2 * np], a, b0);
-      mma_16816<B2_F16>(acc[2 * np + 1], a, b1);
-    }
-  }
-  // A_qk is lower triangular: k-steps beyond this warp's last row contribute 0
-  const int ksteps = warp + 1;
-  for (int ks = 0; ks < ksteps; ++ks) {
-    const int k0 = 16 * ks;
-    uint32_t a[4];
-    a[0] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g) * LAQ + k0 + 2 * t);
-    a[1] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g + 8) * LAQ + k0 + 2 * t);
-    a[2] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g) * LAQ + k0 + 2 * t + 8);
-    a[3] = *reinterpret_cast<const uint32_t*>(sA + (r0 + g + 8) * LAQ + k0 + 2 * t + 8);
-#pragma unroll
-    for (int np = 0; np < 8; ++np) {
-      uint32_t bf[4];
-      ldsm_x4_trans(smem_u32(sV + (k0 + brow) * LBS + 16 * np + bcol), bf);
-      const uint32_t b0[2] = {bf[0], bf[1]}, b1[2] = {bf[2], bf[3]};
-      mma_16816<B2_F16>(acc[2 * np], a, b0);
-      mma_16816<B2_F16>(acc[2 * np + 1], a, b1);
-    }
-  }
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      const int row = r0 + g + 8 * (e >> 1), col = 8 * nt + 2 * t;
-      T* dst = o + (((int64_t)b * Tlen + (int64_t)chunk * C + row) * H + h) * DV + col;
-      dst[0] = from_f32<T>(acc[nt][e]);
-      dst[1] = from_f32<T>(acc[nt][e + 1]);
-    }
 }
 }  // namespace kda
 }  // namespace b2
@@ -713,8 +792,9 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
                           int64_t T, int64_t H, int64_t Dk, int64_t Dv, int64_t chunk, float scale, int dtype,
                           void* stream) {
   B2_CHECK_ARG(q && k && v && g && beta && o && workspace, B2_ERR_INVALID, "kda_fwd: null pointer");
-  B2_CHECK_ARG(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(g, 16), B2_ERR_ALIGN,
-               "kda_fwd: q, k, v and g must be 16-byte aligned");
+  B2_CHECK_ARG(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(g, 16) && aligned(o, 16) &&
+                   aligned(workspace, 16),
+               B2_ERR_ALIGN, "kda_fwd: q, k, v, g, o and the workspace must be 16-byte aligned");
   B2_CHECK_ARG(B > 0 && T > 0 && H > 0, B2_ERR_INVALID, "kda_fwd: bad shape");
   B2_CHECK_ARG(Dk == kda::DK && Dv == kda::DV, B2_ERR_UNSUPPORTED, "kda_fwd: Dk = Dv = 128 only (got %lld, %lld)",
                (long long)Dk, (long long)Dv);
@@ -725,18 +805,18 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
   B2_CHECK_ARG(B * H <= 65535 && T / chunk <= 2147483647, B2_ERR_UNSUPPORTED, "kda_fwd: too large");
   cudaStream_t st = (cudaStream_t)stream;
   float* ws = (float*)workspace;
+  unsigned* err = device_error_word();
+  B2_CHECK_ARG(err, B2_ERR_LAUNCH, "kda_fwd: no device error word");
   const dim3 ga((unsigned)(T / chunk), (unsigned)H, (unsigned)B);
-  const dim3 gb(kda::DV / kda::SV, (unsigned)H, (unsigned)B);
-  set_max_smem((const void*)kda::kda_state_kernel, (int)kda::kB2Smem);
+  const dim3 gb(kda::DV / kda::RV, (unsigned)H, (unsigned)B);
 #define B2_KDA_LAUNCH(TY)                                                                                         \
   do {                                                                                                            \
-    set_max_smem((const void*)kda::kda_intra_kernel<TY>, (int)kda::kA2Smem);                                     \
-    set_max_smem((const void*)kda::kda_output_kernel<TY>, (int)kda::kCSmem);                                      \
-    kda::kda_intra_kernel<TY><<<ga, kda::kA2Threads, kda::kA2Smem, st>>>(                                         \
-        (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale);        \
-    kda::kda_state_kernel<<<gb, kda::kB2Threads, kda::kB2Smem, st>>>(ws, initial_state, final_state, (int)B,     \
-                                                                     (int)T, (int)H);                           \
-    kda::kda_output_kernel<TY><<<ga, kda::kCThreads, kda::kCSmem, st>>>(ws, (TY*)o, (int)B, (int)T, (int)H);     \
+    set_max_smem((const void*)kda::kda_prep_kernel<TY>, (int)kda::prep::kSmem);                                  \
+    set_max_smem((const void*)kda::kda_recur_kernel<TY>, (int)kda::kRSmem);                                      \
+    kda::kda_prep_kernel<TY><<<ga, kda::prep::kThreads, kda::prep::kSmem, st>>>(                                  \
+        (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale, err);   \
+    kda::kda_recur_kernel<TY><<<gb, kda::kRThreads, kda::kRSmem, st>>>(ws, initial_state, final_state, (TY*)o,    \
+                                                                       (int)B, (int)T, (int)H);                 \
   } while (0)
   if (dtype == B2_BF16) B2_KDA_LAUNCH(__nv_bfloat16);
   else if (dtype == B2_F16) B2_KDA_LAUNCH(__half);
