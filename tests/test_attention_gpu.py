@@ -37,16 +37,27 @@ def test_triton_fa_golden(cuda, rec):
     assert (out.cpu() - torch.tensor(g["out"])).abs().max().item() < 0.01
 
 
-@pytest.mark.parametrize("name", ["test_flash_attention_single_head", "test_flash_attention_multi_block",
-                                  "test_flash_attention_causal", "test_flash_attention_gpu",
-                                  "test_causal_attention_gpu"])
+# Each reference test's own acceptance rule, |got - expected| < max(atol, rtol |expected|)
+# (tests/test_emitter.py: single_head :1917, multi_block :1983, causal :2359 / :2369,
+# causal_attention_gpu :5574, flash_attention_gpu :5647).
+TEMPLATE_TOL = {"test_flash_attention_single_head": (1e-3, 1e-2), "test_flash_attention_multi_block": (1e-2, 5e-2),
+                "test_flash_attention_causal": (1e-3, 2e-2), "test_causal_attention_gpu": (5e-2, 0.0),
+                "test_flash_attention_gpu": (1e-1, 0.0)}
+
+
+@pytest.mark.parametrize("name", sorted(TEMPLATE_TOL))
 def test_template_golden(cuda, name):
+    """The reference template tests' fp32 buffers (head_dim 64 runs the tf32
+    tcgen05 kernel, head_dim 8 the CUDA-core kernel) at the reference's own
+    tolerance."""
     import b200kern as bk
     g, rec = golden("ref_" + name), REF_TESTS[name]
     Q, K, V = (torch.tensor(g[n], device=cuda) for n in "qkv")
     out = bk.flash_attention_template(Q, K, V, rec["seq_len"], rec["scale"], rec["head_dim"], causal=rec["causal"])
-    ref = g["expected"] if "expected" in g else g["out"]
-    assert np.abs(out.reshape(-1).cpu().numpy() - ref.reshape(-1)).max() < 1e-3
+    ref = (g["expected"] if "expected" in g else g["out"]).reshape(-1)
+    atol, rtol = TEMPLATE_TOL[name]
+    err = np.abs(out.reshape(-1).cpu().numpy() - ref)
+    assert (err < np.maximum(atol, rtol * np.abs(ref))).all(), f"max err {err.max():.3g}"
 
 
 @pytest.mark.parametrize("name", ["test_gqa_attention", "test_gqa_attention_gpu"])
@@ -74,17 +85,36 @@ def _ref_torch(q, k, v, causal, scale=None):
     return out
 
 
+@pytest.mark.parametrize("D", [128, 64])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,Hq,Hkv,S,causal", [(1, 1, 1, 128, False), (1, 2, 2, 256, True), (2, 4, 2, 384, True),
                                                (1, 4, 1, 200, False), (1, 2, 1, 1000, True), (1, 8, 2, 2048, True)])
-def test_fa_tcgen05(cuda, dtype, B, Hq, Hkv, S, causal):
+def test_fa_tcgen05(cuda, D, dtype, B, Hq, Hkv, S, causal):
     import b200kern as bk
-    g = torch.Generator().manual_seed(S + Hq)
-    q = (torch.randn(B, Hq, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
-    k = (torch.randn(B, Hkv, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
-    v = (torch.randn(B, Hkv, S, 128, generator=g) * 0.5).to(dtype).to(cuda)
+    g = torch.Generator().manual_seed(S + Hq + D)
+    q = (torch.randn(B, Hq, S, D, generator=g) * 0.5).to(dtype).to(cuda)
+    k = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).to(dtype).to(cuda)
+    v = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).to(dtype).to(cuda)
     out = bk.flash_attention(q, k, v, causal=causal)
     _close(out, _ref_torch(q, k, v, causal))
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,causal,window", [(1, 1, 1, 128, False, 0), (2, 8, 8, 1024, True, 0),
+                                                      (1, 4, 2, 300, True, 0), (1, 4, 1, 777, False, 0),
+                                                      (1, 2, 2, 640, True, 100), (1, 4, 2, 2048, True, 0)])
+def test_fa_tf32_d64(cuda, B, Hq, Hkv, S, causal, window):
+    """fp32 q / k / v with head dim 64 (the reference template's default) on
+    the tcgen05 kernel with tf32 operands: fp32 output within rtol = atol =
+    1e-2 of the float64 oracle (N(0,1) inputs, so logits of order 1)."""
+    import b200kern as bk
+    g = torch.Generator().manual_seed(S + Hq + window)
+    q = torch.randn(B, Hq, S, 64, generator=g)
+    k = torch.randn(B, Hkv, S, 64, generator=g)
+    v = torch.randn(B, Hkv, S, 64, generator=g)
+    out = bk.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=causal, window=window)
+    assert out.dtype == torch.float32
+    ref = oatt.attention(q.double().numpy(), k.double().numpy(), v.double().numpy(), causal=causal, window=window)
+    _close(out.cpu(), torch.from_numpy(ref))
 
 
 def test_fa_tcgen05_strided_and_large_logits(cuda):
@@ -117,7 +147,9 @@ def test_fa_oracle_small_bf16(cuda):
 def test_fa_c0_config(cuda):
     """BASELINE configs[0] (the reference's CPU-runnable case): fp32
     [2, 8, 1024, 64], causal, scale 1/8, q then k then v ~ N(0, 1) from
-    seed 0, against the float64 restatement of _ref_attention."""
+    seed 0, against the float64 restatement of _ref_attention.  Runs the
+    tcgen05 kernel with tf32 operands (10-bit mantissa, fp32 accumulate and
+    softmax); north-star tolerance rtol = atol = 1e-2."""
     import b200kern as bk
     torch.manual_seed(0)
     q = torch.randn(2, 8, 1024, 64, dtype=torch.float32)
@@ -125,7 +157,7 @@ def test_fa_c0_config(cuda):
     v = torch.randn(2, 8, 1024, 64, dtype=torch.float32)
     o = bk.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), causal=True, scale=0.125)
     ref = oatt.attention(q.double().numpy(), k.double().numpy(), v.double().numpy(), causal=True, scale=0.125)
-    np.testing.assert_allclose(o.double().cpu().numpy(), ref, rtol=1e-3, atol=1e-3)
+    np.testing.assert_allclose(o.double().cpu().numpy(), ref, rtol=1e-2, atol=1e-2)
 
 
 def _ref_window(q, k, v, window):

@@ -27,10 +27,25 @@
 namespace b2 {
 namespace fa {
 
-constexpr int BQ = 128, BKV = 128, HD = 128;
-constexpr int kTile = BQ * HD * 2;   // 32 KB: a 128 x 128 bf16 tile (two 64-col swizzle atoms)
-constexpr int kAtom = kTile / 2;     // 16 KB
+constexpr int BQ = 128, BKV = 128;
 constexpr int kKStages = 3, kVStages = 2;
+constexpr int kF16 = 0, kBF16 = 1, kTF32 = 2;  // operand formats (tcgen05 instruction descriptor codes)
+
+// Tile geometry of the tcgen05 path for head dim HD and operand format FMT
+// (kTF32: fp32 q / k / v read as tf32, fp32 output).  A tile is BQ rows of HD
+// elements in 128-byte swizzle atoms; one MMA k-step is 32 bytes of K.
+template <int HD_, int FMT_>
+struct FaCfg {
+  static constexpr int HD = HD_, FMT = FMT_;
+  static constexpr int ES = FMT == kTF32 ? 4 : 2;   // element bytes
+  static constexpr int KSTEP = 32 / ES;             // K elements per MMA
+  static constexpr int AE = 128 / ES;               // elements per swizzle row
+  static constexpr int NATOM = HD / AE;
+  static constexpr int kAtom = BQ * 128;            // bytes of one atom column
+  static constexpr int kTile = NATOM * kAtom;
+  static constexpr size_t kSmem = (size_t)kTile * (2 + kKStages + kVStages) + 1024 + 256;
+  static_assert(HD % AE == 0, "head dim must fill whole swizzle rows");
+};
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
@@ -38,7 +53,7 @@ struct Params {
   int B, Hq, Hkv, Sq, Skv, causal, q_tiles;
   int window;  // > 0 (causal only): key kv visible to qpos iff qpos - window < kv <= qpos
   float scale_log2;
-  __nv_bfloat16* o;
+  void* o;
   int64_t os_b, os_h, os_s;
   unsigned* err;
 };
@@ -102,15 +117,43 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
 //          8-11 softmax tile 1 (warp w reads TMEM lanes 32 (w % 4) ..).
 // ---------------------------------------------------------------------------
 constexpr int kThreads2 = 384;
-constexpr size_t kSmem2 = (size_t)kTile * (2 + kKStages + kVStages) + 1024 + 256;
 
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+// D[tmem] (+)= A[tmem] * B[smem]; kind::f16 or kind::tf32 by FMT
+template <int FMT>
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  if constexpr (FMT == kTF32) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+// D[tmem] (+)= A[smem] * B[smem]^T; kind::f16 or kind::tf32 by FMT
+template <int FMT>
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  if constexpr (FMT == kTF32) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    tc::mma_f16_ss(d_tmem, a_desc, b_desc, idesc, accumulate);
+  }
+}
+// instruction descriptor: fp32 accumulate, A / B format FMT (0 f16, 1 bf16, 2 tf32)
+__host__ __device__ constexpr uint32_t idesc_fmt(int M, int N, int fmt, bool b_mn_major) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -123,7 +166,7 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
 }
 
 // Row max of the raw S row (this thread's TMEM lane), masked keys -> -inf.
-template <bool MASK, bool F16>
+template <bool MASK>
 __device__ __forceinline__ float row_max(uint32_t tS, int kv0, int qpos, const Params& p) {
   float mx = -INFINITY;
 #pragma unroll 1
@@ -144,9 +187,9 @@ __device__ __forceinline__ float row_max(uint32_t tS, int kv0, int qpos, const P
   return mx;
 }
 
-// p = exp2(s * scale_log2 - m) written as 16-bit pairs over the S columns
-// (P for the TMEM-A MMA); returns the row sum of p.
-template <bool MASK, bool F16>
+// p = exp2(s * scale_log2 - m) written over the S columns (P for the TMEM-A
+// MMA): 16-bit pairs, or fp32 for the tf32 path; returns the row sum of p.
+template <bool MASK, int FMT>
 __device__ __forceinline__ float exp_to_p(uint32_t tS, int kv0, int qpos, float mref, const Params& p) {
   float rs0 = 0.f, rs1 = 0.f;
   const float sc = p.scale_log2;
@@ -168,23 +211,29 @@ __device__ __forceinline__ float exp_to_p(uint32_t tS, int kv0, int qpos, float 
       }
       rs0 += p0;
       rs1 += p1;
-      if constexpr (F16) {
+      if constexpr (FMT == kF16) {
         __half2 hv = __floats2half2_rn(p0, p1);
         pk[e] = *reinterpret_cast<uint32_t*>(&hv);
-      } else {
+      } else if constexpr (FMT == kBF16) {
         __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
         pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+      } else {
+        sv[2 * e] = __float_as_uint(p0);
+        sv[2 * e + 1] = __float_as_uint(p1);
       }
     }
-    tmem_st_32x32b_x16(tS + 16 * c, pk);
+    if constexpr (FMT == kTF32) tmem_st_32x32b_x32(tS + 32 * c, sv);
+    else tmem_st_32x32b_x16(tS + 16 * c, pk);
   }
   return rs0 + rs1;
 }
 
-template <bool F16>
+template <int HD, int FMT>
 __global__ void __launch_bounds__(kThreads2, 1)
 fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using Cf = FaCfg<HD, FMT>;
+  constexpr int kTile = Cf::kTile, kAtom = Cf::kAtom;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;                      // 2 tiles
@@ -255,21 +304,22 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (lane == 0) {
       const int ntiles = nkv[1] > 0 ? 2 : 1;
       mbar_arrive_expect_tx(q_full, ntiles * kTile);
-      for (int u = 0; u < ntiles; ++u) {
-        tma_load_4d(sQ + u * kTile, &tmQ, 0, q0[u], h, b, q_full);
-        tma_load_4d(sQ + u * kTile + kAtom, &tmQ, 64, q0[u], h, b, q_full);
-      }
+      for (int u = 0; u < ntiles; ++u)
+#pragma unroll
+        for (int a = 0; a < Cf::NATOM; ++a) tma_load_4d(sQ + u * kTile + a * kAtom, &tmQ, a * Cf::AE, q0[u], h, b, q_full);
       int kst = 0, vst = 0;
       uint32_t kph = 0, vph = 0;
       for (int j = jb; j < nkv_max; ++j) {
         if (!wait_abort(&k_empty[kst], kph ^ 1, p.err, 0xB2300001u, abort_flag)) break;
         mbar_arrive_expect_tx(&k_full[kst], kTile);
-        tma_load_4d(sK + kst * kTile, &tmK, 0, j * BKV, hk, b, &k_full[kst]);
-        tma_load_4d(sK + kst * kTile + kAtom, &tmK, 64, j * BKV, hk, b, &k_full[kst]);
+#pragma unroll
+        for (int a = 0; a < Cf::NATOM; ++a)
+          tma_load_4d(sK + kst * kTile + a * kAtom, &tmK, a * Cf::AE, j * BKV, hk, b, &k_full[kst]);
         if (!wait_abort(&v_empty[vst], vph ^ 1, p.err, 0xB2300002u, abort_flag)) break;
         mbar_arrive_expect_tx(&v_full[vst], kTile);
-        tma_load_4d(sV + vst * kTile, &tmV, 0, j * BKV, hk, b, &v_full[vst]);
-        tma_load_4d(sV + vst * kTile + kAtom, &tmV, 64, j * BKV, hk, b, &v_full[vst]);
+#pragma unroll
+        for (int a = 0; a < Cf::NATOM; ++a)
+          tma_load_4d(sV + vst * kTile + a * kAtom, &tmV, a * Cf::AE, j * BKV, hk, b, &v_full[vst]);
         if (++kst == kKStages) { kst = 0; kph ^= 1; }
         if (++vst == kVStages) { vst = 0; vph ^= 1; }
       }
@@ -277,17 +327,17 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   } else if (warp == 1) {
     // ---------------------------------- MMA ----------------------------------
     if (lane == 0) {
-      constexpr uint32_t idS = tc::idesc_f16(BQ, BKV, !F16);
-      constexpr uint32_t idPV = tc::idesc_f16(BQ, HD, !F16, false, true);
+      constexpr uint32_t idS = idesc_fmt(BQ, BKV, FMT, false);
+      constexpr uint32_t idPV = idesc_fmt(BQ, HD, FMT, true);
       bool ok = wait_abort(q_full, 0, p.err, 0xB2300003u, abort_flag);
       int kst = 0, vst = 0;
       uint32_t kph = 0, vph = 0;
       auto issue_s = [&](int u) {
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
+        for (int kk = 0; kk < HD / Cf::KSTEP; ++kk) {
           const uint64_t da = tc::desc_kmajor_sw128(sQ + u * kTile + (kk >> 2) * kAtom + (kk & 3) * 32);
           const uint64_t db = tc::desc_kmajor_sw128(sK + kst * kTile + (kk >> 2) * kAtom + (kk & 3) * 32);
-          tc::mma_f16_ss(tmem + 256 * u, da, db, idS, kk != 0);
+          mma_ss<FMT>(tmem + 256 * u, da, db, idS, kk != 0);
         }
         tc::commit(&s_full[u]);
       };
@@ -317,9 +367,11 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             tc::fence_after_sync();
 #pragma unroll
-            for (int kk = 0; kk < BKV / 16; ++kk) {
-              const uint64_t db = tc::smem_desc(sV + vst * kTile + kk * 16 * 128, kAtom, 1024, tc::kSwizzle128B);
-              mma_f16_ts(tmem + 256 * u + 128, tmem + 256 * u + kk * 8, db, idPV, (j != kb[u]) || kk != 0);
+            // one k-step = KSTEP keys: KSTEP rows of V, 8 TMEM columns of P
+            for (int kk = 0; kk < BKV / Cf::KSTEP; ++kk) {
+              const uint64_t db =
+                  tc::smem_desc(sV + vst * kTile + kk * Cf::KSTEP * 128, kAtom, 1024, tc::kSwizzle128B);
+              mma_ts<FMT>(tmem + 256 * u + 128, tmem + 256 * u + kk * 8, db, idPV, (j != kb[u]) || kk != 0);
             }
             if (j == nkv[u] - 1) tc::commit(&o_done[u]);
           }
@@ -368,7 +420,7 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       const bool need_mask = (p.causal && kv0 + BKV - 1 > q0[u]) || kv0 + BKV > p.Skv ||
                              (p.window > 0 && kv0 <= q0[u] + BQ - 1 - p.window);
       // pass 1: row max of the raw scores (scale > 0 commutes with max)
-      float mx = need_mask ? row_max<true, F16>(tS, kv0, qpos, p) : row_max<false, F16>(tS, kv0, qpos, p);
+      float mx = need_mask ? row_max<true>(tS, kv0, qpos, p) : row_max<false>(tS, kv0, qpos, p);
       mx *= p.scale_log2;
       // lazy, warp-uniform rescale of O (O_u is quiescent: PV_u(j-1) finished)
       const bool need = mx > m_used + kRescaleThreshold;
@@ -379,7 +431,7 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       }
       if (__any_sync(0xffffffffu, need) && j > kb[u]) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
           tc::tmem_ld_32x32b_x32(tO + 32 * c, o);
           tc::tmem_ld_wait();
@@ -390,8 +442,8 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       }
       // pass 2: p = exp2(s * scale - m) -> bf16 pairs over the S columns already read
       const float mref = (m_used == -INFINITY) ? 0.f : m_used;
-      const float rs = need_mask ? exp_to_p<true, F16>(tS, kv0, qpos, mref, p)
-                                 : exp_to_p<false, F16>(tS, kv0, qpos, mref, p);
+      const float rs = need_mask ? exp_to_p<true, FMT>(tS, kv0, qpos, mref, p)
+                                 : exp_to_p<false, FMT>(tS, kv0, qpos, mref, p);
       l += rs;
       tmem_st_wait();
       tc::fence_before_sync();
@@ -402,28 +454,36 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (ok && nkv[u] > kb[u] && wait_abort(&o_done[u], 0, p.err, 0xB230000Au, abort_flag)) {
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.o + b * p.os_b + h * p.os_h + (int64_t)qpos * p.os_s;
+      const int64_t orow = b * p.os_b + h * p.os_h + (int64_t)qpos * p.os_s;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
         tc::tmem_ld_32x32b_x32(tO + 32 * c, o);
         tc::tmem_ld_wait();
         if (qpos < p.Sq) {
-          uint32_t pk[16];
+          if constexpr (FMT == kTF32) {
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + orow + 32 * c);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float a = __uint_as_float(o[2 * e]) * inv, bb = __uint_as_float(o[2 * e + 1]) * inv;
-            if constexpr (F16) {
-              __half2 hv = __floats2half2_rn(a, bb);
-              pk[e] = *reinterpret_cast<uint32_t*>(&hv);
-            } else {
-              __nv_bfloat162 hv = __floats2bfloat162_rn(a, bb);
-              pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+            for (int e = 0; e < 8; ++e)
+              dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
+                                   __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+          } else {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float a = __uint_as_float(o[2 * e]) * inv, bb = __uint_as_float(o[2 * e + 1]) * inv;
+              if constexpr (FMT == kF16) {
+                __half2 hv = __floats2half2_rn(a, bb);
+                pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+              } else {
+                __nv_bfloat162 hv = __floats2bfloat162_rn(a, bb);
+                pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+              }
             }
-          }
-          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.o) + orow + 32 * c);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+          }
         }
       }
     }
@@ -517,7 +577,9 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(const GenParams p) {
 
 }  // namespace fa
 
-static bool make_tmap_4d(CUtensorMap* map, const void* base, bool f16, int64_t D, int64_t S, int64_t H, int64_t B,
+// dims (d, s, h, b), element strides (b, h, s); box = one swizzle row
+// (box_d elements = 128 bytes) x 128 rows.
+static bool make_tmap_4d(CUtensorMap* map, const void* base, int dtype, int64_t D, int64_t S, int64_t H, int64_t B,
                          const int64_t* strides_elems) {
   // dims (d, s, h, b); strides in bytes for s, h, b
   typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -533,16 +595,32 @@ static bool make_tmap_4d(CUtensorMap* map, const void* base, bool f16, int64_t D
     fn = reinterpret_cast<EncodeFn>(p);
   }
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)strides_elems[2] * 2, (cuuint64_t)strides_elems[1] * 2,
-                                 (cuuint64_t)strides_elems[0] * 2};
-  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint64_t es = dtype == B2_F32 ? 4 : 2;
+  const cuuint64_t strides[3] = {(cuuint64_t)strides_elems[2] * es, (cuuint64_t)strides_elems[1] * es,
+                                 (cuuint64_t)strides_elems[0] * es};
+  const cuuint32_t box[4] = {(cuuint32_t)(128 / es), 128, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
+  const CUtensorMapDataType dt = dtype == B2_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == B2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return fn(map, dt, 4, const_cast<void*>(base),
             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static bool strides_ok16(const int64_t* s) { return s[0] % 8 == 0 && s[1] % 8 == 0 && s[2] % 8 == 0; }
+// element strides whose byte values are multiples of 16 (TMA)
+static bool strides_ok(const int64_t* s, int dtype) {
+  const int64_t m = dtype == B2_F32 ? 4 : 8;
+  return s[0] % m == 0 && s[1] % m == 0 && s[2] % m == 0;
+}
+
+template <int HD, int FMT>
+static void launch_fa_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fa::Params& p,
+                         dim3 grid, cudaStream_t st) {
+  using Cf = fa::FaCfg<HD, FMT>;
+  set_max_smem((const void*)fa::fa_fwd2_kernel<HD, FMT>, (int)Cf::kSmem);
+  fa::fa_fwd2_kernel<HD, FMT><<<grid, fa::kThreads2, Cf::kSmem, st>>>(tq, tk, tv, p);
+}
 
 }  // namespace b2
 
@@ -594,15 +672,17 @@ static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int
   B2_CHECK_ARG(D <= 256, B2_ERR_UNSUPPORTED, "flash_attn_fwd: D=%lld > 256", (long long)D);
   if (Sq == 0) return B2_OK;
   cudaStream_t st = (cudaStream_t)stream;
-  const bool fast = D == fa::HD && dtype != B2_F32 && Skv > 0 && strides_ok16(qs) && strides_ok16(ks) &&
-                    strides_ok16(vs) && strides_ok16(os) && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) &&
-                    aligned(o, 16) && B <= 65535 && Hq <= 65535;
+  // tcgen05 path: D = 128 with 16-bit operands, D = 64 with 16-bit operands or
+  // fp32 (read as tf32, fp32 output); TMA-able strides and base addresses
+  const bool shape_ok = (D == 128 && dtype != B2_F32) || D == 64;
+  const bool fast = shape_ok && Skv > 0 && strides_ok(qs, dtype) && strides_ok(ks, dtype) && strides_ok(vs, dtype) &&
+                    strides_ok(os, dtype) && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(o, 16) &&
+                    B <= 65535 && Hq <= 65535;
   if (fast) {
     unsigned* err = device_error_word();
     CUtensorMap tq, tk, tv;
-    const bool f16 = dtype == B2_F16;
-    if (err && make_tmap_4d(&tq, q, f16, D, Sq, Hq, B, qs) && make_tmap_4d(&tk, k, f16, D, Skv, Hkv, B, ks) &&
-        make_tmap_4d(&tv, v, f16, D, Skv, Hkv, B, vs)) {
+    if (err && make_tmap_4d(&tq, q, dtype, D, Sq, Hq, B, qs) && make_tmap_4d(&tk, k, dtype, D, Skv, Hkv, B, ks) &&
+        make_tmap_4d(&tv, v, dtype, D, Skv, Hkv, B, vs)) {
       fa::Params p;
       p.B = (int)B;
       p.Hq = (int)Hq;
@@ -613,18 +693,19 @@ static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int
       p.window = window;
       p.q_tiles = (int)((Sq + fa::BQ - 1) / fa::BQ);
       p.scale_log2 = scale * fa::kLog2e;
-      p.o = (__nv_bfloat16*)o;
+      p.o = o;
       p.os_b = os[0];
       p.os_h = os[1];
       p.os_s = os[2];
       p.err = err;
       dim3 grid((p.q_tiles + 1) / 2, (unsigned)Hq, (unsigned)B);
-      if (f16) {
-        set_max_smem((const void*)fa::fa_fwd2_kernel<true>, (int)fa::kSmem2);
-        fa::fa_fwd2_kernel<true><<<grid, fa::kThreads2, fa::kSmem2, st>>>(tq, tk, tv, p);
+      if (D == 128) {
+        if (dtype == B2_F16) launch_fa_tc<128, fa::kF16>(tq, tk, tv, p, grid, st);
+        else launch_fa_tc<128, fa::kBF16>(tq, tk, tv, p, grid, st);
       } else {
-        set_max_smem((const void*)fa::fa_fwd2_kernel<false>, (int)fa::kSmem2);
-        fa::fa_fwd2_kernel<false><<<grid, fa::kThreads2, fa::kSmem2, st>>>(tq, tk, tv, p);
+        if (dtype == B2_F16) launch_fa_tc<64, fa::kF16>(tq, tk, tv, p, grid, st);
+        else if (dtype == B2_BF16) launch_fa_tc<64, fa::kBF16>(tq, tk, tv, p, grid, st);
+        else launch_fa_tc<64, fa::kTF32>(tq, tk, tv, p, grid, st);
       }
       return launch_status("fa_fwd");
     }
