@@ -367,10 +367,14 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             tc::fence_after_sync();
 #pragma unroll
-            // one k-step = KSTEP keys: KSTEP rows of V, 8 TMEM columns of P
+            // one k-step = KSTEP keys: KSTEP rows of V, 8 TMEM columns of P.
+            // V is the MN-major B operand: 128-byte rows along d, atoms of
+            // 8 rows (16-bit, 128B swizzle) or of 4 rows (tf32, 128B swizzle
+            // with 32-byte atomicity, descriptor layout 1) stacked along K.
             for (int kk = 0; kk < BKV / Cf::KSTEP; ++kk) {
               const uint64_t db =
-                  tc::smem_desc(sV + vst * kTile + kk * Cf::KSTEP * 128, kAtom, 1024, tc::kSwizzle128B);
+                  FMT == kTF32 ? tc::smem_desc(sV + vst * kTile + kk * Cf::KSTEP * 128, kAtom, 512, 1)
+                               : tc::smem_desc(sV + vst * kTile + kk * Cf::KSTEP * 128, kAtom, 1024, tc::kSwizzle128B);
               mma_ts<FMT>(tmem + 256 * u + 128, tmem + 256 * u + kk * 8, db, idPV, (j != kb[u]) || kk != 0);
             }
             if (j == nkv[u] - 1) tc::commit(&o_done[u]);
@@ -579,8 +583,10 @@ __global__ void __launch_bounds__(128) fa_generic_kernel(const GenParams p) {
 
 // dims (d, s, h, b), element strides (b, h, s); box = one swizzle row
 // (box_d elements = 128 bytes) x 128 rows.
+// mn_major_tf32: the 128-byte swizzle with 32-byte atomicity that the MMA's
+// MN-major tf32 operand layout (SWIZZLE_128B_BASE32B) expects (V of the tf32 path).
 static bool make_tmap_4d(CUtensorMap* map, const void* base, int dtype, int64_t D, int64_t S, int64_t H, int64_t B,
-                         const int64_t* strides_elems) {
+                         const int64_t* strides_elems, bool mn_major_tf32 = false) {
   // dims (d, s, h, b); strides in bytes for s, h, b
   typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -604,7 +610,8 @@ static bool make_tmap_4d(CUtensorMap* map, const void* base, int dtype, int64_t 
                                  : dtype == B2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   return fn(map, dt, 4, const_cast<void*>(base),
-            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            mn_major_tf32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -682,7 +689,7 @@ static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int
     unsigned* err = device_error_word();
     CUtensorMap tq, tk, tv;
     if (err && make_tmap_4d(&tq, q, dtype, D, Sq, Hq, B, qs) && make_tmap_4d(&tk, k, dtype, D, Skv, Hkv, B, ks) &&
-        make_tmap_4d(&tv, v, dtype, D, Skv, Hkv, B, vs)) {
+        make_tmap_4d(&tv, v, dtype, D, Skv, Hkv, B, vs, dtype == B2_F32)) {
       fa::Params p;
       p.B = (int)B;
       p.Hq = (int)Hq;

@@ -29,26 +29,36 @@
 // ever leaves the SM.
 #include "b2_common.cuh"
 #include "tc_common.cuh"
+#include <type_traits>
 
 namespace b2 {
 namespace kda {
 
 constexpr int C = 64, DK = 128, DV = 128;
 
-// Workspace block per (b, h, chunk), in floats: fp16 W, U, scale Q e^G and
-// K e^{G_last - G} [64][128], fp16 A_qk [64][64], fp32 e^{G_last} [128]
-// (74,240 bytes).  The fp16 tiles only feed 10-bit-mantissa MMA operands and
-// are O(1); the state itself is carried in fp32 registers.
-constexpr size_t kWsW = 0;
-constexpr size_t kWsU = kWsW + (size_t)C * DK / 2;
-constexpr size_t kWsQg = kWsU + (size_t)C * DV / 2;
-constexpr size_t kWsKr = kWsQg + (size_t)C * DK / 2;
-constexpr size_t kWsAq = kWsKr + (size_t)C * DK / 2;
-constexpr size_t kWsGl = kWsAq + (size_t)C * C / 2;
-constexpr size_t kWsBlock = kWsGl + DK;
-__device__ __forceinline__ __half* ws_h(float* blk, size_t off) { return reinterpret_cast<__half*>(blk + off); }
-__device__ __forceinline__ const __half* ws_h(const float* blk, size_t off) {
-  return reinterpret_cast<const __half*>(blk + off);
+// Workspace block per (b, h, chunk), laid out exactly as kernel B's shared
+// memory stage so that one bulk copy moves it: fp16 W, K e^{G_last - G} and
+// scale Q e^G [64][136] (rows padded by 8 halves: ldmatrix rows on distinct
+// banks), fp16 A_qk [64][72], fp32 e^{G_last} [128], then fp16 U for state
+// columns 0-63 and 64-127 as two [64][72] tiles.  80,384 bytes.  The fp16
+// tiles only feed 10-bit-mantissa MMA operands and are O(1); the state itself
+// is carried in fp32 registers.
+constexpr int LR = DK + 8;    // halves: W, Kr, Qg rows
+constexpr int LA = C + 8;     // halves: A_qk rows
+constexpr int LUS = 64 + 8;   // halves: rows of one 64-column U tile
+constexpr uint32_t kBW = 0;
+constexpr uint32_t kBKr = kBW + C * LR * 2;
+constexpr uint32_t kBQg = kBKr + C * LR * 2;
+constexpr uint32_t kBAq = kBQg + C * LR * 2;
+constexpr uint32_t kBGl = kBAq + C * LA * 2;
+constexpr uint32_t kBShared = kBGl + DK * 4;   // bytes every CTA of the head reads
+constexpr uint32_t kBUTile = C * LUS * 2;      // one U tile
+constexpr uint32_t kBU = kBShared;             // U tile h at kBU + h * kBUTile
+constexpr uint32_t kWsBlockBytes = kBU + 2 * kBUTile;
+constexpr size_t kWsBlock = kWsBlockBytes / 4;  // floats
+static_assert(kBShared % 16 == 0 && kBUTile % 16 == 0, "bulk copy sizes");
+__device__ __forceinline__ __half* ws_h(float* blk, uint32_t byte_off) {
+  return reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(blk) + byte_off);
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -125,11 +135,20 @@ __device__ __forceinline__ uint32_t bf2(float lo, float hi) {
 __device__ __forceinline__ void st_u32(uint8_t* base, uint32_t off, uint32_t v) {
   *reinterpret_cast<uint32_t*>(base + off) = v;
 }
+// a pair of elements kept packed in registers until used (16-bit: one word)
 template <typename T>
-__device__ __forceinline__ float2 ld2(const T* p) {
-  if constexpr (sizeof(T) == 4) return *reinterpret_cast<const float2*>(p);
-  else return make_float2(to_f32<T>(p[0]), to_f32<T>(p[1]));
-}
+struct Pair {
+  using R = typename std::conditional<sizeof(T) == 4, float2, uint32_t>::type;
+  static __device__ __forceinline__ R load(const T* p) { return *reinterpret_cast<const R*>(p); }
+  static __device__ __forceinline__ float2 f2(R r) {
+    if constexpr (sizeof(T) == 4) {
+      return r;
+    } else {
+      const T* h = reinterpret_cast<const T*>(&r);
+      return make_float2(to_f32<T>(h[0]), to_f32<T>(h[1]));
+    }
+  }
+};
 __device__ __forceinline__ float fexp(float x) { return __expf(x); }
 }  // namespace prep
 
@@ -168,9 +187,18 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   if (tid < C) sBeta[tid] = to_f32<T>(beta[row0 + (int64_t)tid * H]);
 
   // ---- 1. G: prefix inside the block, then the preceding blocks' totals ----
+  // every global load of this thread's rows first, so that their latencies overlap
+  using P2 = Pair<T>;
+  typename P2::R kraw[16], qraw[16], vraw[16];
   float2 G[16];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) G[r] = *reinterpret_cast<const float2*>(g + (row0 + (int64_t)(r0 + r) * H) * DK + d0);
+  for (int r = 0; r < 16; ++r) {
+    const int64_t gi = (row0 + (int64_t)(r0 + r) * H) * DK + d0;
+    G[r] = *reinterpret_cast<const float2*>(g + gi);
+    kraw[r] = P2::load(k + gi);
+    qraw[r] = P2::load(q + gi);
+    vraw[r] = P2::load(v + gi);
+  }
 #pragma unroll
   for (int r = 1; r < 16; ++r) {
     G[r].x += G[r - 1].x;
@@ -231,17 +259,15 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const int ib = (I == 3 || I == 1) ? 0 : 64;
   // j-side diagonal rows of this block in its A operand
   const int jd = I == 3 ? 48 : (I == 2 ? 96 : (I == 1 ? 16 : 32));
-  __half* wsQg = ws_h(blk, kWsQg);
-  __half* wsKr = ws_h(blk, kWsKr);
+  __half* wsQg = ws_h(blk, kBQg);
+  __half* wsKr = ws_h(blk, kBKr);
   float2 wk[16];  // beta K e^G for the W operand, this thread's rows
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
     const int t = r0 + r;
-    const int64_t gi = (row0 + (int64_t)t * H) * DK + d0;
-    const float2 kk = ld2(k + gi);
-    float2 sq = ld2(q + gi);
-    sq.x *= scale;
-    sq.y *= scale;
+    const float2 kk = P2::f2(kraw[r]);
+    const float2 q2 = P2::f2(qraw[r]);
+    const float2 sq = make_float2(q2.x * scale, q2.y * scale);
     const float2 e0 = make_float2(fexp(G[r].x - Gr0.x), fexp(G[r].y - Gr0.y));
     const float2 ej = make_float2(fexp(Gnx.x - G[r].x), fexp(Gnx.y - G[r].y));
     const float2 lo = make_float2(kk.x * e0.x, kk.y * e0.y);
@@ -269,8 +295,8 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       else st_u32(sm + kAB, sw_off(t, d0, 128), v2);
     }
     // workspace outputs of this row
-    *reinterpret_cast<__half2*>(wsQg + t * DK + d0) = __floats2half2_rn(lq.x * eG0.x, lq.y * eG0.y);
-    *reinterpret_cast<__half2*>(wsKr + t * DK + d0) = __floats2half2_rn(kj.x * cKr.x, kj.y * cKr.y);
+    *reinterpret_cast<__half2*>(wsQg + t * LR + d0) = __floats2half2_rn(lq.x * eG0.x, lq.y * eG0.y);
+    *reinterpret_cast<__half2*>(wsKr + t * LR + d0) = __floats2half2_rn(kj.x * cKr.x, kj.y * cKr.y);
     const float bt = sBeta[t];
     wk[r] = make_float2(bt * lo.x * eG0.x, bt * lo.y * eG0.y);
   }
@@ -293,7 +319,7 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       const float bt = sBeta[r0 + r];
-      const float2 vv = ld2(v + (row0 + (int64_t)(r0 + r) * H) * DV + d0);
+      const float2 vv = P2::f2(vraw[r]);
       wk[r] = make_float2(bt * vv.x, bt * vv.y);
     }
 #pragma unroll
@@ -311,7 +337,7 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   }
   if (tid < DK / 2) {  // e^{G_last}: block 3 holds row 63
     // (any thread has Gl for its pair)
-    *reinterpret_cast<float2*>(blk + kWsGl + d0) = make_float2(fexp(Gl.x), fexp(Gl.y));
+    *reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(blk) + kBGl + 4 * d0) = make_float2(fexp(Gl.x), fexp(Gl.y));
   }
   tc::fence_proxy_async_smem();
   tc::fence_before_sync();
@@ -439,10 +465,10 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 
   // ---- 6. A_qk -> workspace (fp16, zeros above the diagonal) ----
   {
-    __half* wsAq = ws_h(blk, kWsAq);
+    __half* wsAq = ws_h(blk, kBAq);
     for (int e = tid; e < C * C / 2; e += kThreads) {
       const int r = (2 * e) / C, c2 = (2 * e) % C;
-      *reinterpret_cast<__half2*>(wsAq + 2 * e) = __floats2half2_rn(sAq[r * LT + c2], sAq[r * LT + c2 + 1]);
+      *reinterpret_cast<__half2*>(wsAq + r * LA + c2) = __floats2half2_rn(sAq[r * LT + c2], sAq[r * LT + c2 + 1]);
     }
   }
   // ---- 7. T = (I + A_kk)^-1: diagonal 16 x 16 blocks, column by column ----
@@ -516,13 +542,15 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     const int qd = warp & 3, half = warp >> 2;
     const int d = 32 * qd + lane;
     uint32_t va[32];
-    __half* dst = ws_h(blk, half ? kWsU : kWsW);
+    // W [t][d] rows of LR; U [t][d % 64] in the tile of its 64 state columns
+    __half* dst = half ? ws_h(blk, kBU + (d >> 6) * kBUTile) + (d & 63) : ws_h(blk, kBW) + d;
+    const int ld = half ? LUS : LR;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(qd * 32) << 16) + 64u * half + 32u * c, va);
       tc::tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) dst[(32 * c + i) * DK + d] = __float2half_rn(__uint_as_float(va[i]));
+      for (int i = 0; i < 32; ++i) dst[(32 * c + i) * ld] = __float2half_rn(__uint_as_float(va[i]));
     }
   }
   tc::fence_before_sync();
@@ -553,38 +581,30 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 constexpr int RW = 4;                 // warps per CTA
 constexpr int RV = 16 * RW;           // state columns per CTA
 constexpr int kRThreads = 32 * RW;
-constexpr int LR = DK + 8;            // halves: W, Kr, Qg rows (ldmatrix rows on distinct banks)
-constexpr int LA = C + 8;             // halves: A_qk rows
-constexpr int LUS = RV + 8;           // halves: U slice rows
-constexpr int kRW = 0;                // stage offsets in halves
-constexpr int kRKr = kRW + C * LR;
-constexpr int kRQg = kRKr + C * LR;
-constexpr int kRAq = kRQg + C * LR;
-constexpr int kRU = kRAq + C * LA;
-constexpr int kRStageHalves = kRU + C * LUS;
-constexpr int kRStageBytes = kRStageHalves * 2 + DK * 4;  // + e^{G_last} (fp32)
-constexpr int LO = RV + 4;                                // floats: output staging rows
-constexpr size_t kRSmem = 2 * (size_t)kRStageBytes + (size_t)C * LO * 4;
-static_assert(kRStageBytes % 16 == 0, "stage alignment");
+static_assert(RV == 64, "a CTA reads one 64-column U tile of the workspace");
+// stage = the head's shared tiles (W, Kr, Qg, A_qk, e^{G_last}) + this CTA's U tile
+constexpr uint32_t kRStageBytes = kBShared + kBUTile;
+constexpr int LO = RV + 8;  // output staging row stride (elements)
+template <typename T>
+struct RecurCfg {
+  // three stages for 16-bit outputs; fp32 outputs need the room for a fp32 staging tile
+  static constexpr int kStages = sizeof(T) == 2 ? 3 : 2;
+  static constexpr uint32_t kStaging = (uint32_t)C * LO * sizeof(T);
+  static constexpr size_t kSmem = (size_t)kStages * kRStageBytes + kStaging + 64;
+};
 
-__device__ __forceinline__ void r_load_stage(unsigned char* st, const float* blk, int v0, int tid) {
-  __half* s = reinterpret_cast<__half*>(st);
-  float* sGl = reinterpret_cast<float*>(st + kRStageHalves * 2);
-  for (int e = tid; e < C * DK / 8; e += kRThreads) {
-    const int r = e / (DK / 8), c8 = e % (DK / 8);
-    cp_async16(s + kRW + r * LR + 8 * c8, ws_h(blk, kWsW) + r * DK + 8 * c8);
-    cp_async16(s + kRKr + r * LR + 8 * c8, ws_h(blk, kWsKr) + r * DK + 8 * c8);
-    cp_async16(s + kRQg + r * LR + 8 * c8, ws_h(blk, kWsQg) + r * DK + 8 * c8);
-  }
-  for (int e = tid; e < C * C / 8; e += kRThreads) {
-    const int r = e / (C / 8), c8 = e % (C / 8);
-    cp_async16(s + kRAq + r * LA + 8 * c8, ws_h(blk, kWsAq) + r * C + 8 * c8);
-  }
-  for (int e = tid; e < C * RV / 8; e += kRThreads) {
-    const int r = e / (RV / 8), c8 = e % (RV / 8);
-    cp_async16(s + kRU + r * LUS + 8 * c8, ws_h(blk, kWsU) + r * DV + v0 + 8 * c8);
-  }
-  if (tid < DK / 4) cp_async16(sGl + 4 * tid, blk + kWsGl + 4 * tid);
+// bulk copy global -> shared (no multicast), completion on an mbarrier
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void r_load_stage(uint8_t* st, const uint8_t* blk, int utile, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, kRStageBytes);
+  bulk_g2s(st, blk, kBShared, bar);
+  bulk_g2s(st + kBShared, blk + kBU + utile * kBUTile, kBUTile, bar);
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
@@ -606,31 +626,30 @@ __device__ __forceinline__ float2 unpack_h2(uint32_t u) {
 }
 
 template <typename T>
-__device__ __forceinline__ void store4(T* dst, float4 v) {
-  if constexpr (sizeof(T) == 4) {
-    *reinterpret_cast<float4*>(dst) = v;
-  } else {
-    T h[4] = {from_f32<T>(v.x), from_f32<T>(v.y), from_f32<T>(v.z), from_f32<T>(v.w)};
-    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(h);
-  }
-}
-
-template <typename T>
 __global__ void __launch_bounds__(kRThreads, 1)
 kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ s_out,
-                 T* __restrict__ o, int B, int Tlen, int H) {
-  extern __shared__ __align__(16) unsigned char smb[];
-  float* sO = reinterpret_cast<float*>(smb + 2 * kRStageBytes);
+                 T* __restrict__ o, int B, int Tlen, int H, unsigned* __restrict__ err) {
+  using Cf = RecurCfg<T>;
+  constexpr int NST = Cf::kStages;
+  extern __shared__ __align__(128) uint8_t smb[];
+  T* sO = reinterpret_cast<T*>(smb + NST * kRStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smb + NST * kRStageBytes + Cf::kStaging);
   const int nc = Tlen / C;
   const int v0 = blockIdx.x * RV, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tq = lane & 3, mat = lane >> 3, r8 = lane & 7;
   const int dv0 = v0 + 16 * warp;
-  const float* head = ws + ((size_t)b * H + h) * nc * kWsBlock;
+  const uint8_t* head = reinterpret_cast<const uint8_t*>(ws + ((size_t)b * H + h) * nc * kWsBlock);
   const size_t sbase = ((size_t)b * H + h) * DK * DV;
 
-  r_load_stage(smb, head, v0, tid);
-  cp_async_commit();
+  if (tid == 0) {
+    for (int i = 0; i < NST; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int i = 0; i < NST && i < nc; ++i)
+      r_load_stage(smb + i * kRStageBytes, head + (size_t)i * kWsBlockBytes, blockIdx.x, &full[i]);
 
   // S^T fragments: n-tile nt covers dk 8 nt .. 8 nt + 7; e: (dv g | g + 8) x (dk 2 tq | 2 tq + 1)
   float S[16][4];
@@ -642,23 +661,19 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
       S[nt][e] = s0 ? s0[sbase + (size_t)dk * DV + dv] : 0.f;
     }
 
-  for (int c = 0; c < nc; ++c) {
-    const unsigned char* st = smb + (c & 1) * kRStageBytes;
-    if (c + 1 < nc) {
-      r_load_stage(smb + ((c + 1) & 1) * kRStageBytes, head + (size_t)(c + 1) * kWsBlock, v0, tid);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();  // stage c visible to every warp
-    const __half* sW = reinterpret_cast<const __half*>(st) + kRW;
-    const __half* sKr = reinterpret_cast<const __half*>(st) + kRKr;
-    const __half* sQg = reinterpret_cast<const __half*>(st) + kRQg;
-    const __half* sAq = reinterpret_cast<const __half*>(st) + kRAq;
-    const __half* sU = reinterpret_cast<const __half*>(st) + kRU;
-    const float* sGl = reinterpret_cast<const float*>(st + kRStageHalves * 2);
-
+  bool alive = true;
+  for (int c = 0; c < nc && alive; ++c) {
+    const int sl = c % NST;
+    const uint8_t* st = smb + sl * kRStageBytes;
+    // CTA-uniform verdict, so that no thread leaves the loop while others wait at a barrier
+    alive = __syncthreads_and(mbar_wait(&full[sl], (uint32_t)(c / NST) & 1u, err, 0xB2300003u));
+    if (!alive) break;
+    const __half* sW = reinterpret_cast<const __half*>(st + kBW);
+    const __half* sKr = reinterpret_cast<const __half*>(st + kBKr);
+    const __half* sQg = reinterpret_cast<const __half*>(st + kBQg);
+    const __half* sAq = reinterpret_cast<const __half*>(st + kBAq);
+    const float* sGl = reinterpret_cast<const float*>(st + kBGl);
+    const __half* sU = reinterpret_cast<const __half*>(st + kBShared);
     // S^T as fp16 A fragments, one per 16-wide dk step
     uint32_t sa[8][4];
 #pragma unroll
@@ -752,14 +767,18 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int t = 8 * nt + 2 * tq + (e & 1), dvl = 16 * warp + g + 8 * (e >> 1);
-        sO[t * LO + dvl] = oa[nt][e];
+        sO[t * LO + dvl] = from_f32<T>(oa[nt][e]);
       }
-    __syncthreads();  // staging complete; every warp is done with stage c
-    for (int e = tid; e < C * RV / 4; e += kRThreads) {
-      const int t = e / (RV / 4), c4 = e % (RV / 4);
-      const float4 val = *reinterpret_cast<const float4*>(sO + t * LO + 4 * c4);
-      store4<T>(o + (((int64_t)b * Tlen + (int64_t)c * C + t) * H + h) * DV + v0 + 4 * c4, val);
+    __syncthreads();  // staging complete; every warp is done with stage sl
+    if (tid == 0 && c + NST < nc)
+      r_load_stage(smb + sl * kRStageBytes, head + (size_t)(c + NST) * kWsBlockBytes, blockIdx.x, &full[sl]);
+    constexpr int PER = 16 / sizeof(T);  // elements per 16-byte store
+    for (int e = tid; e < C * RV / PER; e += kRThreads) {
+      const int t = e / (RV / PER), cc = e % (RV / PER);
+      *reinterpret_cast<uint4*>(o + (((int64_t)b * Tlen + (int64_t)c * C + t) * H + h) * DV + v0 + PER * cc) =
+          *reinterpret_cast<const uint4*>(sO + t * LO + PER * cc);
     }
+    __syncthreads();  // staging tile read before the next chunk writes it
   }
   if (s_out) {
 #pragma unroll
@@ -812,11 +831,11 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
 #define B2_KDA_LAUNCH(TY)                                                                                         \
   do {                                                                                                            \
     set_max_smem((const void*)kda::kda_prep_kernel<TY>, (int)kda::prep::kSmem);                                  \
-    set_max_smem((const void*)kda::kda_recur_kernel<TY>, (int)kda::kRSmem);                                      \
+    set_max_smem((const void*)kda::kda_recur_kernel<TY>, (int)kda::RecurCfg<TY>::kSmem);                         \
     kda::kda_prep_kernel<TY><<<ga, kda::prep::kThreads, kda::prep::kSmem, st>>>(                                  \
         (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale, err);   \
-    kda::kda_recur_kernel<TY><<<gb, kda::kRThreads, kda::kRSmem, st>>>(ws, initial_state, final_state, (TY*)o,    \
-                                                                       (int)B, (int)T, (int)H);                 \
+    kda::kda_recur_kernel<TY><<<gb, kda::kRThreads, kda::RecurCfg<TY>::kSmem, st>>>(                             \
+        ws, initial_state, final_state, (TY*)o, (int)B, (int)T, (int)H, err);                                    \
   } while (0)
   if (dtype == B2_BF16) B2_KDA_LAUNCH(__nv_bfloat16);
   else if (dtype == B2_F16) B2_KDA_LAUNCH(__half);
