@@ -1018,21 +1018,21 @@ def strong_record(name, args, rank, world, local, traffic):
            "ms_per_step": round(ms_max / args.steps, 5), "parity_ok": parity_ok, "clocks": clocks,
            "roofline_per_rank": roofline(wl, ms, args.steps, traffic)}
     if name in ("C2", "C2p") and world > 1:
-        import torch.distributed as dist
+        from b200kern.sharding import all_gather_columns_stacked
         gathered = torch.empty(world, *wl.out.shape, dtype=wl.out.dtype, device="cuda")
         stream = torch.cuda.current_stream()
         for _ in range(max(3, args.warmup)):
-            dist.all_gather_into_tensor(gathered, wl.out)
+            all_gather_columns_stacked(wl.out, out=gathered)
         torch.cuda.synchronize()
         barrier(world)
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record(stream)
         for _ in range(args.steps):
-            dist.all_gather_into_tensor(gathered, wl.out)
+            all_gather_columns_stacked(wl.out, out=gathered)
         e1.record(stream)
         for _ in range(args.steps):
             wl.step(stream.cuda_stream)
-            dist.all_gather_into_tensor(gathered, wl.out)
+            all_gather_columns_stacked(wl.out, out=gathered)
         e2.record(stream)
         torch.cuda.synchronize()
         g_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps

@@ -61,6 +61,16 @@ def _worker(rank, world, port, results):
     ok_, _ = okda.recurrent(qh.numpy(), kh.numpy(), vh.numpy(), kg[:, :, h0:h1], kb[:, :, h0:h1])
     ref_k, _ = okda.recurrent(kq, kk, kv, kg, kb)
     ok_kda = np.allclose(ok_, ref_k[:, :, h0:h1], rtol=0, atol=1e-12)
+    # --- equal-width shards: one all_gather_into_tensor, then the [M, N] view ---
+    Ne = 256
+    qe = torch.randint(0, 16, (K, Ne), generator=g)
+    se = torch.rand(K // G, Ne, generator=g) * 0.02 + 1e-3
+    qwe, sse, _, _ = sharding.shard_int4(pack_int4_gptq(qe), se, world=world, rank=rank)
+    parte = torch.from_numpy(oq.int4_matmul(x.numpy(), unpack_int4_gptq(qwe).numpy(), sse.numpy(), None, G))
+    stacked = sharding.all_gather_columns_stacked(parte)
+    ok_st = stacked.shape == (world, M, Ne // world) and np.array_equal(
+        sharding.columns_from_stacked(stacked).numpy(), oq.int4_matmul(x.numpy(), qe.numpy(), se.numpy(), None, G))
+    ok_w4 = ok_w4 and ok_st
     results[rank] = (ok_w4, ok_w8, ok_fa, ok_kda, (a, b))
     dist.barrier()
     dist.destroy_process_group()

@@ -57,3 +57,23 @@ def all_gather_columns(out_shard, group=None):
     parts = [torch.empty_like(pad) for _ in range(world)]
     dist.all_gather(parts, pad, group=group)
     return torch.cat([p[:, : int(w.item())] for p, w in zip(parts, widths)], dim=1)
+
+
+def all_gather_columns_stacked(out_shard, out=None, group=None):
+    """Equal-width column shards [M, N/P] -> [P, M, N/P] on every rank with one
+    all_gather_into_tensor (NCCL over NVLink on GPUs), no padding or copy;
+    columns_from_stacked() gives the [M, N] view when the caller needs it."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if out is None:
+        out = torch.empty((world,) + tuple(out_shard.shape), dtype=out_shard.dtype, device=out_shard.device)
+    # the concatenated [P * M, N/P] form, accepted by every backend
+    dist.all_gather_into_tensor(out.view(world * out_shard.shape[0], -1), out_shard.contiguous(), group=group)
+    return out
+
+
+def columns_from_stacked(stacked):
+    """[P, M, N/P] -> [M, N] (column block r = rank r's shard)."""
+    P, M, W = stacked.shape
+    return stacked.permute(1, 0, 2).reshape(M, P * W)
+
