@@ -250,3 +250,62 @@ def test_no_bounded_wait_ran_out(cuda):
     code = ctypes.c_uint(0)
     st = _lib.load().b2_device_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(code))
     assert st == 0 and code.value == 0, hex(code.value)
+
+
+# ---------------------------------------------------------------------------
+# The reference's own dtype: fp32 activations (|x| up to 1e5, beyond fp16's
+# range), fp32 scales and fractional zeros, fp32 output.  These run the fp32
+# CUDA-core kernels with the reference's arithmetic ((q - z) * s in fp32, fp32
+# products), so the bound is fp32 accumulation error, not a 16-bit rounding:
+# |x - ref| <= 1e-4 (|ref| + rms(ref)) against the float64 oracle.
+# ---------------------------------------------------------------------------
+def _close_f32(out, ref):
+    out = np.asarray(out, dtype=np.float64)
+    err = np.abs(out - ref)
+    bound = 1e-4 * (np.abs(ref) + np.sqrt((ref ** 2).mean()))
+    assert (err <= bound).all(), f"max err {err.max():.4g}, worst ratio {(err / bound).max():.3g}"
+
+
+def _big_x(M, K, g):
+    x = torch.randn(M, K, generator=g) * 2e4
+    x[:, ::97] = 1e5  # magnitudes that overflow fp16
+    return x
+
+
+@pytest.mark.parametrize("layout", ["gptq", "ref"])
+@pytest.mark.parametrize("zeros", [False, True])
+@pytest.mark.parametrize("M,N,K,G", [(1, 1024, 4096, 128), (5, 520, 1024, 64), (16, 256, 512, 128),
+                                     (64, 384, 768, 32)])
+def test_int4_fp32_reference_dtype(cuda, layout, zeros, M, N, K, G):
+    import b200kern as bk
+    g = torch.Generator().manual_seed(M * 7 + N)
+    x = _big_x(M, K, g)
+    q = torch.randint(0, 16, (K, N), generator=g, dtype=torch.int32)
+    s = torch.rand(K // G, N, generator=g) * 0.05 + 1e-3
+    z = torch.rand(K // G, N, generator=g) * 15.0 if zeros else None
+    if layout == "gptq":
+        w = bk.pack_int4_gptq(q)
+        out = bk.int4_matmul(x.to(cuda), w.to(cuda), s.to(cuda), None if z is None else z.to(cuda), group_size=G)
+    else:
+        w = bk.pack_int4_ref(q.t().contiguous())
+        out = bk.int4_matmul(x.to(cuda), w.to(cuda), s.t().contiguous().to(cuda),
+                             None if z is None else z.t().contiguous().to(cuda), group_size=G, layout="ref")
+    assert out.dtype == torch.float32 and tuple(out.shape) == (M, N)
+    ref = oq.int4_matmul(x.double().numpy(), q.numpy(), s.double().numpy(),
+                         None if z is None else z.double().numpy(), G)
+    _close_f32(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("zeros", [False, True])
+@pytest.mark.parametrize("M,N,K", [(1, 1000, 4096), (7, 512, 1024), (33, 256, 640)])
+def test_int8_fp32_reference_dtype(cuda, zeros, M, N, K):
+    import b200kern as bk
+    g = torch.Generator().manual_seed(M + N + K)
+    x = _big_x(M, K, g)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int32).to(torch.int8)
+    s = torch.rand(N, generator=g) * 0.01 + 1e-4
+    z = (torch.rand(N, generator=g) * 2 - 1) if zeros else None
+    out = bk.int8_matmul(x.to(cuda), w.to(cuda), s.to(cuda), None if z is None else z.to(cuda))
+    assert out.dtype == torch.float32
+    ref = oq.int8_matmul(x.double().numpy(), w.numpy(), s.double().numpy(), None if z is None else z.double().numpy())
+    _close_f32(out.cpu().numpy(), ref)

@@ -17,6 +17,7 @@ from . import _lib
 from .errors import B2DtypeError, B2ShapeError
 
 _DT = {torch.float16: 0, torch.bfloat16: 1}
+_DTC = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}  # codes of the C ABI (fp32: reference dtype)
 LAYOUT_GPTQ = "gptq"  # int32 [K/8, N], nibble j of a word holds k = 8*row + j
 LAYOUT_REF = "ref"    # uint8 [N, K/2], low nibble = even k (the reference's)
 
@@ -75,8 +76,10 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
                    and zeros [N, K/G] as in _msl_templates.py:2693-2695.
                    Read natively by b2_int4_matmul_ref (no repack).
     zeros=None means the symmetric zero point 8.
-    input fp16 / bf16 run natively; fp32 input (the reference's dtype) is
-    computed with fp16 activations/scales and returned as fp32.
+    input fp16 / bf16 run the tensor-core kernels; fp32 input (the
+    reference's dtype) runs with fp32 scales / zeros, the reference's fp32
+    dequant (q - z) * s and fp32 products (no 16-bit rounding anywhere) and
+    returns fp32.
     """
     if (layout == LAYOUT_GPTQ and zeros is None and input.dtype in _DT and scales.dtype == input.dtype
             and weight.dtype == torch.int32 and input.dim() == 2 and weight.dim() == 2 and scales.dim() == 2
@@ -110,8 +113,8 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
         if zeros is not None and tuple(zeros.shape) != tuple(scales.shape):
             raise B2ShapeError("zeros must have the shape of scales")
         out_dtype = input.dtype
-        cdt = torch.float16 if input.dtype == torch.float32 else input.dtype
-        if cdt not in _DT:
+        cdt = input.dtype
+        if cdt not in _DT and cdt != torch.float32:
             raise B2DtypeError(f"input dtype {input.dtype} unsupported (fp16, bf16, fp32)")
         x = input.to(cdt).contiguous()
         s = scales.to(cdt).contiguous()
@@ -119,7 +122,7 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
         res = torch.empty(M, N, dtype=cdt, device=input.device)
         if M:
             _lib.call("b2_int4_matmul_ref", _ptr(x), _ptr(weight.contiguous()), _ptr(res), _ptr(s), _ptr(z),
-                      M, N, K, group_size, _DT[cdt], _stream())
+                      M, N, K, group_size, _DTC[cdt], _stream())
         res = res.to(out_dtype)
         if out is not None:
             out.copy_(res)
@@ -137,11 +140,8 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
     if zeros is not None and tuple(zeros.shape) != tuple(scales.shape):
         raise B2ShapeError("zeros must have the shape of scales")
     out_dtype = input.dtype
-    if input.dtype == torch.float32:
-        cdt = torch.float16
-    elif input.dtype in _DT:
-        cdt = input.dtype
-    else:
+    cdt = input.dtype
+    if cdt not in _DT and cdt != torch.float32:
         raise B2DtypeError(f"input dtype {input.dtype} unsupported (fp16, bf16, fp32)")
     x = input.to(cdt).contiguous()
     s = scales.to(cdt).contiguous()
@@ -154,7 +154,7 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
     if M == 0:
         return res.to(out_dtype)
     _lib.call("b2_int4_matmul", _ptr(x), _ptr(w), _ptr(res), _ptr(s), _ptr(z),
-              M, N, K, group_size, _DT[cdt], _stream())
+              M, N, K, group_size, _DTC[cdt], _stream())
     if res.dtype != out_dtype:
         res = res.to(out_dtype)
     if out is not None and res is not out:
@@ -180,6 +180,8 @@ def int8_matmul(input, weight, scales, zeros=None, out=None):
     """out[M, N] = input[M, K] @ ((w8 - z) * s)^T with per-channel s, z [N].
 
     weight int8 [N, K] (the reference layout, _msl_templates.py:2640-2644).
+    fp16 / bf16 input runs the tensor-core kernels; fp32 input runs the
+    reference's fp32 arithmetic ((w - z) * s, fp32 products) and returns fp32.
     """
     _check_cuda(input, weight, scales, zeros)
     if input.dim() != 2 or weight.dim() != 2 or weight.dtype != torch.int8:
@@ -191,11 +193,8 @@ def int8_matmul(input, weight, scales, zeros=None, out=None):
     if scales.numel() != N or (zeros is not None and zeros.numel() != N):
         raise B2ShapeError("scales / zeros must have N elements")
     out_dtype = input.dtype
-    if input.dtype == torch.float32:
-        cdt = torch.float16
-    elif input.dtype in _DT:
-        cdt = input.dtype
-    else:
+    cdt = input.dtype
+    if cdt not in _DT and cdt != torch.float32:
         raise B2DtypeError(f"input dtype {input.dtype} unsupported (fp16, bf16, fp32)")
     x = input.to(cdt).contiguous()
     s = scales.to(cdt).contiguous()
@@ -204,7 +203,7 @@ def int8_matmul(input, weight, scales, zeros=None, out=None):
     if M == 0:
         return res.to(out_dtype)
     _lib.call("b2_int8_matmul", _ptr(x), _ptr(weight.contiguous()), _ptr(res), _ptr(s), _ptr(z),
-              M, N, K, _DT[cdt], _stream())
+              M, N, K, _DTC[cdt], _stream())
     if res.dtype != out_dtype:
         res = res.to(out_dtype)
     if out is not None:

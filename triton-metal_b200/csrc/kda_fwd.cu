@@ -70,61 +70,63 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // ---------------------------------------------------------------------------
 // Kernel A: intra-chunk WY/UT transform on the 5th-gen tensor cores, one CTA
-// per (b, h, chunk), 256 threads.  Thread (dp, I) owns the column pair
-// d = 2 dp, 2 dp + 1 of the 16 rows of block I (rows 16 I .. 16 I + 15).
-//  1. g -> G = in-chunk cumsum (block prefix + block offsets through smem).
-//  2. Every exponential is split at per-block reference rows so that each
-//     factor stays in range; with r0 = 16 I, mid = 16 I + 7 and nx = the
-//     first row of the next block (row 63 for the last block):
-//        i side (rows i of block I)      j side (rows j of block I)
-//        Loff_i  = k_i e^{G_i - G_r0}    Khd_j = k_j e^{G_nx - G_j} e^{G_mid - G_nx}
-//        Ldiag_i = Loff_i e^{G_r0 - G_mid}
-//        Khoff^(I')_j = k_j e^{G_nx - G_j} e^{G_r0(I') - G_nx}   (blocks I' > I)
-//     so A_kk[i][j] / beta_i = Loff_i . Khoff^(I(i))_j (j in an earlier block)
-//     and = Ldiag_i . Khd_j (same block); likewise A_qk with scale q for k on
-//     the i side.  Off-diagonal factors are all <= 1.  On the diagonal the
-//     factors reach e^{+-gap}, gap = max_d (G_r0 - G_nx); blocks with
-//     gap > 80 (fp32 / bf16 range) are recomputed exactly on CUDA cores.
-//  3. The bf16 operands go to shared memory in the 128-byte-swizzled K-major
-//     layout and two tcgen05.mma (M = N = 128, K = 128) produce every lower
-//     block of A_kk and A_qk in TMEM: A rows = j side (block rows 3 and 2,
-//     then 1 and 0), B rows = i side.
-//  4. T = (I + A_kk)^-1 on CUDA cores (fp32): diagonal 16 x 16 blocks by
-//     column substitution, then T_IJ = -T_II sum_M A_IM T_MJ level by level.
+// per (b, h, chunk), 256 threads, two CTAs per SM.  Thread (dp, I) owns the
+// column pair d = 2 dp, 2 dp + 1 of the 16 rows of block I (rows 16 I ..).
+//  1. G = in-chunk cumsum of g: block prefix in registers, block offsets and
+//     the reference rows (each block's first row, the last row) via smem.
+//  2. Every exponential is split at a per-block reference row r0 = 16 I so
+//     that each bf16 factor stays in range (G is non-increasing along t):
+//        i side  L_i  = k_i e^{G_i - G_r0(I(i))}                 (<= 1)
+//                Lq_i = scale q_i e^{G_i - G_r0(I(i))}           (<= 1)
+//        j side  K^(I')_j = k_j e^{G_r0(I') - G_j},  j < 16 (I' + 1)
+//     (<= 1 for j in an earlier block, up to e^{gap} inside block I', gap =
+//     max_d (G_r0 - G_next r0)), so that for i in block I' and j <= i
+//        A_kk[i][j] = beta_i L_i . K^(I')_j,   A_qk[i][j] = Lq_i . K^(I')_j.
+//     Blocks with gap > 80 (beyond bf16 / fp32 range of the factors) get
+//     their diagonal 16 x 16 block recomputed exactly on CUDA cores.
+//  3. Two tcgen05.mma (bf16 operands, K = 128, M = N = 128): A = the j-side
+//     rows of block rows 3 and 2 (then 1 and 0), B = [L; Lq] for all 64 i;
+//     every lower block of A_kk and A_qk lands in TMEM.
+//  4. T = (I + A_kk)^-1: diagonal 16 x 16 blocks by column substitution
+//     (fp32), then T_IJ = -T_II sum_M A_IM T_MJ level by level on tf32 MMAs.
 //  5. W^T = (beta K e^G)^T T^T and U^T = (beta V)^T T^T as two tcgen05.mma
 //     (M = 128 = Dk / Dv, N = 64, K = 64), bf16 operands, fp32 in TMEM.
 //  6. W, U, A_qk, scale Q e^G, K e^{G_last - G} (fp16) and e^{G_last} go to
-//     the workspace block of this chunk for kernel B.
+//     the workspace block of this chunk in kernel B's stage layout.
 // ---------------------------------------------------------------------------
 namespace prep {
 constexpr int kThreads = 256;
-constexpr int LT = C + 4;                     // fp32 row stride of A_kk / A_qk / T
-constexpr uint32_t kOpBytes = 128 * 128 * 2;  // one 128-row, K = 128 bf16 operand
-constexpr uint32_t kAA = 0;                   // j side of block rows 3, 2
-constexpr uint32_t kAB = kAA + kOpBytes;      // j side of block rows 1, 0
-constexpr uint32_t kBA = kAB + kOpBytes;      // i side of block rows 3, 2
-constexpr uint32_t kBB = kBA + kOpBytes;      // i side of block rows 1, 0
-constexpr uint32_t kAW = kBB + kOpBytes;      // (beta K e^G)^T: 128 rows (dk) x K = 64 (t)
-constexpr uint32_t kAU = kAW + 128 * 64 * 2;  // (beta V)^T
-constexpr uint32_t kSG = kAU + 128 * 64 * 2;  // G fp32 [64][128]
-constexpr uint32_t kST = kSG + C * DK * 4;    // T fp32 [64][LT]
-constexpr uint32_t kTot = kST + C * LT * 4;   // block totals of g [4][128]
-constexpr uint32_t kBeta = kTot + 4 * DK * 4; // beta [64]
-constexpr uint32_t kGap = kBeta + C * 4;      // per block max exponent gap (fp32 bits) [4]
-constexpr uint32_t kBar = kGap + 16;          // 2 mbarriers
-constexpr uint32_t kHold = kBar + 16;         // TMEM base address
+constexpr int LT = C + 4;  // fp32 row stride of A_kk / A_qk / T scratch
+// region R: A_kk MMA operands (bf16, K-major, 128-byte swizzle, 1024-aligned);
+// K-blocks of 64 elements each hold `rows` rows
+constexpr uint32_t kRowsAA = 112;                        // j side of block rows 3 (64) and 2 (48)
+constexpr uint32_t kRowsAB = 48;                         // j side of block rows 1 (32) and 0 (16)
+constexpr uint32_t kAA = 0;
+constexpr uint32_t kAB = kAA + 2 * kRowsAA * 128;        // 28 KB
+constexpr uint32_t kBL = kAB + 2 * kRowsAB * 128;        // + 12 KB: i side [L; Lq], 128 rows
+constexpr uint32_t kRegionR = kBL + 2 * 128 * 128;       // + 32 KB = 72 KB
+// after the A_kk MMAs: fp32 scratch and the bf16 T operand alias region R
+constexpr uint32_t kSA = 0;
+constexpr uint32_t kSAq = kSA + C * LT * 4;
+constexpr uint32_t kST = kSAq + C * LT * 4;
+constexpr uint32_t kSGb = kST + C * LT * 4;              // exact fallback: G of one block [16][128]
+constexpr uint32_t kBT = 61440;                          // T bf16: 64 rows (t) x K = 64 (j)
+// region W: W / U MMA A operands, 128 rows (dk / dv) x K = 64 (t)
+constexpr uint32_t kAW = kRegionR;
+constexpr uint32_t kAU = kAW + 128 * 64 * 2;
+constexpr uint32_t kTot = kAW;                           // block totals of g [4][128] (before region W is written)
+constexpr uint32_t kGref = kAU + 128 * 64 * 2;           // G at rows 0, 16, 32, 48, 63: [5][128]
+constexpr uint32_t kBeta = kGref + 5 * DK * 4;
+constexpr uint32_t kGap = kBeta + C * 4;                 // per block max exponent gap (fp32 bits)
+constexpr uint32_t kBar = kGap + 16;
+constexpr uint32_t kHold = kBar + 16;
 constexpr uint32_t kBytes = kHold + 16;
-constexpr size_t kSmem = kBytes + 1024;       // + alignment of the swizzled tiles
-// aliases, valid once the A_kk MMAs have completed
-constexpr uint32_t kSA = kAA;                 // A_kk fp32 [64][LT]
-constexpr uint32_t kSAq = kAA + C * LT * 4;   // A_qk fp32 [64][LT]
-constexpr uint32_t kBT = kBA;                 // T bf16, 64 rows (t) x K = 64 (j)
+constexpr size_t kSmem = kBytes + 1024;                  // + alignment of the swizzled tiles
 constexpr uint32_t kTmemCols = 256;
 constexpr float kGapMax = 80.f;
-static_assert(kSAq + C * LT * 4 <= kBA, "A_kk / A_qk scratch must fit in the two j-side operand tiles");
+static_assert(kSGb + 16 * DK * 4 <= kBT && kBT + 64 * 128 <= kRegionR, "scratch must fit in region R");
+static_assert(kSmem <= 113 * 1024, "two CTAs per SM");
 
-// byte offset of bf16 element (row, k) in a K-major 128B-swizzled operand whose
-// K-blocks (64 elements) each hold `rows` rows
 __device__ __forceinline__ uint32_t sw_off(int row, int k, int rows) {
   return (uint32_t)((k >> 6) * rows * 128 + row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
 }
@@ -135,6 +137,33 @@ __device__ __forceinline__ uint32_t bf2(float lo, float hi) {
 __device__ __forceinline__ void st_u32(uint8_t* base, uint32_t off, uint32_t v) {
   *reinterpret_cast<uint32_t*>(base + off) = v;
 }
+__device__ __forceinline__ float fexp(float x) { return __expf(x); }
+__device__ __forceinline__ float2 exp2f2(float2 a, float2 b) {  // e^{a - b} per component
+  return make_float2(fexp(a.x - b.x), fexp(a.y - b.y));
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return make_float2(a.x * b.x, a.y * b.y); }
+
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ uint32_t tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // a pair of elements kept packed in registers until used (16-bit: one word)
 template <typename T>
 struct Pair {
@@ -149,7 +178,6 @@ struct Pair {
     }
   }
 };
-__device__ __forceinline__ float fexp(float x) { return __expf(x); }
 }  // namespace prep
 
 // Phase timestamps of the first CTAs, compiled only into profiling builds
@@ -168,16 +196,16 @@ __device__ unsigned long long g_kda_prof[64][16];
 #endif
 
 template <typename T>
-__global__ void __launch_bounds__(prep::kThreads, 1)
+__global__ void __launch_bounds__(prep::kThreads, 2)
 kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                 const float* __restrict__ g, const T* __restrict__ beta, float* __restrict__ ws, int B, int Tlen,
                 int H, float scale, unsigned* __restrict__ err) {
   using namespace prep;
+  using P2 = Pair<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  float* sG = reinterpret_cast<float*>(sm + kSG);
-  float* sT = reinterpret_cast<float*>(sm + kST);
   float* sTot = reinterpret_cast<float*>(sm + kTot);
+  float* sGref = reinterpret_cast<float*>(sm + kGref);
   float* sBeta = reinterpret_cast<float*>(sm + kBeta);
   unsigned* sGap = reinterpret_cast<unsigned*>(sm + kGap);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBar);
@@ -202,10 +230,8 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   }
   if (tid < C) sBeta[tid] = to_f32<T>(beta[row0 + (int64_t)tid * H]);
 
-  // ---- 1. G: prefix inside the block, then the preceding blocks' totals ----
-  // every global load of this thread's rows first, so that their latencies overlap
-  using P2 = Pair<T>;
-  typename P2::R kraw[16], qraw[16], vraw[16];
+  // ---- 1. loads (all issued before any use), G ----
+  typename P2::R kraw[16], qraw[16];
   float2 G[16];
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
@@ -213,7 +239,6 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     G[r] = *reinterpret_cast<const float2*>(g + gi);
     kraw[r] = P2::load(k + gi);
     qraw[r] = P2::load(q + gi);
-    vraw[r] = P2::load(v + gi);
   }
 #pragma unroll
   for (int r = 1; r < 16; ++r) {
@@ -236,90 +261,99 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     for (int r = 0; r < 16; ++r) {
       G[r].x += off.x;
       G[r].y += off.y;
-      *reinterpret_cast<float2*>(sG + (r0 + r) * DK + d0) = G[r];
     }
+    *reinterpret_cast<float2*>(sGref + I * DK + d0) = G[0];
+    if (I == 3) *reinterpret_cast<float2*>(sGref + 4 * DK + d0) = G[15];
   }
-  __syncthreads();
-
+  __syncthreads();  // sTot consumed (region W may be written from here on); sGref complete
   B2_PROF(1);
+
   // ---- 2. per-column constants of this block ----
-  const float2 Gr0 = G[0], Gmid = G[7];
-  const float2 Gnx = I < 3 ? *reinterpret_cast<const float2*>(sG + (r0 + 16) * DK + d0) : G[15];
-  const float2 Gl = *reinterpret_cast<const float2*>(sG + (C - 1) * DK + d0);
+  const float2 Gr0 = G[0];
+  const float2 Gnx = *reinterpret_cast<const float2*>(sGref + (I + 1) * DK + d0);  // row 16 (I + 1), or 63
+  const float2 Gl = *reinterpret_cast<const float2*>(sGref + 4 * DK + d0);
   {
     float gap = fmaxf(Gr0.x - Gnx.x, Gr0.y - Gnx.y);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) gap = fmaxf(gap, __shfl_xor_sync(0xffffffffu, gap, o));
     if (lane == 0) atomicMax(&sGap[I], __float_as_uint(fmaxf(gap, 0.f)));
   }
-  const float2 cA = make_float2(fexp(Gr0.x - Gmid.x), fexp(Gr0.y - Gmid.y));
-  const float2 cB = make_float2(fexp(Gmid.x - Gnx.x), fexp(Gmid.y - Gnx.y));
-  const float2 eG0 = make_float2(fexp(Gr0.x), fexp(Gr0.y));
-  const float2 cKr = make_float2(fexp(Gl.x - Gnx.x), fexp(Gl.y - Gnx.y));
-  float2 cOff[3];  // e^{G_r0(I') - G_nx} for I' = I + 1 .. 3
+  const float2 zero2 = make_float2(0.f, 0.f);
+  const float2 eG0 = exp2f2(Gr0, zero2);  // e^{G_r0}
+  const float2 cD = exp2f2(Gr0, Gnx);     // e^{G_r0 - G_nx}, the diagonal j-side factor (>= 1)
+  const float2 cKr = exp2f2(Gl, Gnx);     // e^{G_last - G_nx}
+  float2 cOff[3];                          // e^{G_r0(I') - G_nx}, I' = I + 1 .. 3 (<= 1)
 #pragma unroll
-  for (int u = 0; u < 3; ++u) {
-    const int Ip = I + 1 + u;
-    if (Ip < 4) {
-      const float2 gr = *reinterpret_cast<const float2*>(sG + 16 * Ip * DK + d0);
-      cOff[u] = make_float2(fexp(gr.x - Gnx.x), fexp(gr.y - Gnx.y));
-    } else {
-      cOff[u] = make_float2(0.f, 0.f);
-    }
-  }
+  for (int u = 0; u < 3; ++u)
+    cOff[u] = I + 1 + u < 4 ? exp2f2(*reinterpret_cast<const float2*>(sGref + (I + 1 + u) * DK + d0), Gnx) : zero2;
 
-  // ---- 3. operands: rows of this block for the A_kk / A_qk MMAs, the W / U
-  // operands, and scale Q e^G, K e^{G_last - G} straight to the workspace ----
-  uint8_t* opA = sm + (I >= 2 ? kAA : kAB);
-  uint8_t* opB = sm + (I >= 2 ? kBA : kBB);
-  // i-side rows of this block in its B operand (block rows 3 / 1 at 0, 2 / 0 at 64)
-  const int ib = (I == 3 || I == 1) ? 0 : 64;
-  // j-side diagonal rows of this block in its A operand
-  const int jd = I == 3 ? 48 : (I == 2 ? 96 : (I == 1 ? 16 : 32));
+  // ---- 3. operands of the A_kk / A_qk MMAs, the W operand, and scale Q e^G,
+  // K e^{G_last - G} straight to the workspace ----
   __half* wsQg = ws_h(blk, kBQg);
   __half* wsKr = ws_h(blk, kBKr);
-  float2 wk[16];  // beta K e^G for the W operand, this thread's rows
+  float2 wk[16];  // beta K e^G (W operand); then beta V (U operand)
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
     const int t = r0 + r;
     const float2 kk = P2::f2(kraw[r]);
     const float2 q2 = P2::f2(qraw[r]);
     const float2 sq = make_float2(q2.x * scale, q2.y * scale);
-    const float2 e0 = make_float2(fexp(G[r].x - Gr0.x), fexp(G[r].y - Gr0.y));
-    const float2 ej = make_float2(fexp(Gnx.x - G[r].x), fexp(Gnx.y - G[r].y));
-    const float2 lo = make_float2(kk.x * e0.x, kk.y * e0.y);
-    const float2 lq = make_float2(sq.x * e0.x, sq.y * e0.y);
-    const float2 kj = make_float2(kk.x * ej.x, kk.y * ej.y);
-    // i side: Loff, Lqoff (block rows >= 1), Ldiag, Lqdiag
-    if (I >= 1) {
-      st_u32(opB, sw_off(ib + r, d0, 128), bf2(lo.x, lo.y));
-      st_u32(opB, sw_off(ib + 16 + r, d0, 128), bf2(lq.x, lq.y));
-      st_u32(opB, sw_off(ib + 32 + r, d0, 128), bf2(lo.x * cA.x, lo.y * cA.y));
-      st_u32(opB, sw_off(ib + 48 + r, d0, 128), bf2(lq.x * cA.x, lq.y * cA.y));
-    } else {
-      st_u32(opB, sw_off(64 + r, d0, 128), bf2(lo.x * cA.x, lo.y * cA.y));
-      st_u32(opB, sw_off(80 + r, d0, 128), bf2(lq.x * cA.x, lq.y * cA.y));
-    }
-    // j side: diagonal block, then every later block row I' (off-diagonal)
-    st_u32(opA, sw_off(jd + r, d0, 128), bf2(kj.x * cB.x, kj.y * cB.y));
+    const float2 e0 = exp2f2(G[r], Gr0);  // <= 1
+    const float2 ej = exp2f2(Gnx, G[r]);  // <= 1
+    const float2 lo = mul2(kk, e0), lq = mul2(sq, e0), kj = mul2(kk, ej);
+    // i side: rows t (L) and 64 + t (Lq)
+    st_u32(sm + kBL, sw_off(t, d0, 128), bf2(lo.x, lo.y));
+    st_u32(sm + kBL, sw_off(64 + t, d0, 128), bf2(lq.x, lq.y));
+    // j side: block row I (diagonal) and every later block row
+    const float2 kd = mul2(kj, cD);
+    if (I == 3) st_u32(sm + kAA, sw_off(t, d0, kRowsAA), bf2(kd.x, kd.y));
+    else if (I == 2) st_u32(sm + kAA, sw_off(64 + t, d0, kRowsAA), bf2(kd.x, kd.y));
+    else if (I == 1) st_u32(sm + kAB, sw_off(t, d0, kRowsAB), bf2(kd.x, kd.y));
+    else st_u32(sm + kAB, sw_off(32 + t, d0, kRowsAB), bf2(kd.x, kd.y));
 #pragma unroll
     for (int u = 0; u < 3; ++u) {
       const int Ip = I + 1 + u;
       if (Ip >= 4) break;
-      const uint32_t v2 = bf2(kj.x * cOff[u].x, kj.y * cOff[u].y);
-      if (Ip == 3) st_u32(sm + kAA, sw_off(t, d0, 128), v2);
-      else if (Ip == 2) st_u32(sm + kAA, sw_off(64 + t, d0, 128), v2);
-      else st_u32(sm + kAB, sw_off(t, d0, 128), v2);
+      const float2 ko = mul2(kj, cOff[u]);
+      const uint32_t v2 = bf2(ko.x, ko.y);
+      if (Ip == 3) st_u32(sm + kAA, sw_off(t, d0, kRowsAA), v2);
+      else if (Ip == 2) st_u32(sm + kAA, sw_off(64 + t, d0, kRowsAA), v2);
+      else st_u32(sm + kAB, sw_off(t, d0, kRowsAB), v2);
     }
-    // workspace outputs of this row
     *reinterpret_cast<__half2*>(wsQg + t * LR + d0) = __floats2half2_rn(lq.x * eG0.x, lq.y * eG0.y);
     *reinterpret_cast<__half2*>(wsKr + t * LR + d0) = __floats2half2_rn(kj.x * cKr.x, kj.y * cKr.y);
     const float bt = sBeta[t];
     wk[r] = make_float2(bt * lo.x * eG0.x, bt * lo.y * eG0.y);
   }
-  // W / U operands: rows d, K = t; this thread's 16 t of rows d0, d0 + 1 are
-  // two 16-byte chunks each
+  tc::fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  B2_PROF(2);
+
+  // ---- 4. A_kk / A_qk MMAs (one thread) ----
+  if (tid == 0) {
+    tc::fence_after_sync();
+    constexpr uint32_t idesc = tc::idesc_f16(128, 128, true);
+#pragma unroll
+    for (int s = 0; s < DK / 16; ++s) {
+      const uint32_t ko = 2u * (s & 3);
+      tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(sm + kAA + (s >> 2) * kRowsAA * 128) + ko,
+                     tc::desc_kmajor_sw128(sm + kBL + (s >> 2) * 128 * 128) + ko, idesc, s != 0);
+    }
+#pragma unroll
+    for (int s = 0; s < DK / 16; ++s) {
+      const uint32_t ko = 2u * (s & 3);
+      tc::mma_f16_ss(tmem + 128, tc::desc_kmajor_sw128(sm + kAB + (s >> 2) * kRowsAB * 128) + ko,
+                     tc::desc_kmajor_sw128(sm + kBL + (s >> 2) * 128 * 128) + ko, idesc, s != 0);
+    }
+    tc::commit(&bar[0]);
+  }
+  // meanwhile: the W operand (rows d, K = t) of this thread's 16 t, then
+  // beta V for the U operand (loads issued before the W stores)
   {
+    typename P2::R vraw[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) vraw[r] = P2::load(v + (row0 + (int64_t)(r0 + r) * H) * DV + d0);
     uint32_t p0[8], p1[8];
 #pragma unroll
     for (int r = 0; r < 16; r += 2) {
@@ -352,103 +386,50 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           make_uint4(p1[4 * c], p1[4 * c + 1], p1[4 * c + 2], p1[4 * c + 3]);
     }
   }
-  if (tid < DK / 2) {  // e^{G_last}: block 3 holds row 63
-    // (any thread has Gl for its pair)
-    *reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(blk) + kBGl + 4 * d0) = make_float2(fexp(Gl.x), fexp(Gl.y));
-  }
-  tc::fence_proxy_async_smem();
-  tc::fence_before_sync();
-  __syncthreads();
-
-  B2_PROF(2);
-  // ---- 4. A_kk / A_qk MMAs (one thread) ----
-  if (tid == 0) {
-    tc::fence_after_sync();
-    constexpr uint32_t idesc = tc::idesc_f16(128, 128, true);
-#pragma unroll
-    for (int s = 0; s < DK / 16; ++s) {
-      const uint32_t kb = (uint32_t)(s >> 2) * kOpBytes / 2, ko = 2u * (s & 3);
-      tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(sm + kAA + kb) + ko, tc::desc_kmajor_sw128(sm + kBA + kb) + ko,
-                     idesc, s != 0);
-    }
-#pragma unroll
-    for (int s = 0; s < DK / 16; ++s) {
-      const uint32_t kb = (uint32_t)(s >> 2) * kOpBytes / 2, ko = 2u * (s & 3);
-      tc::mma_f16_ss(tmem + 128, tc::desc_kmajor_sw128(sm + kAB + kb) + ko,
-                     tc::desc_kmajor_sw128(sm + kBB + kb) + ko, idesc, s != 0);
-    }
-    tc::commit(&bar[0]);
-  }
+  if (tid < DK / 2)
+    *reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(blk) + kBGl + 4 * d0) = exp2f2(Gl, zero2);
   bool alive = mbar_wait(&bar[0], 0, err, 0xB2300001u);
   tc::fence_after_sync();
-  // A_kk / A_qk scratch (aliases the j-side tiles the MMAs just read)
+  // A_kk / A_qk scratch (aliases region R, which the MMAs just read)
   float* sA = reinterpret_cast<float*>(sm + kSA);
   float* sAq = reinterpret_cast<float*>(sm + kSAq);
+  float* sT = reinterpret_cast<float*>(sm + kST);
   for (int e = tid; e < C * LT; e += kThreads) {
     sA[e] = 0.f;
     sAq[e] = 0.f;
   }
   __syncthreads();
-
   B2_PROF(3);
-  // ---- 5. TMEM -> A_kk (times beta_i), A_qk (lower parts only) ----
+
+  // ---- 5. TMEM -> A_kk (times beta_i), A_qk: lane j = A-operand row; the
+  // block row's 16 L columns (A_kk) and 16 Lq columns (A_qk) ----
   if (alive) {
     const int qd = warp & 3, half = warp >> 2;
-    const int L = 32 * qd + lane;  // TMEM lane = A-operand row
-    uint32_t vals[64];
-    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+    const int L = 32 * qd + lane;
+    // (TMEM column base, block row, j of lane L) per warp; block rows with no lane here are skipped
+    int Ib = -1, j = 0;
+    uint32_t cb = 0;
     if (half == 0) {
-      // block rows 3 (lanes 0..63) and 2 (lanes 64..111)
-      const uint32_t cbase = qd < 2 ? 0u : 64u;
-      uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals);
-      uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals + 32);
-      tc::tmem_ld_32x32b_x32(tmem + lane_off + cbase, v0);
-      tc::tmem_ld_32x32b_x32(tmem + lane_off + cbase + 32, v1);
-      tc::tmem_ld_wait();
-      const int Ib = qd < 2 ? 3 : 2;
-      const int j = qd < 2 ? L : L - 64;
-      const int ri = 16 * Ib;  // first row of the block row
-      if (j < ri) {            // off-diagonal: columns 0..15 A_kk, 16..31 A_qk
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          sA[(ri + i) * LT + j] = __uint_as_float(vals[i]) * sBeta[ri + i];
-          sAq[(ri + i) * LT + j] = __uint_as_float(vals[16 + i]);
-        }
-      } else if (j < ri + 16) {  // diagonal: columns 32..47 A_kk, 48..63 A_qk
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if (j < ri + i) sA[(ri + i) * LT + j] = __uint_as_float(vals[32 + i]) * sBeta[ri + i];
-          if (j <= ri + i) sAq[(ri + i) * LT + j] = __uint_as_float(vals[48 + i]);
-        }
-      }
+      Ib = qd < 2 ? 3 : 2;
+      j = qd < 2 ? L : L - 64;
+      cb = 0;
     } else if (qd < 2) {
-      // block rows 1 (lanes 0..31) and 0 (lanes 32..47), TMEM columns 128..
-      uint32_t (&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals);
-      uint32_t (&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(vals + 32);
-      tc::tmem_ld_32x32b_x32(tmem + lane_off + 128 + (qd == 0 ? 0u : 64u), v0);
-      tc::tmem_ld_32x32b_x32(tmem + lane_off + 128 + (qd == 0 ? 32u : 96u), v1);
+      Ib = qd == 0 ? 1 : 0;
+      j = qd == 0 ? L : L - 32;
+      cb = 128;
+    }
+    if (Ib >= 0) {
+      const int ri = 16 * Ib;
+      uint32_t va[16], vq[16];
+      const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+      tmem_ld_x16(tmem + lane_off + cb + 16 * Ib, va);
+      tmem_ld_x16(tmem + lane_off + cb + 64 + 16 * Ib, vq);
       tc::tmem_ld_wait();
-      if (qd == 0) {
-        const int j = L;
-        if (j < 16) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            sA[(16 + i) * LT + j] = __uint_as_float(vals[i]) * sBeta[16 + i];
-            sAq[(16 + i) * LT + j] = __uint_as_float(vals[16 + i]);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (j < 16 + i) sA[(16 + i) * LT + j] = __uint_as_float(vals[32 + i]) * sBeta[16 + i];
-            if (j <= 16 + i) sAq[(16 + i) * LT + j] = __uint_as_float(vals[48 + i]);
-          }
-        }
-      } else if (L < 48) {
-        const int j = L - 32;
+      if (j < ri + 16) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          if (j < i) sA[i * LT + j] = __uint_as_float(vals[i]) * sBeta[i];
-          if (j <= i) sAq[i * LT + j] = __uint_as_float(vals[16 + i]);
+          if (j < ri + i) sA[(ri + i) * LT + j] = __uint_as_float(va[i]) * sBeta[ri + i];
+          if (j <= ri + i) sAq[(ri + i) * LT + j] = __uint_as_float(vq[i]);
         }
       }
     }
@@ -457,9 +438,19 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   __syncthreads();
   B2_PROF(4);
   // diagonal blocks whose exponent gap is beyond the bf16 / fp32 range of the
-  // split factors: exact fp32 on CUDA cores (pairs j <= i of the block)
+  // split factors: exact fp32 on CUDA cores (pairs j <= i of the block), with
+  // the block's in-chunk G rebuilt from g (relative to its first row)
   for (int Ib = 0; Ib < 4; ++Ib) {
     if (__uint_as_float(sGap[Ib]) <= kGapMax) continue;
+    float* sGb = reinterpret_cast<float*>(sm + kSGb);
+    if (tid < DK) {
+      float acc = 0.f;
+      for (int r = 0; r < 16; ++r) {
+        acc += g[(row0 + (int64_t)(16 * Ib + r) * H) * DK + tid];
+        sGb[r * DK + tid] = acc;
+      }
+    }
+    __syncthreads();
     for (int p = tid; p < 136; p += kThreads) {
       int i = 0, rem = p;
       while (rem > i) {
@@ -472,7 +463,7 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       const T* kj = k + (row0 + (int64_t)rj * H) * DK;
       float akk = 0.f, aqk = 0.f;
       for (int d = 0; d < DK; ++d) {
-        const float e = fexp(sG[ri * DK + d] - sG[rj * DK + d]);
+        const float e = fexp(sGb[i * DK + d] - sGb[rem * DK + d]);
         const float kjd = to_f32<T>(kj[d]) * e;
         akk += to_f32<T>(ki[d]) * kjd;
         aqk += to_f32<T>(qi[d]) * kjd;
@@ -480,10 +471,10 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       if (rj < ri) sA[ri * LT + rj] = akk * sBeta[ri];
       sAq[ri * LT + rj] = aqk * scale;
     }
+    __syncthreads();
   }
-  __syncthreads();
-
   B2_PROF(5);
+
   // ---- 6. A_qk -> workspace (fp16, zeros above the diagonal) ----
   {
     __half* wsAq = ws_h(blk, kBAq);
@@ -513,24 +504,53 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   }
   __syncthreads();
   B2_PROF(6);
-  // off-diagonal blocks level by level: X_IJ = sum_{M=J}^{I-1} A_IM T_MJ (into
-  // sAq, no longer needed), T_IJ = -T_II X_IJ
-  for (int Ib = 1; Ib < 4; ++Ib) {
-    const int nel = 256 * Ib;
-    for (int e = tid; e < nel; e += kThreads) {
-      const int J = e >> 8, ii = (e >> 4) & 15, jj = e & 15;
-      float s = 0.f;
-      for (int m = 16 * J; m < 16 * Ib; ++m) s += sA[(16 * Ib + ii) * LT + m] * sT[m * LT + 16 * J + jj];
-      sAq[(16 * Ib + ii) * LT + 16 * J + jj] = s;
+  // off-diagonal blocks level by level on tf32 MMAs (m16n8k8, fp32
+  // accumulate), warp J < Ib of level Ib owning block (Ib, J):
+  //   X_IJ = sum_{M=J}^{Ib-1} A_IM T_MJ  (into sAq, no longer needed)
+  //   T_IJ = -T_II X_IJ
+  {
+    const int gq = lane >> 2, tq = lane & 3;
+    for (int Ib = 1; Ib < 4; ++Ib) {
+      if (warp < Ib) {
+        const int J = warp, ri = 16 * Ib, cj = 16 * J;
+        float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        for (int m0 = cj; m0 < ri; m0 += 8) {
+          const uint32_t a0 = tf32(sA[(ri + gq) * LT + m0 + tq]), a1 = tf32(sA[(ri + gq + 8) * LT + m0 + tq]);
+          const uint32_t a2 = tf32(sA[(ri + gq) * LT + m0 + tq + 4]), a3 = tf32(sA[(ri + gq + 8) * LT + m0 + tq + 4]);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+            mma_tf32(x[nt], a0, a1, a2, a3, tf32(sT[(m0 + tq) * LT + cj + 8 * nt + gq]),
+                     tf32(sT[(m0 + tq + 4) * LT + cj + 8 * nt + gq]));
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          sAq[(ri + gq) * LT + cj + 8 * nt + 2 * tq] = x[nt][0];
+          sAq[(ri + gq) * LT + cj + 8 * nt + 2 * tq + 1] = x[nt][1];
+          sAq[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq] = x[nt][2];
+          sAq[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq + 1] = x[nt][3];
+        }
+        __syncwarp();
+        float y[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const int kb = ri + 8 * ks;
+          const uint32_t a0 = tf32(sT[(ri + gq) * LT + kb + tq]), a1 = tf32(sT[(ri + gq + 8) * LT + kb + tq]);
+          const uint32_t a2 = tf32(sT[(ri + gq) * LT + kb + tq + 4]), a3 = tf32(sT[(ri + gq + 8) * LT + kb + tq + 4]);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+            mma_tf32(y[nt], a0, a1, a2, a3, tf32(sAq[(kb + tq) * LT + cj + 8 * nt + gq]),
+                     tf32(sAq[(kb + tq + 4) * LT + cj + 8 * nt + gq]));
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          sT[(ri + gq) * LT + cj + 8 * nt + 2 * tq] = -y[nt][0];
+          sT[(ri + gq) * LT + cj + 8 * nt + 2 * tq + 1] = -y[nt][1];
+          sT[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq] = -y[nt][2];
+          sT[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq + 1] = -y[nt][3];
+        }
+      }
+      __syncthreads();
     }
-    __syncthreads();
-    for (int e = tid; e < nel; e += kThreads) {
-      const int J = e >> 8, ii = (e >> 4) & 15, jj = e & 15;
-      float s = 0.f;
-      for (int m = 0; m <= ii; ++m) s += sT[(16 * Ib + ii) * LT + 16 * Ib + m] * sAq[(16 * Ib + m) * LT + 16 * J + jj];
-      sT[(16 * Ib + ii) * LT + 16 * J + jj] = -s;
-    }
-    __syncthreads();
   }
   B2_PROF(7);
   // ---- 8. T (bf16) as the B operand: rows t, K = j ----

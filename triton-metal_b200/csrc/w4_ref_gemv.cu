@@ -193,15 +193,23 @@ using namespace b2;
 int b2_detail_w4_gemm_ref(const void* x, const void* w, void* out, const void* s, const void* z, int64_t M,
                           int64_t N, int64_t K, int64_t G, int dtype, cudaStream_t st);
 
+namespace b2 {
+// quant_f32.cu: fp32 activations / scales / zeros / output on CUDA cores
+int b2_detail_quant_f32(int layout, const void* x, const void* w, void* out, const void* s, const void* z,
+                        int64_t M, int64_t N, int64_t K, int64_t G, cudaStream_t st);
+}  // namespace b2
+
 extern "C" int b2_int4_matmul_ref(const void* input, const void* weight, void* output, const void* scales,
                                   const void* zeros, int64_t M, int64_t N, int64_t K, int64_t group_size, int dtype,
                                   void* stream) {
   B2_CHECK_ARG(input && weight && output && scales, B2_ERR_INVALID, "int4_matmul_ref: null pointer");
   B2_CHECK_ARG(M >= 0 && N > 0 && K > 0 && group_size > 0, B2_ERR_INVALID, "int4_matmul_ref: bad shape");
-  B2_CHECK_ARG(dtype == B2_F16 || dtype == B2_BF16, B2_ERR_DTYPE, "int4_matmul_ref: dtype %d unsupported", dtype);
+  B2_CHECK_ARG(dtype == B2_F16 || dtype == B2_BF16 || dtype == B2_F32, B2_ERR_DTYPE,
+               "int4_matmul_ref: dtype %d unsupported", dtype);
   B2_CHECK_ARG(M * N < (1ll << 31) && N * K / 2 < (1ll << 31), B2_ERR_UNSUPPORTED, "int4_matmul_ref: too large");
   if (M == 0) return B2_OK;
   cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == B2_F32) return b2_detail_quant_f32(1, input, weight, output, scales, zeros, M, N, K, group_size, st);
   const auto X = (const uint16_t*)input;
   const auto W = (const uint8_t*)weight;
   const auto O = (uint16_t*)output;

@@ -607,6 +607,12 @@ using namespace b2;
 int b2_detail_w4_gemm(const void* x, const void* w, void* out, const void* s, const void* z,
                       int64_t M, int64_t N, int64_t K, int64_t G, int dtype, cudaStream_t st);
 
+namespace b2 {
+// quant_f32.cu: fp32 activations / scales / zeros / output on CUDA cores
+int b2_detail_quant_f32(int layout, const void* x, const void* w, void* out, const void* s, const void* z,
+                        int64_t M, int64_t N, int64_t K, int64_t G, cudaStream_t st);
+}  // namespace b2
+
 extern "C" int b2_int4_matmul(const void* input, const void* weight, void* output,
                               const void* scales, const void* zeros,
                               int64_t M, int64_t N, int64_t K, int64_t group_size,
@@ -618,10 +624,12 @@ extern "C" int b2_int4_matmul(const void* input, const void* weight, void* outpu
                (long long)K);
   B2_CHECK_ARG(group_size > 0 && K % group_size == 0, B2_ERR_INVALID,
                "int4_matmul: group_size=%lld must divide K=%lld", (long long)group_size, (long long)K);
-  B2_CHECK_ARG(dtype == B2_F16 || dtype == B2_BF16, B2_ERR_DTYPE, "int4_matmul: dtype %d unsupported", dtype);
+  B2_CHECK_ARG(dtype == B2_F16 || dtype == B2_BF16 || dtype == B2_F32, B2_ERR_DTYPE,
+               "int4_matmul: dtype %d unsupported", dtype);
   B2_CHECK_ARG(M * N < (1ll << 31) && K * N / 8 < (1ll << 31), B2_ERR_UNSUPPORTED, "int4_matmul: too large");
   if (M == 0) return B2_OK;
   cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == B2_F32) return b2_detail_quant_f32(0, input, weight, output, scales, zeros, M, N, K, group_size, st);
   if (gemv_ok(input, weight, scales, zeros, M, N, K, group_size)) {
     return dtype == B2_F16 ? gemv_dispatch<B2_F16>(input, weight, output, scales, zeros, M, N, K, group_size, st)
                            : gemv_dispatch<B2_BF16>(input, weight, output, scales, zeros, M, N, K, group_size, st);

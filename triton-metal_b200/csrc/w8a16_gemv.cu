@@ -208,16 +208,24 @@ using namespace b2;
 int b2_detail_w8_gemm(const void* x, const void* w, void* out, const void* s, const void* z,
                       int64_t M, int64_t N, int64_t K, int dtype, cudaStream_t st);
 
+namespace b2 {
+// quant_f32.cu: fp32 activations / scales / zeros / output on CUDA cores
+int b2_detail_quant_f32(int layout, const void* x, const void* w, void* out, const void* s, const void* z,
+                        int64_t M, int64_t N, int64_t K, int64_t G, cudaStream_t st);
+}  // namespace b2
+
 extern "C" int b2_int8_matmul(const void* input, const void* weight, void* output,
                               const void* scales, const void* zeros,
                               int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
   B2_CHECK_ARG(input && weight && output && scales, B2_ERR_INVALID, "int8_matmul: null pointer");
   B2_CHECK_ARG(M >= 0 && N > 0 && K > 0, B2_ERR_INVALID, "int8_matmul: bad shape M=%lld N=%lld K=%lld",
                (long long)M, (long long)N, (long long)K);
-  B2_CHECK_ARG(dtype == B2_F16 || dtype == B2_BF16, B2_ERR_DTYPE, "int8_matmul: dtype %d unsupported", dtype);
+  B2_CHECK_ARG(dtype == B2_F16 || dtype == B2_BF16 || dtype == B2_F32, B2_ERR_DTYPE,
+               "int8_matmul: dtype %d unsupported", dtype);
   B2_CHECK_ARG(M * N < (1ll << 31) && N * K < (1ll << 40), B2_ERR_UNSUPPORTED, "int8_matmul: too large");
   if (M == 0) return B2_OK;
   cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == B2_F32) return b2_detail_quant_f32(2, input, weight, output, scales, zeros, M, N, K, 0, st);
   const bool fast = M <= 16 && K % 64 == 0 && aligned(input, 16) && aligned(weight, 16);
   if (fast)
     return dtype == B2_F16 ? w8_dispatch<B2_F16>(input, weight, output, scales, zeros, M, N, K, st)
