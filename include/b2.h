@@ -65,8 +65,11 @@ B2_API int b2_device_error(void* stream, unsigned int* code);
  *   scales  : dtype [K/G, N]
  *   zeros   : NULL -> symmetric zero point 8 (the layout's default);
  *             else dtype [K/G, N] zero points (asymmetric).
- *   dtype   : B2_F16 or B2_BF16 for input, scales, zeros and output.
- * Chooses the decode GEMV (M <= 16) or the tcgen05 prefill GEMM (M > 16).
+ *   dtype   : B2_F16 or B2_BF16 for input, scales, zeros and output: the
+ *             decode GEMV (M <= 16) or the tcgen05 prefill GEMM (M > 16);
+ *             B2_F32 (the reference's own dtype) for input, scales, zeros
+ *             and output: the reference's arithmetic, (q - z) * s and every
+ *             product in fp32 on CUDA cores (K % 8 == 0, G % 8 == 0).
  */
 B2_API int b2_int4_matmul(const void* input, const void* weight, void* output,
                    const void* scales, const void* zeros,
@@ -80,6 +83,8 @@ B2_API int b2_int4_matmul(const void* input, const void* weight, void* output,
  * buffer order input, weight, output, scales, zeros, M, N, K at :2652-2661).
  *   weight  : int8 [N, K] (K-major, the reference layout)
  *   scales  : dtype [N];  zeros: NULL (symmetric) or dtype [N].
+ *   dtype   : B2_F16 / B2_BF16 (tensor cores), or B2_F32 (the reference's
+ *             dtype: fp32 (w - z) * s and fp32 products, K % 8 == 0).
  */
 B2_API int b2_int8_matmul(const void* input, const void* weight, void* output,
                    const void* scales, const void* zeros,
@@ -92,8 +97,10 @@ B2_API int b2_int8_matmul(const void* input, const void* weight, void* output,
  * :2705-2712): weight uint8 [N, K/2], byte j of row n = k 2j (low nibble)
  * and 2j+1 (high nibble) (:2725-2732); scales and zeros [N, K/G] in the
  * activation dtype (zeros NULL = 8); input [M, K], output [M, N].
- * M <= 16: K-major mma.sync GEMV (K % 128 == 0, G % 32 == 0); M > 16: the
- * tcgen05 prefill GEMM (K % 64 == 0, G % 64 == 0); else a generic kernel.
+ * 16-bit dtypes: M <= 16: K-major mma.sync GEMV (K % 128 == 0, G % 32 ==
+ * 0); M > 16: the tcgen05 prefill GEMM (K % 64 == 0, G % 64 == 0); else a
+ * generic kernel.  B2_F32 (the reference's buffers as they are): fp32
+ * scales / zeros / output and the reference's fp32 arithmetic.
  */
 B2_API int b2_int4_matmul_ref(const void* input, const void* weight, void* output,
                               const void* scales, const void* zeros,
@@ -211,7 +218,10 @@ B2_API int b2_repeat_kv(const void* input, void* output, int64_t n_kv_heads,
  *   q, k, v : dtype (B2_BF16) [B,T,H,Dk|Dv];  g : fp32 [B,T,H,Dk] log-decay
  *   beta    : dtype [B,T,H];  initial_state : fp32 [B,H,Dk,Dv] or NULL
  *   o       : dtype [B,T,H,Dv];  final_state : fp32 [B,H,Dk,Dv] or NULL
- *   workspace: device scratch of b2_kda_workspace_size(...) bytes.
+ *   workspace: device scratch of b2_kda_workspace_size(...) bytes
+ *             (80,384 bytes per (b, h, 64-step chunk)), 16-byte aligned.
+ * Two kernels: a per-chunk WY/UT transform on tcgen05 and a fused state +
+ * output recurrence; the state is carried in fp32.
  */
 B2_API size_t b2_kda_workspace_size(int64_t B, int64_t T, int64_t H,
                              int64_t Dk, int64_t Dv, int64_t chunk);
@@ -228,7 +238,7 @@ B2_API int b2_kda_fwd(const void* q, const void* k, const void* v, const float* 
  * input and output buffers).  No counterpart in the reference (which has no
  * KDA at all).  The workspace is a fixed 64 MiB device array inside the
  * library that every GPU loading it keeps until exit; shapes needing more
- * (B*H*(T/64) > 272) are rejected with B2_ERR_INVALID.  The first call on a
+ * (B*H*(T/64) > 834 chunk-heads) are rejected with B2_ERR_INVALID.  The first call on a
  * device looks up the array's address (do it before any stream capture).
  * All calls share the array: calls overlapping on the GPU race.
  */

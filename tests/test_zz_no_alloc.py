@@ -94,7 +94,7 @@ def test_noalloc_rejects_oversized_problem(cuda):
     from b200kern import _lib
     lib = _lib.load()
     q, k, v, g, beta = _inputs(cuda, 1, 64, 1, 0)
-    # 1 x 16384 x 32 needs 8192 chunk-heads of workspace, above the 272 the array holds
+    # 1 x 16384 x 32 needs 8192 chunk-heads of workspace, above the 834 the array holds
     st = lib.b2_kda_fwd_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), None,
                                 v.data_ptr(), None, 1, 16384, 32, 128, 128, 64, ctypes.c_float(0.088), 1,
                                 torch.cuda.current_stream().cuda_stream)

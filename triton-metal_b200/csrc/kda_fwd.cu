@@ -608,37 +608,34 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 
 // ---------------------------------------------------------------------------
 // Kernel B: fused state recurrence + outputs, one CTA per (b, h, 64 state
-// columns), 8 warps.  Warp (gq, kh) owns the 16 state columns v0 + 16 gq ..
-// + 15 and the 64 dk rows 64 kh .. 64 kh + 63 of the state.  Columns of the
-// state are independent (the transition acts on the Dk side only).  Each
-// warp holds its part of the transposed state S^T [Dv, Dk] in fp32 m16n8
-// accumulator fragments, whose fp16 copies are the A operands of the next
-// MMAs straight from registers:
-//   V'^T = U^T - S^T W^T                 (16 x 64, K = 128: two dk halves,
-//                                         partial sums swapped through smem)
-//   O^T  = S^T Qg^T + V'^T A_qk^T        (16 x 64; finished by the kh = 0 warp)
-//   S^T  = S^T o e^{G_last} + V'^T Kr    (16 x 64 per warp, K = 64)
-// W, Kr, Qg, A_qk, e^{G_last} and this CTA's U tile stream through a
-// two-stage ring, one bulk copy per tile group (the workspace block is laid
-// out like the stage); the B operands come out of it by ldmatrix (Kr
+// columns), 4 warps; warp w owns the 16 state columns dv0 = v0 + 16 w ..
+// dv0 + 15 for the whole sequence.  Columns of the state are independent (the
+// transition acts on the Dk side only), so a warp never waits for another
+// warp's state.  Everything runs on the transposed state S^T [Dv, Dk], held
+// in fp32 m16n8 accumulator fragments, whose fp16 copies are the A operands
+// of the next MMAs directly from registers:
+//   V'^T = U^T - S^T W^T                 (16 x 64, K = 128)
+//   O^T  = S^T Qg^T + V'^T A_qk^T        (16 x 64, K = 128 and K = 64, causal)
+//   S^T  = S^T o e^{G_last} + V'^T Kr    (16 x 128, K = 64)
+// W, Kr, Qg, A_qk, this CTA's U columns and e^{G_last} stream through a
+// two-stage cp.async ring; the B operands come out of it by ldmatrix (Kr
 // transposed).  S^T and V'^T enter the MMAs rounded to fp16 (10-bit
 // mantissa); the state itself stays fp32.  O leaves through a shared-memory
 // tile so that each output row is one coalesced store.
 // ---------------------------------------------------------------------------
-constexpr int RW = 8;                 // warps per CTA: 4 column groups x 2 dk halves
-constexpr int RV = 64;                // state columns per CTA
+constexpr int RW = 4;                 // warps per CTA
+constexpr int RV = 16 * RW;           // state columns per CTA
 constexpr int kRThreads = 32 * RW;
+static_assert(RV == 64, "a CTA reads one 64-column U tile of the workspace");
 // stage = the head's shared tiles (W, Kr, Qg, A_qk, e^{G_last}) + this CTA's U tile
 constexpr uint32_t kRStageBytes = kBShared + kBUTile;
 constexpr int LO = RV + 8;  // output staging row stride (elements)
-// partial sums exchanged between the two dk halves of a column group:
-// 8 partial V'^T tiles and 4 partial O^T tiles, 16 x 64 fp32 each
-constexpr uint32_t kXchBytes = (8 + 4) * 32 * 32 * 4;
 template <typename T>
 struct RecurCfg {
-  static constexpr int kStages = 2;
+  // three stages for 16-bit outputs; fp32 outputs need the room for a fp32 staging tile
+  static constexpr int kStages = sizeof(T) == 2 ? 3 : 2;
   static constexpr uint32_t kStaging = (uint32_t)C * LO * sizeof(T);
-  static constexpr size_t kSmem = (size_t)kStages * kRStageBytes + kStaging + kXchBytes + 64;
+  static constexpr size_t kSmem = (size_t)kStages * kRStageBytes + kStaging + 64;
 };
 
 // bulk copy global -> shared (no multicast), completion on an mbarrier
@@ -681,20 +678,14 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
   constexpr int NST = Cf::kStages;
   extern __shared__ __align__(128) uint8_t smb[];
   T* sO = reinterpret_cast<T*>(smb + NST * kRStageBytes);
-  float* xch = reinterpret_cast<float*>(smb + NST * kRStageBytes + Cf::kStaging);  // partial sums
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xch) + kXchBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smb + NST * kRStageBytes + Cf::kStaging);
   const int nc = Tlen / C;
   const int v0 = blockIdx.x * RV, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tq = lane & 3, mat = lane >> 3, r8 = lane & 7;
-  const int gq = warp & 3, kh = warp >> 2;  // 16 state columns gq, dk half kh
-  const int dv0 = v0 + 16 * gq, dk0 = 64 * kh;
+  const int dv0 = v0 + 16 * warp;
   const uint8_t* head = reinterpret_cast<const uint8_t*>(ws + ((size_t)b * H + h) * nc * kWsBlock);
   const size_t sbase = ((size_t)b * H + h) * DK * DV;
-  // partial-sum slots: [pair gq][half][fragment element][lane]
-  float* myP = xch + ((gq * 2 + kh) * 32) * 32;        // this warp's partial V'^T (S^T W^T)
-  float* otP = xch + ((gq * 2 + (kh ^ 1)) * 32) * 32;  // the partner's
-  float* oP = xch + (8 * 32 + gq * 32) * 32;            // partial O^T of the dk-half-1 warp
 
   if (tid == 0) {
     for (int i = 0; i < NST; ++i) mbar_init(&full[i], 1);
@@ -705,13 +696,13 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
     for (int i = 0; i < NST && i < nc; ++i)
       r_load_stage(smb + i * kRStageBytes, head + (size_t)i * kWsBlockBytes, blockIdx.x, &full[i]);
 
-  // S^T fragments of this warp's 16 columns x 64 dk: n-tile nt covers dk0 + 8 nt ..
-  float S[8][4];
+  // S^T fragments: n-tile nt covers dk 8 nt .. 8 nt + 7; e: (dv g | g + 8) x (dk 2 tq | 2 tq + 1)
+  float S[16][4];
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
+  for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int dk = dk0 + 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
+      const int dk = 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
       S[nt][e] = s0 ? s0[sbase + (size_t)dk * DV + dv] : 0.f;
     }
 
@@ -728,26 +719,38 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
     const __half* sAq = reinterpret_cast<const __half*>(st + kBAq);
     const float* sGl = reinterpret_cast<const float*>(st + kBGl);
     const __half* sU = reinterpret_cast<const __half*>(st + kBShared);
-
-    uint32_t sa[4][4];
+    // S^T as fp16 A fragments, one per 16-wide dk step
+    uint32_t sa[8][4];
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+    for (int kk = 0; kk < 8; ++kk) {
       sa[kk][0] = pack_h2(S[2 * kk][0], S[2 * kk][1]);
       sa[kk][1] = pack_h2(S[2 * kk][2], S[2 * kk][3]);
       sa[kk][2] = pack_h2(S[2 * kk + 1][0], S[2 * kk + 1][1]);
       sa[kk][3] = pack_h2(S[2 * kk + 1][2], S[2 * kk + 1][3]);
     }
-    // partial S^T W^T and S^T Qg^T over this warp's 64 dk
+    // acc = S^T W^T - U^T (= -V'^T), starting from -U^T read as C fragments
     float vp[8][4], oa[8][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int p = 0; p < 4; ++p) {
+      uint32_t u[4];
+      ldsm_x4_trans(smem_u32(sU + (8 * (2 * p + (mat >> 1)) + r8) * LUS + 16 * warp + ((mat & 1) << 3)), u);
+      const float2 a0 = unpack_h2(u[0]), a1 = unpack_h2(u[1]), a2 = unpack_h2(u[2]), a3 = unpack_h2(u[3]);
+      vp[2 * p][0] = -a0.x;
+      vp[2 * p][1] = -a0.y;
+      vp[2 * p][2] = -a1.x;
+      vp[2 * p][3] = -a1.y;
+      vp[2 * p + 1][0] = -a2.x;
+      vp[2 * p + 1][1] = -a2.y;
+      vp[2 * p + 1][2] = -a3.x;
+      vp[2 * p + 1][3] = -a3.y;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) vp[n][e] = oa[n][e] = 0.f;
+      for (int e = 0; e < 4; ++e) oa[2 * p][e] = oa[2 * p + 1][e] = 0.f;
+    }
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+    for (int kk = 0; kk < 8; ++kk) {
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
-        const int row = 16 * np + r8 + ((mat >> 1) << 3), col = dk0 + 16 * kk + ((mat & 1) << 3);
+        const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
         uint32_t bw[4], bq[4];
         ldsm_x4(smem_u32(sW + row * LR + col), bw);
         const uint32_t w0[2] = {bw[0], bw[1]}, w1[2] = {bw[2], bw[3]};
@@ -759,76 +762,34 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
         mma_16816<B2_F16>(oa[2 * np + 1], sa[kk], q1);
       }
     }
-    // exchange partials with the partner warp (same columns, other dk half)
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) myP[(4 * n + e) * 32 + lane] = vp[n][e];
-    if (kh == 1) {
-#pragma unroll
-      for (int n = 0; n < 8; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) oP[(4 * n + e) * 32 + lane] = oa[n][e];
-    }
-    asm volatile("bar.sync %0, 64;" ::"r"(1 + gq) : "memory");
-    // V'^T = U^T - (both partials), as fp16 A fragments over the chunk's 4 16-step blocks
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) vp[n][e] += otP[(4 * n + e) * 32 + lane];
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      uint32_t u[4];
-      ldsm_x4_trans(smem_u32(sU + (8 * (2 * p + (mat >> 1)) + r8) * LUS + 16 * gq + ((mat & 1) << 3)), u);
-      const float2 a0 = unpack_h2(u[0]), a1 = unpack_h2(u[1]), a2 = unpack_h2(u[2]), a3 = unpack_h2(u[3]);
-      vp[2 * p][0] = a0.x - vp[2 * p][0];
-      vp[2 * p][1] = a0.y - vp[2 * p][1];
-      vp[2 * p][2] = a1.x - vp[2 * p][2];
-      vp[2 * p][3] = a1.y - vp[2 * p][3];
-      vp[2 * p + 1][0] = a2.x - vp[2 * p + 1][0];
-      vp[2 * p + 1][1] = a2.y - vp[2 * p + 1][1];
-      vp[2 * p + 1][2] = a3.x - vp[2 * p + 1][2];
-      vp[2 * p + 1][3] = a3.y - vp[2 * p + 1][3];
-    }
+    // V'^T = -acc as fp16 A fragments over the chunk's 4 16-step blocks
     uint32_t va[4][4];
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      va[kk][0] = pack_h2(vp[2 * kk][0], vp[2 * kk][1]);
-      va[kk][1] = pack_h2(vp[2 * kk][2], vp[2 * kk][3]);
-      va[kk][2] = pack_h2(vp[2 * kk + 1][0], vp[2 * kk + 1][1]);
-      va[kk][3] = pack_h2(vp[2 * kk + 1][2], vp[2 * kk + 1][3]);
+      va[kk][0] = pack_h2(-vp[2 * kk][0], -vp[2 * kk][1]);
+      va[kk][1] = pack_h2(-vp[2 * kk][2], -vp[2 * kk][3]);
+      va[kk][2] = pack_h2(-vp[2 * kk + 1][0], -vp[2 * kk + 1][1]);
+      va[kk][3] = pack_h2(-vp[2 * kk + 1][2], -vp[2 * kk + 1][3]);
     }
-    if (kh == 0) {
-      // O^T = both S^T Qg^T partials + V'^T A_qk^T (A_qk[i][j] = 0 for j > i)
+    // O^T += V'^T A_qk^T: A_qk[i][j] = 0 for j > i, so key block kk only
+    // reaches query blocks np >= kk
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+    for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) oa[n][e] += oP[(4 * n + e) * 32 + lane];
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          if (np < kk) continue;
-          const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
-          uint32_t ba[4];
-          ldsm_x4(smem_u32(sAq + row * LA + col), ba);
-          const uint32_t a0[2] = {ba[0], ba[1]}, a1[2] = {ba[2], ba[3]};
-          mma_16816<B2_F16>(oa[2 * np], va[kk], a0);
-          mma_16816<B2_F16>(oa[2 * np + 1], va[kk], a1);
-        }
+      for (int np = 0; np < 4; ++np) {
+        if (np < kk) continue;
+        const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
+        uint32_t ba[4];
+        ldsm_x4(smem_u32(sAq + row * LA + col), ba);
+        const uint32_t a0[2] = {ba[0], ba[1]}, a1[2] = {ba[2], ba[3]};
+        mma_16816<B2_F16>(oa[2 * np], va[kk], a0);
+        mma_16816<B2_F16>(oa[2 * np + 1], va[kk], a1);
       }
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = 8 * nt + 2 * tq + (e & 1), dvl = 16 * gq + g + 8 * (e >> 1);
-          sO[t * LO + dvl] = from_f32<T>(oa[nt][e]);
-        }
     }
-    // S^T (this warp's dk half) = S^T o e^{G_last} + V'^T Kr
+    // S^T = S^T o e^{G_last} (per dk column) + V'^T Kr
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float2 gl = *reinterpret_cast<const float2*>(sGl + dk0 + 8 * nt + 2 * tq);
+    for (int nt = 0; nt < 16; ++nt) {
+      const float2 gl = *reinterpret_cast<const float2*>(sGl + 8 * nt + 2 * tq);
       S[nt][0] *= gl.x;
       S[nt][1] *= gl.y;
       S[nt][2] *= gl.x;
@@ -837,16 +798,23 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
+      for (int np = 0; np < 8; ++np) {
         uint32_t bk[4];
-        ldsm_x4_trans(smem_u32(sKr + (16 * kk + r8 + ((mat & 1) << 3)) * LR + dk0 + 16 * np + ((mat >> 1) << 3)),
-                      bk);
+        ldsm_x4_trans(smem_u32(sKr + (16 * kk + r8 + ((mat & 1) << 3)) * LR + 16 * np + ((mat >> 1) << 3)), bk);
         const uint32_t k0[2] = {bk[0], bk[1]}, k1[2] = {bk[2], bk[3]};
         mma_16816<B2_F16>(S[2 * np], va[kk], k0);
         mma_16816<B2_F16>(S[2 * np + 1], va[kk], k1);
       }
     }
-    __syncthreads();  // staging complete; every warp is done with stage sl and the partial slots
+    // O^T -> staging tile [t][dv], then coalesced rows of o
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = 8 * nt + 2 * tq + (e & 1), dvl = 16 * warp + g + 8 * (e >> 1);
+        sO[t * LO + dvl] = from_f32<T>(oa[nt][e]);
+      }
+    __syncthreads();  // staging complete; every warp is done with stage sl
     if (tid == 0 && c + NST < nc)
       r_load_stage(smb + sl * kRStageBytes, head + (size_t)(c + NST) * kWsBlockBytes, blockIdx.x, &full[sl]);
     constexpr int PER = 16 / sizeof(T);  // elements per 16-byte store
@@ -855,13 +823,14 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
       *reinterpret_cast<uint4*>(o + (((int64_t)b * Tlen + (int64_t)c * C + t) * H + h) * DV + v0 + PER * cc) =
           *reinterpret_cast<const uint4*>(sO + t * LO + PER * cc);
     }
+    __syncthreads();  // staging tile read before the next chunk writes it
   }
   if (s_out) {
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+    for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int dk = dk0 + 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
+        const int dk = 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
         s_out[sbase + (size_t)dk * DV + dv] = S[nt][e];
       }
   }
