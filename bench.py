@@ -236,6 +236,7 @@ def host_threads():
 # workload: W4A16 decode GEMV (C1)
 # --------------------------------------------------------------------------
 W4_N, W4_K, W4_G, W4_LAYERS = 11008, 4096, 128, 32
+KDA_HEADS = 0  # --heads: a smaller C4 (fewer heads) for profiler captures
 
 
 def w4_gemv_bytes(M, N=W4_N, K=W4_K, G=W4_G):
@@ -251,9 +252,9 @@ class W4Gemv:
     bound = "hbm"
     value_scale = 1e9
     peak_key, peak_unit = "hbm_gbs", "GB/s"
-    launches_per_step = W4_LAYERS
 
     def __init__(self, M, rank, device=True, N=W4_N, col0=0):
+        self.launches_per_step = W4_LAYERS
         import b200kern as bk
         from b200kern import _lib
         from b200kern.synthetic import w4_inputs
@@ -713,6 +714,7 @@ class KDA:
     def __init__(self, rank, device=True, B=1, T=16384, H=32, D=128, heads=None):
         import b200kern as bk
         self.bk = bk
+        H = KDA_HEADS or H
         gen = torch.Generator().manual_seed(rank)
         F = torch.nn.functional
         q = F.normalize(torch.randn(B, T, H, D, generator=gen), dim=-1).bfloat16()
@@ -1125,6 +1127,7 @@ def run_reference(args):
 
 
 def main():
+    global W4_LAYERS, KDA_HEADS
     faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1137,7 +1140,11 @@ def main():
     ap.add_argument("--sub", choices=["auto", "none"], default="auto",
                     help="auto: the default C1 run also measures the other configs as sub-records")
     ap.add_argument("--cpu-budget", type=float, default=5.0, help="seconds of CPU baseline sampling per record")
+    ap.add_argument("--layers", type=int, default=W4_LAYERS,
+                    help="GEMV weight copies per step (a smaller stack for profiler captures)")
+    ap.add_argument("--heads", type=int, default=0, help="kda: heads (a smaller C4 for profiler captures)")
     args = ap.parse_args()
+    W4_LAYERS, KDA_HEADS = args.layers, args.heads
     line = run_reference(args) if args.impl == "reference" else run_ours(args)
     if line is not None:
         print(json.dumps(line), flush=True)
