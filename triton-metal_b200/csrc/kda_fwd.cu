@@ -394,11 +394,8 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   float* sA = reinterpret_cast<float*>(sm + kSA);
   float* sAq = reinterpret_cast<float*>(sm + kSAq);
   float* sT = reinterpret_cast<float*>(sm + kST);
-  for (int e = tid; e < C * LT; e += kThreads) {
-    sA[e] = 0.f;
-    sAq[e] = 0.f;
-  }
-  __syncthreads();
+  // (no clearing: the read-back below writes every lower entry, T reads only
+  // lower entries of A_kk, and the A_qk store writes zeros above the diagonal)
   B2_PROF(3);
 
   // ---- 5. TMEM -> A_kk (times beta_i), A_qk: lane j = A-operand row; the
@@ -475,15 +472,9 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   }
   B2_PROF(5);
 
-  // ---- 6. A_qk -> workspace (fp16, zeros above the diagonal) ----
-  {
-    __half* wsAq = ws_h(blk, kBAq);
-    for (int e = tid; e < C * C / 2; e += kThreads) {
-      const int r = (2 * e) / C, c2 = (2 * e) % C;
-      *reinterpret_cast<__half2*>(wsAq + r * LA + c2) = __floats2half2_rn(sAq[r * LT + c2], sAq[r * LT + c2 + 1]);
-    }
-  }
-  // ---- 7. T = (I + A_kk)^-1: diagonal 16 x 16 blocks, column by column ----
+  // ---- 6 / 7. warps 0-1: T = (I + A_kk)^-1 on the diagonal 16 x 16 blocks,
+  // column by column; warps 2-7 meanwhile: A_qk -> workspace (fp16, zeros
+  // above the diagonal) and zeros of T above the diagonal blocks ----
   if (tid < C) {
     const int D = tid >> 4, jj = tid & 15, base = 16 * D;
     float col[16];
@@ -497,10 +488,17 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) sT[(base + i) * LT + base + jj] = col[i];
-  }
-  for (int e = tid; e < C * C; e += kThreads) {  // zero T above the diagonal blocks
-    const int i = e / C, jc = e % C;
-    if ((jc >> 4) > (i >> 4)) sT[i * LT + jc] = 0.f;
+  } else {
+    __half* wsAq = ws_h(blk, kBAq);
+    for (int e = tid - C; e < C * C / 2; e += kThreads - C) {
+      const int r = (2 * e) / C, c2 = (2 * e) % C;
+      const float a0 = c2 <= r ? sAq[r * LT + c2] : 0.f, a1 = c2 + 1 <= r ? sAq[r * LT + c2 + 1] : 0.f;
+      *reinterpret_cast<__half2*>(wsAq + r * LA + c2) = __floats2half2_rn(a0, a1);
+    }
+    for (int e = tid - C; e < C * C; e += kThreads - C) {
+      const int i = e / C, jc = e % C;
+      if ((jc >> 4) > (i >> 4)) sT[i * LT + jc] = 0.f;
+    }
   }
   __syncthreads();
   B2_PROF(6);

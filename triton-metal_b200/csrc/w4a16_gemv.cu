@@ -281,8 +281,14 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
     __syncwarp();
   }
   bool alive = mbar_wait(sbar, 0, err, 0xB2000003u);
-  for (int s = sid; s < ngroups && alive; s += kStageLanes) {
-    const int slot = s % stages;
+  // ring slot and fill parity of group s, advanced without divisions (s
+  // steps by the 8 stage lanes; stages is a multiple of 8 or covers every
+  // group, and gps is a power of two)
+  int slot = sid % stages;
+  uint32_t fill_par = (uint32_t)(sid / stages) & 1u;
+  for (int s = sid; s < ngroups && alive;
+       s += kStageLanes, slot += kStageLanes, fill_par ^= (slot >= stages) ? 1u : 0u,
+           slot -= (slot >= stages) ? stages : 0) {
     // x fragments of this group (L2 hits, or this warp's shared copy), loaded before the stage wait
     uint32_t bp[RQ][NT][4];
 #pragma unroll
@@ -307,22 +313,21 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
     // ds[n][.] = sum over the group's k of x[m], m = 8n + 2t (+1), via MMA
     float ds[NT][2][4];
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) ds[n][j][c] = 0.f;
-#pragma unroll
     for (int rq = 0; rq < RQ; ++rq)
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         const uint32_t b0[2] = {bp[rq][n][0], bp[rq][n][1]};
         const uint32_t b1[2] = {bp[rq][n][2], bp[rq][n][3]};
-        mma_16816<DT>(ds[n][0], ones, b0);
-        mma_16816<DT>(ds[n][1], ones, b1);
+        if (rq == 0) {
+          mma_16816_z<DT>(ds[n][0], ones, b0);
+          mma_16816_z<DT>(ds[n][1], ones, b1);
+        } else {
+          mma_16816<DT>(ds[n][0], ones, b0);
+          mma_16816<DT>(ds[n][1], ones, b1);
+        }
       }
-    const int slot0 = slot - slot % gps;  // first slot of this group's box
-    if (!mbar_wait(&full[slot0], (s / stages) & 1, err, 0xB2000002u)) {
+    const int slot0 = slot & ~(gps - 1);  // first slot of this group's box
+    if (!mbar_wait(&full[slot0], fill_par, err, 0xB2000002u)) {
       alive = false;
       break;
     }
@@ -334,16 +339,9 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
 #pragma unroll
     for (int ip = 0; ip < MPW; ip += 2) {
       if (ch + NCH * ip < nmt) {
-        // two m-tiles x two k-steps -> 4*NT independent MMA chains
+        // two m-tiles x two k-steps -> 4*NT independent MMA chains (the first
+        // MMA of each chain starts from a zero accumulator)
         float cg[2][2][NT][4];
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-#pragma unroll
-              for (int c = 0; c < 4; ++c) cg[i][j][n][c] = 0.f;
         uint2 wv[2][RQ];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -371,8 +369,13 @@ w4_gemv_stream_kernel(const __grid_constant__ GemvMaps maps, const uint16_t* __r
             for (int n = 0; n < NT; ++n) {
               const uint32_t b0[2] = {bp[rq][n][0], bp[rq][n][1]};
               const uint32_t b1[2] = {bp[rq][n][2], bp[rq][n][3]};
-              mma_16816<DT>(cg[i][0][n], a0, b0);
-              mma_16816<DT>(cg[i][1][n], a1, b1);
+              if (rq == 0) {
+                mma_16816_z<DT>(cg[i][0][n], a0, b0);
+                mma_16816_z<DT>(cg[i][1][n], a1, b1);
+              } else {
+                mma_16816<DT>(cg[i][0][n], a0, b0);
+                mma_16816<DT>(cg[i][1][n], a1, b1);
+              }
             }
           }
         }
