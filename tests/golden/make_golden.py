@@ -1,7 +1,8 @@
 """Generate the golden fixtures in this folder from the reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-REFERENCE_ROOT (default /root/reference); the GPU box never runs this.
+Run in a container that has the reference checkout (read-only); its path
+must be given in the REFERENCE_ROOT environment variable.  The GPU box never
+runs this.
 
 Two sources of golden vectors:
  1. The reference's own hot-path tests in tests/test_emitter.py are executed
@@ -30,7 +31,9 @@ import numpy as np
 sys.dont_write_bytecode = True
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("REFERENCE_ROOT")
+if not REF:
+    raise SystemExit("set REFERENCE_ROOT to the reference checkout (bledden/triton-metal)")
 sys.path.insert(0, REPO)
 from oracle import attention as oatt  # noqa: E402
 from oracle import quant as oq  # noqa: E402
