@@ -12,7 +12,8 @@
 //                                                          -> b2_int4_matmul
 //           (reference int4_matmul, _msl_templates.py:2716-2743)
 //
-// Persistent, warp-specialised CTA (one per SM), tile 128 x 256 x 64:
+// Persistent, warp-specialised CTA (one per SM), tile 128 x bn x 64 (bn <= 256
+// picked per launch to fill the last round of tiles):
 //   warp 0      TMA producer: x tile (and W tile / packed W tile) per k-block
 //               into a ring of shared-memory stages (128B-swizzled, no
 //               multicast);
@@ -73,6 +74,8 @@ struct Params {
   const uint16_t* zeros;   // same shape as scales, or null (symmetric)
   uint16_t* out;
   int tiles_m, tiles_n;
+  int bn;          // CTA tile width in columns (<= BN, multiple of 32), chosen per launch
+  uint32_t idesc;  // MMA instruction descriptor for M = 128, N = bn
   unsigned* err;
 };
 
@@ -263,13 +266,14 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * BN;
+        const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * p.bn;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_or_abort(&empty[stage], phase ^ 1, p, 0xB2100001u, abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t bytes = C::kABytesC + (MODE == 0 ? kBBytes : C::kPackedBytes);
+          // the B box is bn rows (MODE 2: bn columns of 8 int32 rows)
+          const uint32_t bytes = C::kABytesC + (uint32_t)p.bn * (MODE == 0 ? BK * 2 : (MODE == 1 ? BK : BK / 2));
           mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d(sA + stage * C::kABytesC, &tmA, kb * BK, m0, &full[stage]);
           if constexpr (MODE == 0) tma_load_2d(sB + stage * kBBytes, &tmB, kb * BK, n0, &full[stage]);
@@ -286,7 +290,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   } else if (warp == 1) {
     // ------------------------------ MMA issuer --------------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_f16(BM, BN, DT == B2_BF16);
+      const uint32_t idesc = p.idesc;
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -374,7 +378,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
-      const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * BN;
+      const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * p.bn;
       const int acc = C::TWO ? 0 : (it & 1);
       const uint32_t acc_phase = C::TWO ? (it & 1) : ((it >> 1) & 1);
       if (!wait_or_abort(&tfull[acc], acc_phase, p, 0xB2100005u, abort_flag)) break;
@@ -396,7 +400,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const uint32_t tcol = C::TWO ? h * kAccCols : acc * kAccCols;
         uint16_t* orow = p.out + (size_t)row * p.N + n0;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < p.bn / 32; ++c) {
           uint32_t r[32];
           // warp-collective: every lane loads, rows / columns past the edge
           // only skip their stores
@@ -442,14 +446,15 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     const int d = (warp - 6) * 32 + lane;
     const int n = d & (BN - 1);  // B row (output column) this thread fills
     const int h = d / BN;        // which half of the row's 64 k
+    const bool n_in = n < p.bn;  // threads past the tile width only keep the barrier counts
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     int tile_it = 0;
     int kbi = 0;  // k-blocks dequantised so far (B buffer of the W8 mode)
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tile_it) {
-      const int n0 = (tile / p.tiles_m) * BN;
-      const bool col_ok = n0 + n < p.N;
+      const int n0 = (tile / p.tiles_m) * p.bn;
+      const bool col_ok = n_in && n0 + n < p.N;
       uint32_t s2 = 0, bz2 = 0, zr2 = 0;
       float xsum = 0.f;  // W8 with zeros: this thread's quarter of an x row
       int cur_group = -1;
@@ -478,12 +483,13 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         }
         uint8_t* brow = sB + bb * kBBytes + n * 128;
         const int sw = n & 7;
-        if constexpr (MODE == 2) {
+        if (!n_in) {
+        } else if constexpr (MODE == 2) {
           const uint32_t* pk = reinterpret_cast<const uint32_t*>(sP + stage * C::kPackedBytes);
 #pragma unroll
           for (int rr = 0; rr < BK / 16; ++rr) {
             const int r = h * (BK / 16) + rr;
-            const uint4 v = dequant8_int4<DT, ZP>(pk[r * BN + n], s2, bz2, zr2);
+            const uint4 v = dequant8_int4<DT, ZP>(pk[r * p.bn + n], s2, bz2, zr2);
             *reinterpret_cast<uint4*>(brow + ((r ^ sw) << 4)) = v;
           }
         } else if constexpr (MODE == 3) {
@@ -555,6 +561,25 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 
 }  // namespace gemm
 
+// Tile width for a persistent grid of `sms` CTAs: the tiles of the last
+// round leave SMs idle, so a narrower tile that fills the rounds better can
+// finish first (C2: N = 14336, 16 row tiles -> 896 tiles of 256 columns =
+// 6.05 rounds of 148, or 1024 tiles of 224 = 6.92 rounds).  Cost model:
+// rounds x (bn + 32), the 32 standing for the per-tile A stream and epilogue.
+static int pick_bn(int tiles_m, int64_t N, int sms) {
+  int best = gemm::BN;
+  int64_t best_cost = -1;
+  for (int bn = gemm::BN; bn >= 128; bn -= 32) {
+    const int64_t tiles = (int64_t)tiles_m * ((N + bn - 1) / bn);
+    const int64_t cost = ((tiles + sms - 1) / sms) * (bn + 32);
+    if (best_cost < 0 || cost < best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 template <int MODE, int DT, bool ZP>
 static int launch_gemm(const void* x, const void* w, const void* scales, const void* zeros, void* out, int64_t M,
                        int64_t N, int64_t K, int64_t G, cudaStream_t st) {
@@ -568,17 +593,19 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
     return B2_ERR_LAUNCH;
   }
   const CUtensorMapDataType adt = DT == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int grid = num_sms();
+  const int bn = pick_bn((int)((M + C::BMC - 1) / C::BMC), N, grid);
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, x, adt, K, M, K * 2, BK, C::BMC, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ERR_INVALID;
   bool okb;
   if (MODE == 0)
-    okb = make_tmap_2d(&tb, w, adt, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    okb = make_tmap_2d(&tb, w, adt, K, N, K * 2, BK, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   else if (MODE == 1)
-    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, BK, BN);
+    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, BK, bn);
   else if (MODE == 2)
-    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, N, K / 8, N * 4, BN, BK / 8);
+    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, N, K / 8, N * 4, bn, BK / 8);
   else
-    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, BK / 2, BN);
+    okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, BK / 2, bn);
   if (!okb) return B2_ERR_INVALID;
   Params p;
   p.M = (int)M;
@@ -589,10 +616,11 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   p.zeros = (const uint16_t*)zeros;
   p.out = (uint16_t*)out;
   p.tiles_m = (int)((M + C::BMC - 1) / C::BMC);
-  p.tiles_n = (int)((N + BN - 1) / BN);
+  p.tiles_n = (int)((N + bn - 1) / bn);
+  p.bn = bn;
+  p.idesc = tc::idesc_f16(BM, bn, DT == B2_BF16);
   p.err = err;
   const int ntiles = p.tiles_m * p.tiles_n;
-  int grid = num_sms();
   if (grid > ntiles) grid = ntiles;
   auto kern = wxa16_gemm_kernel<MODE, DT, ZP>;
   set_max_smem((const void*)kern, (int)C::kSmem);
