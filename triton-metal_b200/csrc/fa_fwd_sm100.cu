@@ -254,12 +254,8 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npairs = (p.q_tiles + 1) / 2;
-  // 1-D grid, longest causal pairs first across all heads and batches (the
-  // last CTAs to start are the shortest, so the final round ends together);
-  // the heads of one GQA group are neighbours and read the same K/V
-  const int hb = p.Hq * p.B;
-  const int pi = npairs - 1 - (int)(blockIdx.x / hb);
-  const int h = (int)(blockIdx.x % hb) % p.Hq, b = (int)(blockIdx.x % hb) / p.Hq;
+  const int pi = npairs - 1 - (int)blockIdx.x;  // longest causal pairs first
+  const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hkv);
   const int nkv_all = (p.Skv + BKV - 1) / BKV;
   // Tile u visits KV tiles kb[u] .. nkv[u]-1 (kb > 0 only with a sliding
@@ -688,7 +684,7 @@ static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int
   const bool shape_ok = (D == 128 && dtype != B2_F32) || D == 64;
   const bool fast = shape_ok && Skv > 0 && strides_ok(qs, dtype) && strides_ok(ks, dtype) && strides_ok(vs, dtype) &&
                     strides_ok(os, dtype) && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(o, 16) &&
-                    ((Sq + 2 * fa::BQ - 1) / (2 * fa::BQ)) * Hq * B < (int64_t)1 << 31;
+                    B <= 65535 && Hq <= 65535;
   if (fast) {
     unsigned* err = device_error_word();
     CUtensorMap tq, tk, tv;
@@ -709,7 +705,7 @@ static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int
       p.os_h = os[1];
       p.os_s = os[2];
       p.err = err;
-      dim3 grid((unsigned)(((p.q_tiles + 1) / 2) * Hq * B));
+      dim3 grid((p.q_tiles + 1) / 2, (unsigned)Hq, (unsigned)B);
       if (D == 128) {
         if (dtype == B2_F16) launch_fa_tc<128, fa::kF16>(tq, tk, tv, p, grid, st);
         else launch_fa_tc<128, fa::kBF16>(tq, tk, tv, p, grid, st);
