@@ -15,7 +15,8 @@
 //               for the two tiles in ping-pong order
 //   warps 4-11  two softmax warpgroups (one per Q tile), one query row per
 //               thread (TMEM lane = row): row max in the log2 domain,
-//               p = exp2(s - m), row sum, P as bf16 written back into TMEM
+//               p = exp2(s - m) (a third of them by a polynomial on the
+//               FMA pipe, the rest on MUFU), row sum, P as bf16 written back into TMEM
 //               over its S columns; O is rescaled in TMEM only when the
 //               running max grows by more than 8 (2^8 headroom in P).
 //               Final O / l -> global.
@@ -165,52 +166,114 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Paired fp32 arithmetic of sm_100 (one instruction for two lanes of a
+// 64-bit register pair) and the 3-input max: the softmax warps issue one
+// instruction per two scores for the scale, the row sum and the max.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// exp2 of two lanes on the FMA pipe, to take part of the softmax's
+// exponentials off the MUFU unit (the method of FlashAttention-4: Cody-Waite
+// split x = j + f, j = rint(x), |f| <= 1/2, then a polynomial for 2^f and j
+// added into the exponent field).  The cubic is this file's own relative
+// minimax fit of 2^f on [-1/2, 1/2] (max relative error 7.5e-5, below the
+// 2^-9 / 2^-12 rounding of the 16-bit P it feeds).  x <= 8 here; x is clamped
+// at -125 so that 2^j stays a normal number.
+__device__ __forceinline__ uint64_t exp2_poly_f2(uint64_t x2) {
+  const uint64_t x = f2_pack(fmaxf(f2_lo(x2), -125.f), fmaxf(f2_hi(x2), -125.f));
+  const float kRound = 12582912.f;  // 1.5 * 2^23: x + kRound rounds x to an integer in the low mantissa bits
+  const uint64_t t = add_f2(x, f2_pack(kRound, kRound));
+  const uint64_t j = add_f2(t, f2_pack(-kRound, -kRound));
+  const uint64_t fr = fma_f2(j, f2_pack(-1.f, -1.f), x);
+  uint64_t q = fma_f2(f2_pack(0.05517132f, 0.05517132f), fr, f2_pack(0.24261054f, 0.24261054f));
+  q = fma_f2(q, fr, f2_pack(0.69326097f, 0.69326097f));
+  q = fma_f2(q, fr, f2_pack(0.99992812f, 0.99992812f));
+  // bits(t) = 0x4B400000 + j, so bits(t) << 23 = j << 23 (mod 2^32)
+  const uint32_t lo = (uint32_t)t * (1u << 23) + (uint32_t)q;
+  const uint32_t hi = (uint32_t)(t >> 32) * (1u << 23) + (uint32_t)(q >> 32);
+  return (uint64_t)lo | ((uint64_t)hi << 32);
+}
+
+__device__ __forceinline__ bool key_masked(int kv, int qpos, const Params& p) {
+  return kv >= p.Skv || (p.causal && kv > qpos) || (p.window > 0 && kv <= qpos - p.window);
+}
+
 // Row max of the raw S row (this thread's TMEM lane), masked keys -> -inf.
 template <bool MASK>
 __device__ __forceinline__ float row_max(uint32_t tS, int kv0, int qpos, const Params& p) {
   float mx = -INFINITY;
+  // two 32-column loads per wait: 64 columns in flight
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    uint32_t sv[32];
-    tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
+  for (int c = 0; c < 4; c += 2) {
+    uint32_t sv[64];
+    tc::tmem_ld_32x32b_x32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
+    tc::tmem_ld_32x32b_x32(tS + 32 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
     tc::tmem_ld_wait();
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      float v = __uint_as_float(sv[e]);
+    for (int e = 0; e < 64; e += 2) {
+      float v0 = __uint_as_float(sv[e]), v1 = __uint_as_float(sv[e + 1]);
       if constexpr (MASK) {
         const int kv = kv0 + 32 * c + e;
-        if (kv >= p.Skv || (p.causal && kv > qpos) || (p.window > 0 && kv <= qpos - p.window)) v = -INFINITY;
+        if (key_masked(kv, qpos, p)) v0 = -INFINITY;
+        if (key_masked(kv + 1, qpos, p)) v1 = -INFINITY;
       }
-      mx = fmaxf(mx, v);
+      mx = max3(mx, v0, v1);
     }
   }
   return mx;
 }
 
 // p = exp2(s * scale_log2 - m) written over the S columns (P for the TMEM-A
-// MMA): 16-bit pairs, or fp32 for the tf32 path; returns the row sum of p.
+// MMA): 16-bit pairs, or fp32 for the tf32 path; returns the row sum of p
+// (two partial sums, even and odd keys, in one register pair).
 template <bool MASK, int FMT>
 __device__ __forceinline__ float exp_to_p(uint32_t tS, int kv0, int qpos, float mref, const Params& p) {
-  float rs0 = 0.f, rs1 = 0.f;
-  const float sc = p.scale_log2;
+  uint64_t rs = 0;
+  const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(-mref, -mref);
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    uint32_t sv[32];
-    tc::tmem_ld_32x32b_x32(tS + 32 * c, sv);
+  for (int c = 0; c < 4; c += 2) {
+    uint32_t sv[64];
+    tc::tmem_ld_32x32b_x32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
+    tc::tmem_ld_32x32b_x32(tS + 32 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
     tc::tmem_ld_wait();
-    uint32_t pk[16];
+    uint32_t pk[32];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      float p0 = ex2(fmaf(__uint_as_float(sv[2 * e]), sc, -mref));
-      float p1 = ex2(fmaf(__uint_as_float(sv[2 * e + 1]), sc, -mref));
+    for (int e = 0; e < 32; ++e) {
+      const uint64_t x = fma_f2((uint64_t)sv[2 * e] | ((uint64_t)sv[2 * e + 1] << 32), sc2, nm2);
+      float p0, p1;
+      // ~1/3 of the pairs on the FMA pipe (measured at C3: 1/4 and 1/3 both
+      // ~1020 TF/s, 3/8 ~1005, 1/2 ~965; all-MUFU ~970)
+      if (FMT != kTF32 && e % 3 == 2) {
+        const uint64_t y = exp2_poly_f2(x);
+        p0 = f2_lo(y);
+        p1 = f2_hi(y);
+      } else {
+        p0 = ex2(f2_lo(x));
+        p1 = ex2(f2_hi(x));
+      }
       if constexpr (MASK) {
         const int kv = kv0 + 32 * c + 2 * e;
-        if (kv >= p.Skv || (p.causal && kv > qpos) || (p.window > 0 && kv <= qpos - p.window)) p0 = 0.f;
-        if (kv + 1 >= p.Skv || (p.causal && kv + 1 > qpos) || (p.window > 0 && kv + 1 <= qpos - p.window))
-          p1 = 0.f;
+        if (key_masked(kv, qpos, p)) p0 = 0.f;
+        if (key_masked(kv + 1, qpos, p)) p1 = 0.f;
       }
-      rs0 += p0;
-      rs1 += p1;
+      rs = add_f2(rs, f2_pack(p0, p1));
       if constexpr (FMT == kF16) {
         __half2 hv = __floats2half2_rn(p0, p1);
         pk[e] = *reinterpret_cast<uint32_t*>(&hv);
@@ -222,10 +285,14 @@ __device__ __forceinline__ float exp_to_p(uint32_t tS, int kv0, int qpos, float 
         sv[2 * e + 1] = __float_as_uint(p1);
       }
     }
-    if constexpr (FMT == kTF32) tmem_st_32x32b_x32(tS + 32 * c, sv);
-    else tmem_st_32x32b_x16(tS + 16 * c, pk);
+    if constexpr (FMT == kTF32) {
+      tmem_st_32x32b_x32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
+      tmem_st_32x32b_x32(tS + 32 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+    } else {
+      tmem_st_32x32b_x32(tS + 16 * c, pk);
+    }
   }
-  return rs0 + rs1;
+  return f2_lo(rs) + f2_hi(rs);
 }
 
 template <int HD, int FMT>
