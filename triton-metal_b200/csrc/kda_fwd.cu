@@ -36,27 +36,30 @@ namespace kda {
 
 constexpr int C = 64, DK = 128, DV = 128;
 
-// Workspace block per (b, h, chunk), laid out exactly as kernel B's shared
-// memory stage so that one bulk copy moves it: fp16 W, K e^{G_last - G} and
-// scale Q e^G [64][136] (rows padded by 8 halves: ldmatrix rows on distinct
-// banks), fp16 A_qk [64][72], fp32 e^{G_last} [128], then fp16 U for state
-// columns 0-63 and 64-127 as two [64][72] tiles.  80,384 bytes.  The fp16
-// tiles only feed 10-bit-mantissa MMA operands and are O(1); the state itself
-// is carried in fp32 registers.
+// Workspace block per (b, h, chunk), laid out as kernel B's shared-memory
+// stages so that bulk copies move it: fp16 W and K e^{G_last - G} [64][136]
+// (rows padded by 8 halves: ldmatrix rows on distinct banks), fp32
+// e^{G_last} [128] (the state CTA's part), fp16 scale Q e^G [64][136] and
+// A_qk [64][72] (the output CTA's part), then fp16 U for state columns 0-63
+// and 64-127 as two [64][72] tiles.  80,384 bytes.  The fp16 tiles only feed
+// 10-bit-mantissa MMA operands and are O(1); the state itself is carried in
+// fp32 registers.
 constexpr int LR = DK + 8;    // halves: W, Kr, Qg rows
 constexpr int LA = C + 8;     // halves: A_qk rows
 constexpr int LUS = 64 + 8;   // halves: rows of one 64-column U tile
 constexpr uint32_t kBW = 0;
 constexpr uint32_t kBKr = kBW + C * LR * 2;
-constexpr uint32_t kBQg = kBKr + C * LR * 2;
+constexpr uint32_t kBGl = kBKr + C * LR * 2;
+constexpr uint32_t kBQg = kBGl + DK * 4;
 constexpr uint32_t kBAq = kBQg + C * LR * 2;
-constexpr uint32_t kBGl = kBAq + C * LA * 2;
-constexpr uint32_t kBShared = kBGl + DK * 4;   // bytes every CTA of the head reads
-constexpr uint32_t kBUTile = C * LUS * 2;      // one U tile
-constexpr uint32_t kBU = kBShared;             // U tile h at kBU + h * kBUTile
+constexpr uint32_t kBShared = kBAq + C * LA * 2;  // bytes shared by the head's CTAs
+constexpr uint32_t kBUTile = C * LUS * 2;          // one U tile
+constexpr uint32_t kBU = kBShared;                 // U tile h at kBU + h * kBUTile
 constexpr uint32_t kWsBlockBytes = kBU + 2 * kBUTile;
-constexpr size_t kWsBlock = kWsBlockBytes / 4;  // floats
-static_assert(kBShared % 16 == 0 && kBUTile % 16 == 0, "bulk copy sizes");
+constexpr size_t kWsBlock = kWsBlockBytes / 4;     // floats
+constexpr uint32_t kBStatePart = kBQg;             // [0, kBQg): W, Kr, e^{G_last}
+constexpr uint32_t kBOutPart = kBShared - kBQg;    // [kBQg, kBShared): Qg, A_qk
+static_assert(kBQg % 16 == 0 && kBShared % 16 == 0 && kBUTile % 16 == 0, "bulk copy sizes");
 __device__ __forceinline__ __half* ws_h(float* blk, uint32_t byte_off) {
   return reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(blk) + byte_off);
 }
@@ -184,12 +187,21 @@ struct Pair {
 // (-DB2_KDA_PROFILE); the product build has no hook.
 #ifdef B2_KDA_PROFILE
 __device__ unsigned long long g_kda_prof[64][16];
+__device__ unsigned long long g_kda_rprof[2][8][256];
+#define B2_RPROF(k, c)                                                                       \
+  do {                                                                                       \
+    if (lane == 0 && warp == 0 && blockIdx.x < 2 && blockIdx.y == 0 && blockIdx.z == 0 && (c) < 256) \
+      g_kda_rprof[rank][k][c] = globaltimer_ns();                                             \
+  } while (0)
 #define B2_PROF(i)                                                                  \
   do {                                                                              \
     if (threadIdx.x == 0 && blockIdx.x < 64 && blockIdx.y == 0 && blockIdx.z == 0)  \
       g_kda_prof[blockIdx.x][i] = globaltimer_ns();                                 \
   } while (0)
 #else
+#define B2_RPROF(k, c) \
+  do {                 \
+  } while (0)
 #define B2_PROF(i) \
   do {             \
   } while (0)
@@ -605,36 +617,55 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 }
 
 // ---------------------------------------------------------------------------
-// Kernel B: fused state recurrence + outputs, one CTA per (b, h, 64 state
-// columns), 4 warps; warp w owns the 16 state columns dv0 = v0 + 16 w ..
-// dv0 + 15 for the whole sequence.  Columns of the state are independent (the
-// transition acts on the Dk side only), so a warp never waits for another
-// warp's state.  Everything runs on the transposed state S^T [Dv, Dk], held
-// in fp32 m16n8 accumulator fragments, whose fp16 copies are the A operands
-// of the next MMAs directly from registers:
-//   V'^T = U^T - S^T W^T                 (16 x 64, K = 128)
-//   O^T  = S^T Qg^T + V'^T A_qk^T        (16 x 64, K = 128 and K = 64, causal)
-//   S^T  = S^T o e^{G_last} + V'^T Kr    (16 x 128, K = 64)
-// W, Kr, Qg, A_qk, this CTA's U columns and e^{G_last} stream through a
-// two-stage cp.async ring; the B operands come out of it by ldmatrix (Kr
-// transposed).  S^T and V'^T enter the MMAs rounded to fp16 (10-bit
-// mantissa); the state itself stays fp32.  O leaves through a shared-memory
-// tile so that each output row is one coalesced store.
+// Kernel B: state recurrence + outputs on a cluster of two CTAs per (b, h, 64
+// state columns), 4 warps each; warp w of both CTAs owns the 16 state
+// columns dv0 = v0 + 16 w .. dv0 + 15 for the whole sequence.  Columns of the
+// state are independent (the transition acts on the Dk side only), so a warp
+// never waits for another warp's state.  Everything runs on the transposed
+// state S^T [Dv, Dk], held in fp32 m16n8 accumulator fragments, whose fp16
+// copies are the A operands of the MMAs directly from registers.
+//   state CTA (rank 0), the sequential chain:
+//     V'^T = U^T - S^T W^T                 (16 x 64, K = 128)
+//     S^T  = S^T o e^{G_last} + V'^T Kr    (16 x 128, K = 64)
+//   output CTA (rank 1), off the chain:
+//     O^T  = S^T Qg^T + V'^T A_qk^T        (16 x 64, K = 128 and K = 64, causal)
+// Per chunk, each lane of a state warp sends its fp16 A fragments of S^T
+// (before the update) and V'^T into the output CTA's shared memory
+// (distributed shared memory, a two-slot ring per warp): the lanes stage them
+// in a local slot, one lane bulk-copies the warp's 6 KB across, completing
+// the slot's mbarrier transaction there; the output warp of the same columns
+// reads them back lane for lane, re-arms the slot and releases it to the
+// state warp.  (Per-lane remote stores cost 0.4 us per chunk on the state
+// chain, 0.9 us with a release-arrive after them.)  Each CTA streams its part of the workspace block (W, Kr,
+// e^{G_last} and its U tile; Qg and A_qk) through its own bulk-copy ring; the
+// B operands come out of it by ldmatrix (Kr transposed).  S^T and V'^T enter
+// the MMAs rounded to fp16 (10-bit mantissa); the state itself stays fp32.
+// O leaves through a shared-memory tile so that each output row is one
+// coalesced store.  Every wait is bounded; both CTAs meet at a cluster
+// barrier before either exits, so no shared-memory access targets a CTA that
+// has left.
 // ---------------------------------------------------------------------------
 constexpr int RW = 4;                 // warps per CTA
-constexpr int RV = 16 * RW;           // state columns per CTA
+constexpr int RV = 16 * RW;           // state columns per CTA pair
 constexpr int kRThreads = 32 * RW;
-static_assert(RV == 64, "a CTA reads one 64-column U tile of the workspace");
-// stage = the head's shared tiles (W, Kr, Qg, A_qk, e^{G_last}) + this CTA's U tile
-constexpr uint32_t kRStageBytes = kBShared + kBUTile;
-constexpr int LO = RV + 8;  // output staging row stride (elements)
-template <typename T>
-struct RecurCfg {
-  // three stages for 16-bit outputs; fp32 outputs need the room for a fp32 staging tile
-  static constexpr int kStages = sizeof(T) == 2 ? 3 : 2;
-  static constexpr uint32_t kStaging = (uint32_t)C * LO * sizeof(T);
-  static constexpr size_t kSmem = (size_t)kStages * kRStageBytes + kStaging + 64;
-};
+static_assert(RV == 64, "a cluster reads one 64-column U tile of the workspace");
+constexpr int LO = RV + 8;            // output staging row stride (elements)
+constexpr uint32_t kStage0 = kBStatePart + kBUTile;  // state CTA stage: W, Kr, e^{G_last}, U tile
+constexpr uint32_t kStage1 = kBOutPart;              // output CTA stage: Qg, A_qk
+constexpr int kNS0 = 4, kNS1 = 3;
+constexpr int kSlotWords = 48;                         // per lane: S^T (8 x 4) + V'^T (4 x 4) fragments
+constexpr uint32_t kSlotWarp = 32 * kSlotWords * 4;    // 6 KB
+constexpr uint32_t kSlotBytes = RW * kSlotWarp;        // 24 KB per chunk
+constexpr uint32_t kSlots1 = kNS1 * kStage1;           // output CTA: ring, then 2 slots, then staging
+constexpr uint32_t kStaging1 = kSlots1 + 2 * kSlotBytes;
+constexpr uint32_t kEnd1 = kStaging1 + C * LO * 4;     // (fp32 staging covers every output type)
+constexpr uint32_t kSlots0 = kNS0 * kStage0;           // state CTA: ring, then 2 local staging slots
+constexpr uint32_t kEnd0 = kSlots0 + 2 * kSlotBytes;
+constexpr uint32_t kRBar = kEnd0 > kEnd1 ? kEnd0 : kEnd1;
+// barriers: full0[kNS0], dempty[2][RW] (state CTA); full1[kNS1], dfull[2][RW] (output CTA)
+constexpr uint32_t kRSmem = kRBar + 8 * (kNS0 + kNS1 + 4 * RW);
+static_assert(kRSmem <= 227 * 1024, "kernel B shared memory");
+static_assert(kStage0 % 16 == 0 && kStage1 % 16 == 0 && kSlots1 % 16 == 0, "bulk copy / vector alignment");
 
 // bulk copy global -> shared (no multicast), completion on an mbarrier
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -644,10 +675,59 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-__device__ __forceinline__ void r_load_stage(uint8_t* st, const uint8_t* blk, int utile, uint64_t* bar) {
-  mbar_arrive_expect_tx(bar, kRStageBytes);
-  bulk_g2s(st, blk, kBShared, bar);
-  bulk_g2s(st + kBShared, blk + kBU + utile * kBUTile, kBUTile, bar);
+__device__ __forceinline__ void r_load_stage0(uint8_t* st, const uint8_t* blk, int utile, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, kStage0);
+  bulk_g2s(st, blk, kBStatePart, bar);
+  bulk_g2s(st + kBStatePart, blk + kBU + utile * kBUTile, kBUTile, bar);
+}
+__device__ __forceinline__ void r_load_stage1(uint8_t* st, const uint8_t* blk, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, kStage1);
+  bulk_g2s(st, blk + kBQg, kBOutPart, bar);
+}
+
+// ---- cluster helpers ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of this CTA's shared-memory location `p` in CTA `rank`
+__device__ __forceinline__ uint32_t map_rank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// bulk copy of this CTA's shared memory into a partner CTA's (no multicast);
+// the bytes count against the transaction count of the mbarrier `mbar` there
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(mbar)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// bounded wait that acquires at cluster scope (the arrivals come from the partner CTA)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255u) == 255u && globaltimer_ns() - t0 > kWaitNs) break;
+  }
+  atomicCAS(err, 0u, code);
+  return false;
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
@@ -669,16 +749,17 @@ __device__ __forceinline__ float2 unpack_h2(uint32_t u) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kRThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRThreads, 1)
 kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, float* __restrict__ s_out,
                  T* __restrict__ o, int B, int Tlen, int H, unsigned* __restrict__ err) {
-  using Cf = RecurCfg<T>;
-  constexpr int NST = Cf::kStages;
   extern __shared__ __align__(128) uint8_t smb[];
-  T* sO = reinterpret_cast<T*>(smb + NST * kRStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smb + NST * kRStageBytes + Cf::kStaging);
+  uint64_t* full0 = reinterpret_cast<uint64_t*>(smb + kRBar);
+  uint64_t* dempty = full0 + kNS0;   // [2][RW]
+  uint64_t* full1 = dempty + 2 * RW;
+  uint64_t* dfull = full1 + kNS1;    // [2][RW]
   const int nc = Tlen / C;
-  const int v0 = blockIdx.x * RV, h = blockIdx.y, b = blockIdx.z;
+  const uint32_t rank = cluster_rank();
+  const int utile = blockIdx.x >> 1, v0 = utile * RV, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tq = lane & 3, mat = lane >> 3, r8 = lane & 7;
   const int dv0 = v0 + 16 * warp;
@@ -686,152 +767,270 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
   const size_t sbase = ((size_t)b * H + h) * DK * DV;
 
   if (tid == 0) {
-    for (int i = 0; i < NST; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < kNS0; ++i) mbar_init(&full0[i], 1);
+    for (int i = 0; i < kNS1; ++i) mbar_init(&full1[i], 1);
+    for (int i = 0; i < 2 * RW; ++i) {
+      mbar_init(&dempty[i], 1);  // lane 0 of the output warp, after its warp read the slot
+      mbar_init(&dfull[i], 1);   // the output warp's own expect_tx arrive + 6 KB of remote stores
+    }
     fence_mbar_init();
   }
-  __syncthreads();
-  if (tid == 0)
-    for (int i = 0; i < NST && i < nc; ++i)
-      r_load_stage(smb + i * kRStageBytes, head + (size_t)i * kWsBlockBytes, blockIdx.x, &full[i]);
-
-  // S^T fragments: n-tile nt covers dk 8 nt .. 8 nt + 7; e: (dv g | g + 8) x (dk 2 tq | 2 tq + 1)
-  float S[16][4];
-#pragma unroll
-  for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int dk = 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
-      S[nt][e] = s0 ? s0[sbase + (size_t)dk * DV + dv] : 0.f;
-    }
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive
 
   bool alive = true;
-  for (int c = 0; c < nc && alive; ++c) {
-    const int sl = c % NST;
-    const uint8_t* st = smb + sl * kRStageBytes;
-    // CTA-uniform verdict, so that no thread leaves the loop while others wait at a barrier
-    alive = __syncthreads_and(mbar_wait(&full[sl], (uint32_t)(c / NST) & 1u, err, 0xB2300003u));
-    if (!alive) break;
-    const __half* sW = reinterpret_cast<const __half*>(st + kBW);
-    const __half* sKr = reinterpret_cast<const __half*>(st + kBKr);
-    const __half* sQg = reinterpret_cast<const __half*>(st + kBQg);
-    const __half* sAq = reinterpret_cast<const __half*>(st + kBAq);
-    const float* sGl = reinterpret_cast<const float*>(st + kBGl);
-    const __half* sU = reinterpret_cast<const __half*>(st + kBShared);
-    // S^T as fp16 A fragments, one per 16-wide dk step
-    uint32_t sa[8][4];
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      sa[kk][0] = pack_h2(S[2 * kk][0], S[2 * kk][1]);
-      sa[kk][1] = pack_h2(S[2 * kk][2], S[2 * kk][3]);
-      sa[kk][2] = pack_h2(S[2 * kk + 1][0], S[2 * kk + 1][1]);
-      sa[kk][3] = pack_h2(S[2 * kk + 1][2], S[2 * kk + 1][3]);
-    }
-    // acc = S^T W^T - U^T (= -V'^T), starting from -U^T read as C fragments
-    float vp[8][4], oa[8][4];
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      uint32_t u[4];
-      ldsm_x4_trans(smem_u32(sU + (8 * (2 * p + (mat >> 1)) + r8) * LUS + 16 * warp + ((mat & 1) << 3)), u);
-      const float2 a0 = unpack_h2(u[0]), a1 = unpack_h2(u[1]), a2 = unpack_h2(u[2]), a3 = unpack_h2(u[3]);
-      vp[2 * p][0] = -a0.x;
-      vp[2 * p][1] = -a0.y;
-      vp[2 * p][2] = -a1.x;
-      vp[2 * p][3] = -a1.y;
-      vp[2 * p + 1][0] = -a2.x;
-      vp[2 * p + 1][1] = -a2.y;
-      vp[2 * p + 1][2] = -a3.x;
-      vp[2 * p + 1][3] = -a3.y;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) oa[2 * p][e] = oa[2 * p + 1][e] = 0.f;
-    }
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
-        uint32_t bw[4], bq[4];
-        ldsm_x4(smem_u32(sW + row * LR + col), bw);
-        const uint32_t w0[2] = {bw[0], bw[1]}, w1[2] = {bw[2], bw[3]};
-        mma_16816<B2_F16>(vp[2 * np], sa[kk], w0);
-        mma_16816<B2_F16>(vp[2 * np + 1], sa[kk], w1);
-        ldsm_x4(smem_u32(sQg + row * LR + col), bq);
-        const uint32_t q0[2] = {bq[0], bq[1]}, q1[2] = {bq[2], bq[3]};
-        mma_16816<B2_F16>(oa[2 * np], sa[kk], q0);
-        mma_16816<B2_F16>(oa[2 * np + 1], sa[kk], q1);
-      }
-    }
-    // V'^T = -acc as fp16 A fragments over the chunk's 4 16-step blocks
-    uint32_t va[4][4];
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      va[kk][0] = pack_h2(-vp[2 * kk][0], -vp[2 * kk][1]);
-      va[kk][1] = pack_h2(-vp[2 * kk][2], -vp[2 * kk][3]);
-      va[kk][2] = pack_h2(-vp[2 * kk + 1][0], -vp[2 * kk + 1][1]);
-      va[kk][3] = pack_h2(-vp[2 * kk + 1][2], -vp[2 * kk + 1][3]);
-    }
-    // O^T += V'^T A_qk^T: A_qk[i][j] = 0 for j > i, so key block kk only
-    // reaches query blocks np >= kk
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        if (np < kk) continue;
-        const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
-        uint32_t ba[4];
-        ldsm_x4(smem_u32(sAq + row * LA + col), ba);
-        const uint32_t a0[2] = {ba[0], ba[1]}, a1[2] = {ba[2], ba[3]};
-        mma_16816<B2_F16>(oa[2 * np], va[kk], a0);
-        mma_16816<B2_F16>(oa[2 * np + 1], va[kk], a1);
-      }
-    }
-    // S^T = S^T o e^{G_last} (per dk column) + V'^T Kr
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      const float2 gl = *reinterpret_cast<const float2*>(sGl + 8 * nt + 2 * tq);
-      S[nt][0] *= gl.x;
-      S[nt][1] *= gl.y;
-      S[nt][2] *= gl.x;
-      S[nt][3] *= gl.y;
-    }
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        uint32_t bk[4];
-        ldsm_x4_trans(smem_u32(sKr + (16 * kk + r8 + ((mat & 1) << 3)) * LR + 16 * np + ((mat >> 1) << 3)), bk);
-        const uint32_t k0[2] = {bk[0], bk[1]}, k1[2] = {bk[2], bk[3]};
-        mma_16816<B2_F16>(S[2 * np], va[kk], k0);
-        mma_16816<B2_F16>(S[2 * np + 1], va[kk], k1);
-      }
-    }
-    // O^T -> staging tile [t][dv], then coalesced rows of o
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = 8 * nt + 2 * tq + (e & 1), dvl = 16 * warp + g + 8 * (e >> 1);
-        sO[t * LO + dvl] = from_f32<T>(oa[nt][e]);
-      }
-    __syncthreads();  // staging complete; every warp is done with stage sl
-    if (tid == 0 && c + NST < nc)
-      r_load_stage(smb + sl * kRStageBytes, head + (size_t)(c + NST) * kWsBlockBytes, blockIdx.x, &full[sl]);
-    constexpr int PER = 16 / sizeof(T);  // elements per 16-byte store
-    for (int e = tid; e < C * RV / PER; e += kRThreads) {
-      const int t = e / (RV / PER), cc = e % (RV / PER);
-      *reinterpret_cast<uint4*>(o + (((int64_t)b * Tlen + (int64_t)c * C + t) * H + h) * DV + v0 + PER * cc) =
-          *reinterpret_cast<const uint4*>(sO + t * LO + PER * cc);
-    }
-    __syncthreads();  // staging tile read before the next chunk writes it
-  }
-  if (s_out) {
+  int c = 0;       // chunk the loop stopped at
+  int issued = 0;  // chunks whose stage load thread 0 has issued
+  if (rank == 0) {
+    // ================================ state CTA ================================
+    if (tid == 0)
+      for (; issued < kNS0 && issued < nc; ++issued)
+        r_load_stage0(smb + issued * kStage0, head + (size_t)issued * kWsBlockBytes, utile, &full0[issued]);
+    // this lane's fragment slot in the output CTA: 12 16-byte groups, lane-interleaved
+    const uint32_t slot_remote = map_rank(smb + kSlots1 + warp * kSlotWarp, 1);
+    uint4* slot_stage = reinterpret_cast<uint4*>(smb + kSlots0 + warp * kSlotWarp) + lane;
+    const uint32_t dfull_remote = map_rank(&dfull[warp], 1);
+    // S^T fragments: n-tile nt covers dk 8 nt .. 8 nt + 7; e: (dv g | g + 8) x (dk 2 tq | 2 tq + 1)
+    float S[16][4];
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int dk = 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
-        s_out[sbase + (size_t)dk * DV + dv] = S[nt][e];
+        S[nt][e] = s0 ? s0[sbase + (size_t)dk * DV + dv] : 0.f;
       }
+    for (; c < nc && alive; ++c) {
+      const int sl = c % kNS0, ds = c & 1;
+      const uint8_t* st = smb + sl * kStage0;
+      // CTA-uniform verdict, so that no thread leaves the loop while others wait at a barrier
+      B2_RPROF(0, c);
+      alive = __syncthreads_and(mbar_wait(&full0[sl], (uint32_t)(c / kNS0) & 1u, err, 0xB2300003u));
+      if (!alive) break;
+      B2_RPROF(1, c);
+      const __half* sW = reinterpret_cast<const __half*>(st + kBW);
+      const __half* sKr = reinterpret_cast<const __half*>(st + kBKr);
+      const float* sGl = reinterpret_cast<const float*>(st + kBGl);
+      const __half* sU = reinterpret_cast<const __half*>(st + kBStatePart);
+      // S^T as fp16 A fragments, one per 16-wide dk step
+      uint32_t sa[8][4];
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        sa[kk][0] = pack_h2(S[2 * kk][0], S[2 * kk][1]);
+        sa[kk][1] = pack_h2(S[2 * kk][2], S[2 * kk][3]);
+        sa[kk][2] = pack_h2(S[2 * kk + 1][0], S[2 * kk + 1][1]);
+        sa[kk][3] = pack_h2(S[2 * kk + 1][2], S[2 * kk + 1][3]);
+      }
+      // acc = S^T W^T - U^T (= -V'^T), starting from -U^T read as C fragments
+      float vp[8][4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        uint32_t u[4];
+        ldsm_x4_trans(smem_u32(sU + (8 * (2 * p + (mat >> 1)) + r8) * LUS + 16 * warp + ((mat & 1) << 3)), u);
+        const float2 a0 = unpack_h2(u[0]), a1 = unpack_h2(u[1]), a2 = unpack_h2(u[2]), a3 = unpack_h2(u[3]);
+        vp[2 * p][0] = -a0.x;
+        vp[2 * p][1] = -a0.y;
+        vp[2 * p][2] = -a1.x;
+        vp[2 * p][3] = -a1.y;
+        vp[2 * p + 1][0] = -a2.x;
+        vp[2 * p + 1][1] = -a2.y;
+        vp[2 * p + 1][2] = -a3.x;
+        vp[2 * p + 1][3] = -a3.y;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
+          uint32_t bw[4];
+          ldsm_x4(smem_u32(sW + row * LR + col), bw);
+          const uint32_t w0[2] = {bw[0], bw[1]}, w1[2] = {bw[2], bw[3]};
+          mma_16816<B2_F16>(vp[2 * np], sa[kk], w0);
+          mma_16816<B2_F16>(vp[2 * np + 1], sa[kk], w1);
+        }
+      }
+      // V'^T = -acc as fp16 A fragments over the chunk's 4 16-step blocks
+      uint32_t va[4][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        va[kk][0] = pack_h2(-vp[2 * kk][0], -vp[2 * kk][1]);
+        va[kk][1] = pack_h2(-vp[2 * kk][2], -vp[2 * kk][3]);
+        va[kk][2] = pack_h2(-vp[2 * kk + 1][0], -vp[2 * kk + 1][1]);
+        va[kk][3] = pack_h2(-vp[2 * kk + 1][2], -vp[2 * kk + 1][3]);
+      }
+      B2_RPROF(2, c);
+      // hand S^T and V'^T to the output warp of the same columns: asynchronous
+      // remote stores that complete the slot's mbarrier transaction there
+      bool sent = mbar_wait_cluster(&dempty[ds * RW + warp], ((uint32_t)(c >> 1) & 1u) ^ 1u, err, 0xB230000Bu);
+      B2_RPROF(3, c);
+      if (sent) {
+        // local staging slot (free: the output warp consumed its previous copy),
+        // then one bulk copy of the warp's 6 KB into the output CTA
+        uint4* stg = slot_stage + ds * (kSlotBytes / 16);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) stg[kk * 32] = make_uint4(sa[kk][0], sa[kk][1], sa[kk][2], sa[kk][3]);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) stg[(8 + kk) * 32] = make_uint4(va[kk][0], va[kk][1], va[kk][2], va[kk][3]);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0)
+          bulk_s2cluster(slot_remote + ds * kSlotBytes, smb + kSlots0 + ds * kSlotBytes + warp * kSlotWarp, kSlotWarp,
+                         dfull_remote + ds * RW * 8);
+      }
+      B2_RPROF(4, c);
+      // S^T = S^T o e^{G_last} (per dk column) + V'^T Kr
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+        const float2 gl = *reinterpret_cast<const float2*>(sGl + 8 * nt + 2 * tq);
+        S[nt][0] *= gl.x;
+        S[nt][1] *= gl.y;
+        S[nt][2] *= gl.x;
+        S[nt][3] *= gl.y;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          uint32_t bk[4];
+          ldsm_x4_trans(smem_u32(sKr + (16 * kk + r8 + ((mat & 1) << 3)) * LR + 16 * np + ((mat >> 1) << 3)), bk);
+          const uint32_t k0[2] = {bk[0], bk[1]}, k1[2] = {bk[2], bk[3]};
+          mma_16816<B2_F16>(S[2 * np], va[kk], k0);
+          mma_16816<B2_F16>(S[2 * np + 1], va[kk], k1);
+        }
+      }
+      B2_RPROF(5, c);
+      // every warp is done with stage sl (and agrees on the hand-over)
+      alive = __syncthreads_and(sent);
+      B2_RPROF(6, c);
+      if (alive && tid == 0 && c + kNS0 < nc) {
+        r_load_stage0(smb + sl * kStage0, head + (size_t)(c + kNS0) * kWsBlockBytes, utile, &full0[sl]);
+        issued = c + kNS0 + 1;
+      }
+    }
+    // the output warp has read the last two hand-overs, so no bulk copy out of
+    // this CTA's staging slots is still in flight when the cluster exits
+    for (int cc = c > 2 ? c - 2 : 0; cc < c && cc < nc; ++cc)
+      mbar_wait_cluster(&dempty[(cc & 1) * RW + warp], (uint32_t)(cc >> 1) & 1u, err, 0xB230000Fu);
+    if (s_out && alive) {
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int dk = 8 * nt + 2 * tq + (e & 1), dv = dv0 + g + 8 * (e >> 1);
+          s_out[sbase + (size_t)dk * DV + dv] = S[nt][e];
+        }
+    }
+  } else {
+    // =============================== output CTA ================================
+    T* sO = reinterpret_cast<T*>(smb + kStaging1);
+    const uint32_t dempty_remote = map_rank(&dempty[warp], 0);
+    const uint4* slot_local = reinterpret_cast<const uint4*>(smb + kSlots1 + warp * kSlotWarp) + lane;
+    // arm both fragment slots for their first hand-over
+    if (lane == 0)
+      for (int i = 0; i < 2 && i < nc; ++i) mbar_arrive_expect_tx(&dfull[i * RW + warp], kSlotWarp);
+    if (tid == 0)
+      for (; issued < kNS1 && issued < nc; ++issued)
+        r_load_stage1(smb + issued * kStage1, head + (size_t)issued * kWsBlockBytes, &full1[issued]);
+    for (; c < nc && alive; ++c) {
+      const int sl = c % kNS1, ds = c & 1;
+      const uint8_t* st = smb + sl * kStage1;
+      B2_RPROF(0, c);
+      const bool got1 = mbar_wait(&full1[sl], (uint32_t)(c / kNS1) & 1u, err, 0xB230000Cu);
+      B2_RPROF(1, c);
+      const bool got = got1 && mbar_wait_cluster(&dfull[ds * RW + warp], (uint32_t)(c >> 1) & 1u, err, 0xB230000Du);
+      B2_RPROF(2, c);
+      alive = __syncthreads_and(got);
+      B2_RPROF(3, c);
+      if (!alive) break;
+      const __half* sQg = reinterpret_cast<const __half*>(st + (kBQg - kBQg));
+      const __half* sAq = reinterpret_cast<const __half*>(st + (kBAq - kBQg));
+      uint32_t sa[8][4], va[4][4];
+      const uint4* slot = slot_local + ds * (kSlotBytes / 16);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint4 x = slot[kk * 32];
+        sa[kk][0] = x.x;
+        sa[kk][1] = x.y;
+        sa[kk][2] = x.z;
+        sa[kk][3] = x.w;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint4 x = slot[(8 + kk) * 32];
+        va[kk][0] = x.x;
+        va[kk][1] = x.y;
+        va[kk][2] = x.z;
+        va[kk][3] = x.w;
+      }
+      // the slot is free again: re-arm it for chunk c + 2, then tell the state warp
+      __syncwarp();
+      if (lane == 0) {
+        if (c + 2 < nc) mbar_arrive_expect_tx(&dfull[ds * RW + warp], kSlotWarp);
+        mbar_arrive_remote(dempty_remote + ds * RW * 8);
+      }
+      float oa[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) oa[n][e] = 0.f;
+      // O^T = S^T Qg^T
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
+          uint32_t bq[4];
+          ldsm_x4(smem_u32(sQg + row * LR + col), bq);
+          const uint32_t q0[2] = {bq[0], bq[1]}, q1[2] = {bq[2], bq[3]};
+          mma_16816<B2_F16>(oa[2 * np], sa[kk], q0);
+          mma_16816<B2_F16>(oa[2 * np + 1], sa[kk], q1);
+        }
+      }
+      // O^T += V'^T A_qk^T: A_qk[i][j] = 0 for j > i, so key block kk only
+      // reaches query blocks np >= kk
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          if (np < kk) continue;
+          const int row = 16 * np + r8 + ((mat >> 1) << 3), col = 16 * kk + ((mat & 1) << 3);
+          uint32_t ba[4];
+          ldsm_x4(smem_u32(sAq + row * LA + col), ba);
+          const uint32_t a0[2] = {ba[0], ba[1]}, a1[2] = {ba[2], ba[3]};
+          mma_16816<B2_F16>(oa[2 * np], va[kk], a0);
+          mma_16816<B2_F16>(oa[2 * np + 1], va[kk], a1);
+        }
+      }
+      // O^T -> staging tile [t][dv], then coalesced rows of o
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = 8 * nt + 2 * tq + (e & 1), dvl = 16 * warp + g + 8 * (e >> 1);
+          sO[t * LO + dvl] = from_f32<T>(oa[nt][e]);
+        }
+      __syncthreads();  // staging complete; every warp is done with stage sl
+      if (tid == 0 && c + kNS1 < nc) {
+        r_load_stage1(smb + sl * kStage1, head + (size_t)(c + kNS1) * kWsBlockBytes, &full1[sl]);
+        issued = c + kNS1 + 1;
+      }
+      constexpr int PER = 16 / sizeof(T);  // elements per 16-byte store
+      for (int e = tid; e < C * RV / PER; e += kRThreads) {
+        const int t = e / (RV / PER), cc = e % (RV / PER);
+        *reinterpret_cast<uint4*>(o + (((int64_t)b * Tlen + (int64_t)c * C + t) * H + h) * DV + v0 + PER * cc) =
+            *reinterpret_cast<const uint4*>(sO + t * LO + PER * cc);
+      }
+      __syncthreads();  // staging tile read before the next chunk writes it
+    }
   }
+  // A CTA that gave up may leave bulk copies in flight into its own ring (the
+  // stages of the chunks from c up to the last one issued): wait for them (bounded) before the
+  // cluster exits.
+  if (!alive && tid == 0) {
+    const int ns = rank == 0 ? kNS0 : kNS1;
+    uint64_t* fb = rank == 0 ? full0 : full1;
+    for (int cc = c > 0 ? c - 1 : 0; cc < issued; ++cc)
+      mbar_wait(&fb[cc % ns], (uint32_t)(cc / ns) & 1u, err, 0xB230000Eu);
+  }
+  cluster_sync();  // neither CTA leaves while the other may still address its shared memory
 }
 }  // namespace kda
 }  // namespace b2
@@ -839,6 +1038,9 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
 using namespace b2;
 
 #ifdef B2_KDA_PROFILE
+extern "C" __attribute__((visibility("default"))) int b2_kda_rprof_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, kda::g_kda_rprof, sizeof(kda::g_kda_rprof));
+}
 extern "C" __attribute__((visibility("default"))) int b2_kda_prof_read(unsigned long long* host) {
   return (int)cudaMemcpyFromSymbol(host, kda::g_kda_prof, sizeof(kda::g_kda_prof));
 }
@@ -876,14 +1078,14 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
   unsigned* err = device_error_word();
   B2_CHECK_ARG(err, B2_ERR_LAUNCH, "kda_fwd: no device error word");
   const dim3 ga((unsigned)(T / chunk), (unsigned)H, (unsigned)B);
-  const dim3 gb(kda::DV / kda::RV, (unsigned)H, (unsigned)B);
+  const dim3 gb(2 * (kda::DV / kda::RV), (unsigned)H, (unsigned)B);  // clusters of 2 along x
 #define B2_KDA_LAUNCH(TY)                                                                                         \
   do {                                                                                                            \
     set_max_smem((const void*)kda::kda_prep_kernel<TY>, (int)kda::prep::kSmem);                                  \
-    set_max_smem((const void*)kda::kda_recur_kernel<TY>, (int)kda::RecurCfg<TY>::kSmem);                         \
+    set_max_smem((const void*)kda::kda_recur_kernel<TY>, (int)kda::kRSmem);                                      \
     kda::kda_prep_kernel<TY><<<ga, kda::prep::kThreads, kda::prep::kSmem, st>>>(                                  \
         (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale, err);   \
-    kda::kda_recur_kernel<TY><<<gb, kda::kRThreads, kda::RecurCfg<TY>::kSmem, st>>>(                             \
+    kda::kda_recur_kernel<TY><<<gb, kda::kRThreads, kda::kRSmem, st>>>(                                         \
         ws, initial_state, final_state, (TY*)o, (int)B, (int)T, (int)H, err);                                    \
   } while (0)
   if (dtype == B2_BF16) B2_KDA_LAUNCH(__nv_bfloat16);
