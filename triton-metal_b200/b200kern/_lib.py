@@ -79,6 +79,20 @@ def call(name, *args):
     return status
 
 
+def fn(name):
+    """The bound ctypes function of an entry point (for hot paths that check
+    the status themselves with ``check``)."""
+    f = _fns.get(name)
+    if f is None:
+        f = _fns[name] = getattr(load(), name)
+    return f
+
+
+def check(status, name):
+    if status != 0:
+        raise_for_status(status, name, load().b2_last_error().decode())
+
+
 def strides_arg(t):
     return (ctypes.c_int64 * 3)(*t)
 

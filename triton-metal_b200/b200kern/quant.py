@@ -81,25 +81,32 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
     dequant (q - z) * s and fp32 products (no 16-bit rounding anywhere) and
     returns fp32.
     """
-    if (layout == LAYOUT_GPTQ and zeros is None and input.dtype in _DT and scales.dtype == input.dtype
-            and weight.dtype == torch.int32 and input.dim() == 2 and weight.dim() == 2 and scales.dim() == 2
-            and input.is_cuda and weight.is_cuda and scales.is_cuda and input.is_contiguous()
-            and weight.is_contiguous() and scales.is_contiguous()):
-        # common decode / prefill case: no conversion or copy, straight to the kernel
-        M, K = input.shape
-        N = weight.shape[1]
-        if weight.shape[0] * 8 == K and K % group_size == 0 and scales.shape == (K // group_size, N):
-            if out is not None and out.dtype == input.dtype and out.is_contiguous() and out.shape == (M, N):
-                res = out
-            else:
-                res = torch.empty(M, N, dtype=input.dtype, device=input.device)
-            if M:
-                _lib.call("b2_int4_matmul", input.data_ptr(), weight.data_ptr(), res.data_ptr(), scales.data_ptr(),
-                          None, M, N, K, group_size, _DT[input.dtype], _stream())
-            if out is not None and res is not out:
-                out.copy_(res)
-                return out
-            return res
+    # Common decode / prefill case, straight to the kernel with no conversion
+    # or copy.  A decode step issues one of these per layer and the kernel
+    # takes a few microseconds, so this path reads each tensor attribute once.
+    dti = input.dtype
+    dt = _DT.get(dti)
+    if (dt is not None and zeros is None and layout == LAYOUT_GPTQ and weight.dtype == torch.int32
+            and scales.dtype == dti and input.is_cuda and weight.is_cuda and scales.is_cuda):
+        ish, wsh = input.shape, weight.shape
+        if (len(ish) == 2 and len(wsh) == 2 and input.is_contiguous() and weight.is_contiguous()
+                and scales.is_contiguous()):
+            M, K = ish
+            N = wsh[1]
+            if wsh[0] * 8 == K and K % group_size == 0 and scales.shape == (K // group_size, N):
+                if (out is not None and out.dtype == dti and out.is_cuda and out.is_contiguous()
+                        and out.shape == (M, N)):
+                    res = out
+                else:
+                    res = torch.empty(M, N, dtype=dti, device=input.device)
+                if M:
+                    _lib.check(_lib.fn("b2_int4_matmul")(input.data_ptr(), weight.data_ptr(), res.data_ptr(),
+                                                         scales.data_ptr(), None, M, N, K, group_size, dt,
+                                                         _lib.current_stream()), "b2_int4_matmul")
+                if out is not None and res is not out:
+                    out.copy_(res)
+                    return out
+                return res
     _check_cuda(input, weight, scales, zeros)
     if input.dim() != 2:
         raise B2ShapeError(f"input must be [M, K], got {tuple(input.shape)}")
