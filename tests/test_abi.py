@@ -56,3 +56,15 @@ def test_host_validation_without_gpu():
     assert st == errors.ERR_DTYPE
     st = lib.b2_int8_matmul(None, 1, 1, 1, None, 1, 32, 128, 0, None)
     assert st == errors.ERR_INVALID
+
+
+def test_caller_output_must_be_a_device_tensor_of_the_right_shape():
+    """A caller-supplied ``out`` is written through its raw pointer, so a host
+    tensor, a wrong dtype or a wrong shape is refused before any launch."""
+    import pytest
+    import torch
+    from b200kern import _lib, errors
+    with pytest.raises(errors.B2ShapeError):
+        _lib.check_out(torch.empty(2, 3), (2, 3), torch.float32, "op")  # host memory
+    with pytest.raises(errors.B2ShapeError):
+        _lib.check_out(torch.empty(2, 3, device="meta"), (2, 4), torch.float32, "op")

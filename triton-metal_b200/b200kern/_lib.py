@@ -93,6 +93,18 @@ def check(status, name):
         raise_for_status(status, name, load().b2_last_error().decode())
 
 
+def check_out(out, shape, dtype, name, contiguous=True):
+    """A caller-supplied output must be a CUDA tensor of the op's shape and
+    dtype (and, where the kernel writes it densely, contiguous): the kernel
+    writes through its raw pointer."""
+    from .errors import B2ShapeError
+    if not out.is_cuda or out.dtype != dtype or tuple(out.shape) != tuple(shape) or \
+            (contiguous and not out.is_contiguous()):
+        raise B2ShapeError(f"{name}: out must be a {'contiguous ' if contiguous else ''}CUDA {dtype} tensor of "
+                           f"shape {tuple(shape)}, got {out.dtype} {tuple(out.shape)} on {out.device}")
+    return out
+
+
 def strides_arg(t):
     return (ctypes.c_int64 * 3)(*t)
 

@@ -54,7 +54,8 @@ def flash_attention(q, k, v, causal=False, scale=None, out=None, window=0):
         raise B2ShapeError(f"Hq={Hq} must be a multiple of Hkv={Hkv}")
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    o = out if out is not None else torch.empty(B, Hq, Sq, D, dtype=q.dtype, device=q.device)
+    o = (_lib.check_out(out, (B, Hq, Sq, D), q.dtype, "flash_attention", contiguous=False) if out is not None
+         else torch.empty(B, Hq, Sq, D, dtype=q.dtype, device=q.device))
     q, qs = _strides(q)
     k, ks = _strides(k)
     v, vs = _strides(v)
@@ -141,7 +142,8 @@ def decode_attention(q, k_cache, v_cache, seq_lens, scale=None, page_table=None,
     lens = _seq_lens(seq_lens, B, q.device)
     scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
     q = q.contiguous()
-    o = out if out is not None else torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
+    o = (_lib.check_out(out, (B, Hq, D), q.dtype, "decode_attention") if out is not None
+         else torch.empty(B, Hq, D, dtype=q.dtype, device=q.device))
     lib = _lib.load()
     need = int(lib.b2_decode_attn_workspace_size(B, Hq, Hkv, D, S))
     ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
@@ -196,7 +198,8 @@ def repeat_kv(x, n_rep, out=None):
     nb = 1
     for d in lead:
         nb *= d
-    res = out if out is not None else torch.empty(*lead, Hkv * n_rep, S, D, dtype=x.dtype, device=x.device)
+    res = (_lib.check_out(out, (*lead, Hkv * n_rep, S, D), x.dtype, "repeat_kv") if out is not None
+           else torch.empty(*lead, Hkv * n_rep, S, D, dtype=x.dtype, device=x.device))
     _lib.call("b2_repeat_kv", x.data_ptr(), res.data_ptr(), nb * Hkv, S, D, int(n_rep), x.element_size(), _stream())
     return res
 

@@ -44,13 +44,15 @@ def kda_chunk_fwd(q, k, v, g, beta, scale=None, initial_state=None, output_final
         raise B2ShapeError("shapes must be q,k,g [B,T,H,Dk], v [B,T,H,Dv], beta [B,T,H]")
     scale = Dk ** -0.5 if scale is None else float(scale)
     q, k, v, g, beta = (t.contiguous() for t in (q, k, v, g, beta))
-    o = out if out is not None else torch.empty(B, T, H, Dv, dtype=q.dtype, device=q.device)
+    o = (_lib.check_out(out, (B, T, H, Dv), q.dtype, "kda_chunk_fwd") if out is not None
+         else torch.empty(B, T, H, Dv, dtype=q.dtype, device=q.device))
     s_out = None
     if output_final_state:
         s_out = final_state_out
         if s_out is None:
             s_out = torch.empty(B, H, Dk, Dv, dtype=torch.float32, device=q.device)
-        elif s_out.dtype != torch.float32 or tuple(s_out.shape) != (B, H, Dk, Dv) or not s_out.is_contiguous():
+        elif (not s_out.is_cuda or s_out.dtype != torch.float32 or tuple(s_out.shape) != (B, H, Dk, Dv)
+              or not s_out.is_contiguous()):
             raise B2ShapeError("final_state_out must be a contiguous fp32 [B, H, Dk, Dv] tensor")
     s0 = None
     if initial_state is not None:

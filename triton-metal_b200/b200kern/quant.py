@@ -154,7 +154,7 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
     s = scales.to(cdt).contiguous()
     z = None if zeros is None else zeros.to(cdt).contiguous()
     w = weight.contiguous()
-    if out is not None and (out.dtype == cdt and out.is_contiguous() and tuple(out.shape) == (M, N)):
+    if out is not None and (out.is_cuda and out.dtype == cdt and out.is_contiguous() and tuple(out.shape) == (M, N)):
         res = out
     else:
         res = torch.empty(M, N, dtype=cdt, device=input.device)
@@ -230,6 +230,7 @@ def gemm_bf16(x, w, out=None):
     N = w.shape[0]
     if w.shape[1] != K:
         raise B2ShapeError("K mismatch")
-    res = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    res = (_lib.check_out(out, (M, N), torch.bfloat16, "gemm_bf16") if out is not None
+           else torch.empty(M, N, dtype=torch.bfloat16, device=x.device))
     _lib.call("b2_gemm_bf16", _ptr(x.contiguous()), _ptr(w.contiguous()), _ptr(res), M, N, K, _stream())
     return res
