@@ -304,9 +304,27 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   __half* wsQg = ws_h(blk, kBQg);
   __half* wsKr = ws_h(blk, kBKr);
   float2 wk[16];  // beta K e^G (W operand); then beta V (U operand)
+  // Swizzled operand addresses, hoisted: row t = r0 + r of a K-major tile
+  // with `rows` rows sits at (d0 / 64) rows 128 + t 128, and this thread's
+  // 16-byte chunk moves with t % 8 = r % 8 (r0 is a multiple of 16).
+  uint32_t swz[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) swz[j] = ((((uint32_t)(d0 & 63) >> 3) ^ (uint32_t)j) << 4) + (uint32_t)(d0 & 7) * 2;
+  // j-side rows of block row J: [A_kk operand region, first row]
+  auto jrow = [&](int J) -> uint8_t* {
+    const uint32_t region = J >= 2 ? kAA + (uint32_t)(d0 >> 6) * kRowsAA * 128 : kAB + (uint32_t)(d0 >> 6) * kRowsAB * 128;
+    const int row0 = J == 3 ? 0 : J == 2 ? 64 : J == 1 ? 0 : 32;
+    return sm + region + (row0 + r0) * 128;
+  };
+  uint8_t* const pL = sm + kBL + (uint32_t)(d0 >> 6) * 128 * 128 + r0 * 128;  // rows t (L); + 64 rows: Lq
+  uint8_t* const pD = jrow(I);
+  uint8_t* pO[3];
+#pragma unroll
+  for (int u = 0; u < 3; ++u) pO[u] = jrow(I + 1 + u < 4 ? I + 1 + u : 0);
 #pragma unroll
   for (int r = 0; r < 16; ++r) {
     const int t = r0 + r;
+    const uint32_t rs = (uint32_t)r * 128 + swz[r & 7];
     const float2 kk = P2::f2(kraw[r]);
     const float2 q2 = P2::f2(qraw[r]);
     const float2 sq = make_float2(q2.x * scale, q2.y * scale);
@@ -314,23 +332,16 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     const float2 ej = exp2f2(Gnx, G[r]);  // <= 1
     const float2 lo = mul2(kk, e0), lq = mul2(sq, e0), kj = mul2(kk, ej);
     // i side: rows t (L) and 64 + t (Lq)
-    st_u32(sm + kBL, sw_off(t, d0, 128), bf2(lo.x, lo.y));
-    st_u32(sm + kBL, sw_off(64 + t, d0, 128), bf2(lq.x, lq.y));
+    st_u32(pL, rs, bf2(lo.x, lo.y));
+    st_u32(pL + 64 * 128, rs, bf2(lq.x, lq.y));
     // j side: block row I (diagonal) and every later block row
     const float2 kd = mul2(kj, cD);
-    if (I == 3) st_u32(sm + kAA, sw_off(t, d0, kRowsAA), bf2(kd.x, kd.y));
-    else if (I == 2) st_u32(sm + kAA, sw_off(64 + t, d0, kRowsAA), bf2(kd.x, kd.y));
-    else if (I == 1) st_u32(sm + kAB, sw_off(t, d0, kRowsAB), bf2(kd.x, kd.y));
-    else st_u32(sm + kAB, sw_off(32 + t, d0, kRowsAB), bf2(kd.x, kd.y));
+    st_u32(pD, rs, bf2(kd.x, kd.y));
 #pragma unroll
     for (int u = 0; u < 3; ++u) {
-      const int Ip = I + 1 + u;
-      if (Ip >= 4) break;
+      if (I + 1 + u >= 4) break;
       const float2 ko = mul2(kj, cOff[u]);
-      const uint32_t v2 = bf2(ko.x, ko.y);
-      if (Ip == 3) st_u32(sm + kAA, sw_off(t, d0, kRowsAA), v2);
-      else if (Ip == 2) st_u32(sm + kAA, sw_off(64 + t, d0, kRowsAA), v2);
-      else st_u32(sm + kAB, sw_off(t, d0, kRowsAB), v2);
+      st_u32(pO[u], rs, bf2(ko.x, ko.y));
     }
     *reinterpret_cast<__half2*>(wsQg + t * LR + d0) = __floats2half2_rn(lq.x * eG0.x, lq.y * eG0.y);
     *reinterpret_cast<__half2*>(wsKr + t * LR + d0) = __floats2half2_rn(kj.x * cKr.x, kj.y * cKr.y);
