@@ -114,6 +114,9 @@ constexpr uint32_t kSAq = kSA + C * LT * 4;
 constexpr uint32_t kST = kSAq + C * LT * 4;
 constexpr uint32_t kSGb = kST + C * LT * 4;              // exact fallback: G of one block [16][128]
 constexpr uint32_t kBT = 61440;                          // T bf16: 64 rows (t) x K = 64 (j)
+// after the W / U MMAs: staging of W and U in the workspace layout (region R)
+constexpr uint32_t kStgW = 0;
+constexpr uint32_t kStgU = kStgW + C * LR * 2;
 // region W: W / U MMA A operands, 128 rows (dk / dv) x K = 64 (t)
 constexpr uint32_t kAW = kRegionR;
 constexpr uint32_t kAU = kAW + 128 * 64 * 2;
@@ -128,8 +131,15 @@ constexpr size_t kSmem = kBytes + 1024;                  // + alignment of the s
 constexpr uint32_t kTmemCols = 256;
 constexpr float kGapMax = 80.f;
 static_assert(kSGb + 16 * DK * 4 <= kBT && kBT + 64 * 128 <= kRegionR, "scratch must fit in region R");
+static_assert(kStgU + 2 * kBUTile <= kRegionR && kStgW % 16 == 0 && kStgU % 16 == 0, "W / U staging");
 static_assert(kSmem <= 113 * 1024, "two CTAs per SM");
 
+// bulk copy shared -> global (bulk-group completion)
+__device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ uint32_t sw_off(int row, int k, int rows) {
   return (uint32_t)((k >> 6) * rows * 128 + row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
 }
@@ -602,13 +612,16 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   if (alive) alive = mbar_wait(&bar[1], 0, err, 0xB2300002u);
   tc::fence_after_sync();
   B2_PROF(8);
-  // ---- 9. W^T, U^T (TMEM lane = dk / dv, column = t) -> W, U [t][d] fp16 ----
+  // ---- 9. W^T, U^T (TMEM lane = dk / dv, column = t) -> W, U [t][d] fp16,
+  // staged in shared memory in the workspace layout (region R is free once
+  // the W / U MMAs are done) and written out by two bulk copies ----
   if (alive) {
     const int qd = warp & 3, half = warp >> 2;
     const int d = 32 * qd + lane;
     uint32_t va[32];
     // W [t][d] rows of LR; U [t][d % 64] in the tile of its 64 state columns
-    __half* dst = half ? ws_h(blk, kBU + (d >> 6) * kBUTile) + (d & 63) : ws_h(blk, kBW) + d;
+    __half* dst = half ? reinterpret_cast<__half*>(sm + kStgU + (d >> 6) * kBUTile) + (d & 63)
+                       : reinterpret_cast<__half*>(sm + kStgW) + d;
     const int ld = half ? LUS : LR;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -618,8 +631,15 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       for (int i = 0; i < 32; ++i) dst[(32 * c + i) * ld] = __float2half_rn(__uint_as_float(va[i]));
     }
   }
+  tc::fence_proxy_async_smem();
   tc::fence_before_sync();
-  __syncthreads();
+  alive = __syncthreads_and(alive);
+  if (tid == 0 && alive) {
+    uint8_t* gb = reinterpret_cast<uint8_t*>(blk);
+    bulk_s2g(gb + kBW, sm + kStgW, C * LR * 2);
+    bulk_s2g(gb + kBU, sm + kStgU, 2 * kBUTile);
+    asm volatile("cp.async.bulk.commit_group;\ncp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
   if (warp == 0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
