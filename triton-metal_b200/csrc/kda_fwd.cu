@@ -535,53 +535,70 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   }
   __syncthreads();
   B2_PROF(6);
-  // off-diagonal blocks level by level on tf32 MMAs (m16n8k8, fp32
-  // accumulate), warp J < Ib of level Ib owning block (Ib, J):
-  //   X_IJ = sum_{M=J}^{Ib-1} A_IM T_MJ  (into sAq, no longer needed)
-  //   T_IJ = -T_II X_IJ
+  // off-diagonal blocks of T on tf32 MMAs (m16n8k8, fp32 accumulate) in two
+  // levels of the 2 x 2 block inverse
+  //   T_BA = -T_BB A_BA T_AA    (A, B: the two halves of a diagonal block)
+  // level 1 (16 x 16 halves, warps 0, 1):  blocks (1, 0) and (3, 2)
+  // level 2 (32 x 32 halves, warps 0-3):   blocks (2, 0) (2, 1) (3, 0) (3, 1)
+  // each as X_IJ = sum_M A_IM T_MJ (into sAq, no longer needed), then
+  // T_IJ = -sum_M T_IM X_MJ.
   {
     const int gq = lane >> 2, tq = lane & 3;
-    for (int Ib = 1; Ib < 4; ++Ib) {
-      if (warp < Ib) {
-        const int J = warp, ri = 16 * Ib, cj = 16 * J;
-        float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        for (int m0 = cj; m0 < ri; m0 += 8) {
-          const uint32_t a0 = tf32(sA[(ri + gq) * LT + m0 + tq]), a1 = tf32(sA[(ri + gq + 8) * LT + m0 + tq]);
-          const uint32_t a2 = tf32(sA[(ri + gq) * LT + m0 + tq + 4]), a3 = tf32(sA[(ri + gq + 8) * LT + m0 + tq + 4]);
+    // X rows ri .. ri + 15, columns cj .. cj + 15, over m = mlo .. mhi - 1
+    auto xpart = [&](int ri, int cj, int mlo, int mhi) {
+      float x[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int m0 = mlo; m0 < mhi; m0 += 8) {
+        const uint32_t a0 = tf32(sA[(ri + gq) * LT + m0 + tq]), a1 = tf32(sA[(ri + gq + 8) * LT + m0 + tq]);
+        const uint32_t a2 = tf32(sA[(ri + gq) * LT + m0 + tq + 4]), a3 = tf32(sA[(ri + gq + 8) * LT + m0 + tq + 4]);
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-            mma_tf32(x[nt], a0, a1, a2, a3, tf32(sT[(m0 + tq) * LT + cj + 8 * nt + gq]),
-                     tf32(sT[(m0 + tq + 4) * LT + cj + 8 * nt + gq]));
-        }
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          sAq[(ri + gq) * LT + cj + 8 * nt + 2 * tq] = x[nt][0];
-          sAq[(ri + gq) * LT + cj + 8 * nt + 2 * tq + 1] = x[nt][1];
-          sAq[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq] = x[nt][2];
-          sAq[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq + 1] = x[nt][3];
-        }
-        __syncwarp();
-        float y[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const int kb = ri + 8 * ks;
-          const uint32_t a0 = tf32(sT[(ri + gq) * LT + kb + tq]), a1 = tf32(sT[(ri + gq + 8) * LT + kb + tq]);
-          const uint32_t a2 = tf32(sT[(ri + gq) * LT + kb + tq + 4]), a3 = tf32(sT[(ri + gq + 8) * LT + kb + tq + 4]);
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-            mma_tf32(y[nt], a0, a1, a2, a3, tf32(sAq[(kb + tq) * LT + cj + 8 * nt + gq]),
-                     tf32(sAq[(kb + tq + 4) * LT + cj + 8 * nt + gq]));
-        }
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          sT[(ri + gq) * LT + cj + 8 * nt + 2 * tq] = -y[nt][0];
-          sT[(ri + gq) * LT + cj + 8 * nt + 2 * tq + 1] = -y[nt][1];
-          sT[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq] = -y[nt][2];
-          sT[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq + 1] = -y[nt][3];
-        }
+        for (int nt = 0; nt < 2; ++nt)
+          mma_tf32(x[nt], a0, a1, a2, a3, tf32(sT[(m0 + tq) * LT + cj + 8 * nt + gq]),
+                   tf32(sT[(m0 + tq + 4) * LT + cj + 8 * nt + gq]));
       }
-      __syncthreads();
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        sAq[(ri + gq) * LT + cj + 8 * nt + 2 * tq] = x[nt][0];
+        sAq[(ri + gq) * LT + cj + 8 * nt + 2 * tq + 1] = x[nt][1];
+        sAq[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq] = x[nt][2];
+        sAq[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq + 1] = x[nt][3];
+      }
+    };
+    // T rows ri .. ri + 15, columns cj .. cj + 15 = -sum_{k = klo}^{ri + 15} T[ri][k] X[k][cj]
+    auto ypart = [&](int ri, int cj, int klo) {
+      float y[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int kb = klo; kb < ri + 16; kb += 8) {
+        const uint32_t a0 = tf32(sT[(ri + gq) * LT + kb + tq]), a1 = tf32(sT[(ri + gq + 8) * LT + kb + tq]);
+        const uint32_t a2 = tf32(sT[(ri + gq) * LT + kb + tq + 4]), a3 = tf32(sT[(ri + gq + 8) * LT + kb + tq + 4]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          mma_tf32(y[nt], a0, a1, a2, a3, tf32(sAq[(kb + tq) * LT + cj + 8 * nt + gq]),
+                   tf32(sAq[(kb + tq + 4) * LT + cj + 8 * nt + gq]));
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        sT[(ri + gq) * LT + cj + 8 * nt + 2 * tq] = -y[nt][0];
+        sT[(ri + gq) * LT + cj + 8 * nt + 2 * tq + 1] = -y[nt][1];
+        sT[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq] = -y[nt][2];
+        sT[(ri + gq + 8) * LT + cj + 8 * nt + 2 * tq + 1] = -y[nt][3];
+      }
+    };
+    if (warp < 2) {  // level 1: (1, 0) and (3, 2)
+      const int ri = warp ? 48 : 16, cj = ri - 16;
+      xpart(ri, cj, cj, ri);
+      __syncwarp();
+      ypart(ri, cj, ri);
     }
+    __syncthreads();
+    if (warp < 4) {  // level 2, X: rows 32 .. 63, columns 0 .. 31
+      const int ri = 32 + 16 * (warp >> 1), cj = 16 * (warp & 1);
+      xpart(ri, cj, cj, 32);
+    }
+    __syncthreads();
+    if (warp < 4) {  // level 2, T: rows 32 .. 63, columns 0 .. 31
+      const int ri = 32 + 16 * (warp >> 1), cj = 16 * (warp & 1);
+      ypart(ri, cj, 32);
+    }
+    __syncthreads();
   }
   B2_PROF(7);
   // ---- 8. T (bf16) as the B operand: rows t, K = j ----
