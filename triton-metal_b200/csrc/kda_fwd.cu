@@ -91,7 +91,8 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 //     rows of block rows 3 and 2 (then 1 and 0), B = [L; Lq] for all 64 i;
 //     every lower block of A_kk and A_qk lands in TMEM.
 //  4. T = (I + A_kk)^-1: diagonal 16 x 16 blocks by column substitution
-//     (fp32), then T_IJ = -T_II sum_M A_IM T_MJ level by level on tf32 MMAs.
+//     (fp32), then the off-diagonal blocks in two levels of the 2 x 2 block
+//     inverse T_BA = -T_BB A_BA T_AA (16- then 32-row halves) on tf32 MMAs.
 //  5. W^T = (beta K e^G)^T T^T and U^T = (beta V)^T T^T as two tcgen05.mma
 //     (M = 128 = Dk / Dv, N = 64, K = 64), bf16 operands, fp32 in TMEM.
 //  6. W, U, A_qk, scale Q e^G, K e^{G_last - G} (fp16) and e^{G_last} go to
