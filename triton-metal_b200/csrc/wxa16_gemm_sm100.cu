@@ -562,34 +562,28 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 
 }  // namespace gemm
 
-// Tile width for a persistent grid of `sms` CTAs.  The tiles of the last
-// round leave SMs idle, so a narrower tile that fills the rounds better can
-// finish first (C2: N = 14336, 16 row tiles -> 896 tiles of 256 columns =
-// 6.05 rounds of 148, or 1024 tiles of 224 = 6.92 rounds).  Cost model:
-// rounds x (bn + 32), the 32 standing for the per-tile A stream and epilogue.
-// Measured at C2: an N = 224 tile costs ~97% of an N = 256 one in the bf16
-// and W4 modes (tensor-bound: the narrower tile lost 2-4%), while the W8
-// mode, bound by its dequantisers, gained 10% (988 -> 1084 TF/s); so only W8
-// considers widths between 128 and 256.  B2_GEMM_BN overrides the choice
-// (a multiple of 32 in 128..256; for tuning).
-static int pick_bn(int mode, int tiles_m, int64_t N, int sms) {
+// Tile width for a persistent grid of `sms` CTAs: 256 or 224 columns,
+// whichever finishes the tiles in less time.  A round of tiles costs one
+// tile's time, and a 224-column tile measured ~97% of a 256-column one (the
+// N = 224 MMA costs about as much as N = 256; the dequant work is 12.5%
+// less), while narrower tiles were much slower (W4 / W8 at M = 4096,
+// K = 4096: 192 columns -10..-25%, 128 columns -30..-40%).  So the model is
+// rounds x (256: 100, 224: 97).  C2 (N = 14336): 7 rounds either way -> 224;
+// bf16 at C2 (128-row tiles): 13 rounds of 256 against 14 of 224 -> 256;
+// a two-GPU column shard (N = 7168): 4 rounds either way -> 224.
+// B2_GEMM_BN overrides the choice (a multiple of 32 in 128..256; for tuning).
+static int pick_bn(int tiles_m, int64_t N, int sms) {
   static const int forced = [] {
     const char* e = getenv("B2_GEMM_BN");
     const int v = e ? atoi(e) : 0;
     return (v >= 128 && v <= gemm::BN && v % 32 == 0) ? v : 0;
   }();
   if (forced) return forced;
-  int best = gemm::BN;
-  int64_t best_cost = -1;
-  for (int bn = gemm::BN; bn >= 128; bn -= (mode == 1 ? 32 : 128)) {
+  auto cost = [&](int bn) {
     const int64_t tiles = (int64_t)tiles_m * ((N + bn - 1) / bn);
-    const int64_t cost = ((tiles + sms - 1) / sms) * (bn + 32);
-    if (best_cost < 0 || cost < best_cost) {
-      best = bn;
-      best_cost = cost;
-    }
-  }
-  return best;
+    return ((tiles + sms - 1) / sms) * (bn == gemm::BN ? 100 : 97);
+  };
+  return cost(224) < cost(gemm::BN) ? 224 : gemm::BN;
 }
 
 template <int MODE, int DT, bool ZP>
@@ -606,7 +600,7 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   }
   const CUtensorMapDataType adt = DT == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int grid = num_sms();
-  const int bn = pick_bn(MODE, (int)((M + C::BMC - 1) / C::BMC), N, grid);
+  const int bn = pick_bn((int)((M + C::BMC - 1) / C::BMC), N, grid);
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, x, adt, K, M, K * 2, BK, C::BMC, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ERR_INVALID;
   bool okb;
