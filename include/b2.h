@@ -220,8 +220,9 @@ B2_API int b2_repeat_kv(const void* input, void* output, int64_t n_kv_heads,
  *   o       : dtype [B,T,H,Dv];  final_state : fp32 [B,H,Dk,Dv] or NULL
  *   workspace: device scratch of b2_kda_workspace_size(...) bytes
  *             (80,384 bytes per (b, h, 64-step chunk)), 16-byte aligned.
- * Two kernels: a per-chunk WY/UT transform on tcgen05 and a fused state +
- * output recurrence; the state is carried in fp32.
+ * Two kernels: a per-chunk WY/UT transform on tcgen05 and the state +
+ * output recurrence on clusters of two CTAs (one carries the state, its
+ * partner computes the outputs); the state is carried in fp32.
  */
 B2_API size_t b2_kda_workspace_size(int64_t B, int64_t T, int64_t H,
                              int64_t Dk, int64_t Dv, int64_t chunk);
