@@ -53,6 +53,7 @@ constexpr float kRescaleThreshold = 8.f;  // log2 units
 struct Params {
   int B, Hq, Hkv, Sq, Skv, causal, q_tiles;
   int window;  // > 0 (causal only): key kv visible to qpos iff qpos - window < kv <= qpos
+  int single;  // 1: one Q tile per CTA instead of a pair (small grids)
   float scale_log2;
   void* o;
   int64_t os_b, os_h, os_s;
@@ -320,8 +321,11 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int npairs = (p.q_tiles + 1) / 2;
-  const int pi = npairs - 1 - (int)blockIdx.x;  // longest causal pairs first
+  // one unit = a pair of Q tiles, or one Q tile when the grid would not fill
+  // the SMs (p.single: the second softmax warpgroup idles, the CTAs halve)
+  const int per = p.single ? 1 : 2;
+  const int nunits = (p.q_tiles + per - 1) / per;
+  const int pi = nunits - 1 - (int)blockIdx.x;  // longest causal units first
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.Hq / p.Hkv);
   const int nkv_all = (p.Skv + BKV - 1) / BKV;
@@ -330,8 +334,10 @@ fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   int q0[2], nkv[2], kb[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
-    q0[u] = (2 * pi + u) * BQ;
-    nkv[u] = (2 * pi + u < p.q_tiles) ? (p.causal ? min(nkv_all, (q0[u] + BQ - 1) / BKV + 1) : nkv_all) : 0;
+    q0[u] = (per * pi + u) * BQ;
+    nkv[u] = (u < per && per * pi + u < p.q_tiles)
+                 ? (p.causal ? min(nkv_all, (q0[u] + BQ - 1) / BKV + 1) : nkv_all)
+                 : 0;
     kb[u] = p.window > 0 ? min(max(0, q0[u] - p.window + 1) / BKV, nkv[u]) : 0;
   }
   const int nkv_max = max(nkv[0], nkv[1]);
@@ -772,7 +778,9 @@ static int fa_fwd_impl(const void* q, const void* k, const void* v, void* o, int
       p.os_h = os[1];
       p.os_s = os[2];
       p.err = err;
-      dim3 grid((p.q_tiles + 1) / 2, (unsigned)Hq, (unsigned)B);
+      // Q-tile pairs, or single Q tiles when the pairs would not fill the SMs
+      p.single = (int64_t)((p.q_tiles + 1) / 2) * Hq * B < num_sms() ? 1 : 0;
+      dim3 grid(p.single ? p.q_tiles : (p.q_tiles + 1) / 2, (unsigned)Hq, (unsigned)B);
       if (D == 128) {
         if (dtype == B2_F16) launch_fa_tc<128, fa::kF16>(tq, tk, tv, p, grid, st);
         else launch_fa_tc<128, fa::kBF16>(tq, tk, tv, p, grid, st);
