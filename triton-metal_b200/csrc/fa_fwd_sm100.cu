@@ -7,7 +7,8 @@
 // and the GQA head map kv_head = q_head / n_q_per_kv (_msl_templates.py:2101).
 //
 // Fast path (D = 128, bf16/fp16): one CTA per pair of 128-row Q tiles of one
-// (b, h), longest causal pairs first.
+// (b, h), longest causal pairs first (one Q tile per CTA when the pairs would
+// not fill the SMs).
 //   warp 0      TMA: both Q tiles once; K tiles (3-stage ring) and V tiles
 //               (2-stage) shared by the two Q tiles
 //   warp 1      TMEM owner + MMA issuer: S_u = Q_u K^T (M=N=128, K=16 x 8)
