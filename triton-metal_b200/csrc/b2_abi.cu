@@ -112,6 +112,26 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, ui
   return true;
 }
 
+bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t (&dims)[3],
+                  const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3], CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled unavailable");
+    return false;
+  }
+  const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  const cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+  const cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    return false;
+  }
+  return true;
+}
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device)
 // and size instead of on every launch.
 void set_max_smem(const void* func, int bytes) {

@@ -145,6 +145,11 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, ui
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
+// 3-D tiled tensor map: dims {d0 (contiguous), d1, d2}, byte strides of d1
+// and d2, box {b0, b1, b2}.  Not cached (one encode per call).
+bool make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t (&dims)[3],
+                  const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3], CUtensorMapSwizzle swizzle);
+
 int num_sms();
 
 // cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes), cached per

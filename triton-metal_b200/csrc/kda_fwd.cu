@@ -29,6 +29,7 @@
 // ever leaves the SM.
 #include "b2_common.cuh"
 #include "tc_common.cuh"
+#include <string.h>
 #include <type_traits>
 
 namespace b2 {
@@ -94,6 +95,8 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 //     (fp32), then the off-diagonal blocks in two levels of the 2 x 2 block
 //     inverse T_BA = -T_BB A_BA T_AA (16- then 32-row halves) on tf32 MMAs.
 //  5. W^T = (beta K e^G)^T T^T and U^T = (beta V)^T T^T as two tcgen05.mma
+//     (bf16: v arrives by TMA as the MN-major A operand and beta is folded
+//     into the columns of T)
 //     (M = 128 = Dk / Dv, N = 64, K = 64), bf16 operands, fp32 in TMEM.
 //  6. W, U, A_qk, scale Q e^G, K e^{G_last - G} (fp16) and e^{G_last} go to
 //     the workspace block of this chunk in kernel B's stage layout.
@@ -126,7 +129,7 @@ constexpr uint32_t kGref = kAU + 128 * 64 * 2;           // G at rows 0, 16, 32,
 constexpr uint32_t kBeta = kGref + 5 * DK * 4;
 constexpr uint32_t kGap = kBeta + C * 4;                 // per block max exponent gap (fp32 bits)
 constexpr uint32_t kBar = kGap + 16;
-constexpr uint32_t kHold = kBar + 16;
+constexpr uint32_t kHold = kBar + 24;  // bar[3]
 constexpr uint32_t kBytes = kHold + 16;
 constexpr size_t kSmem = kBytes + 1024;                  // + alignment of the swizzled tiles
 constexpr uint32_t kTmemCols = 256;
@@ -222,8 +225,12 @@ template <typename T>
 __global__ void __launch_bounds__(prep::kThreads, 2)
 kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                 const float* __restrict__ g, const T* __restrict__ beta, float* __restrict__ ws, int B, int Tlen,
-                int H, float scale, unsigned* __restrict__ err) {
+                int H, float scale, unsigned* __restrict__ err, const __grid_constant__ CUtensorMap tmV) {
   using namespace prep;
+  // bf16 inputs: the chunk's v tile [64 t][128 d] arrives by TMA straight into
+  // the U MMA's A operand (MN-major), and beta moves into T's columns
+  // (U = T diag(beta) V, W = T diag(beta) K e^G), so no thread touches v.
+  constexpr bool kTmaV = std::is_same<T, __nv_bfloat16>::value;
   using P2 = Pair<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -244,7 +251,20 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   if (tid == 0) {
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
+    mbar_init(&bar[2], 1);
     fence_mbar_init();
+    if constexpr (kTmaV) {
+      // 3-D map {d, h, (b, t)}: two boxes of [64 t][1][64 d] (128-byte swizzle)
+      mbar_arrive_expect_tx(&bar[2], 2u * C * 64 * 2);
+      const int tv = b * Tlen + chunk * C;
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb)
+        asm volatile(
+            "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+                smem_u32(sm + kAU + hb * (C * 128))),
+            "l"(&tmV), "r"(64 * hb), "r"(h), "r"(tv), "r"(smem_u32(&bar[2]))
+            : "memory");
+    }
   }
   if (tid < 4) sGap[tid] = 0u;
   if (warp == 0) {
@@ -357,7 +377,7 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     *reinterpret_cast<__half2*>(wsQg + t * LR + d0) = __floats2half2_rn(lq.x * eG0.x, lq.y * eG0.y);
     *reinterpret_cast<__half2*>(wsKr + t * LR + d0) = __floats2half2_rn(kj.x * cKr.x, kj.y * cKr.y);
     const float bt = sBeta[t];
-    wk[r] = make_float2(bt * lo.x * eG0.x, bt * lo.y * eG0.y);
+    wk[r] = kTmaV ? make_float2(lo.x * eG0.x, lo.y * eG0.y) : make_float2(bt * lo.x * eG0.x, bt * lo.y * eG0.y);
   }
   tc::fence_proxy_async_smem();
   tc::fence_before_sync();
@@ -386,8 +406,10 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   // beta V for the U operand (loads issued before the W stores)
   {
     typename P2::R vraw[16];
+    if constexpr (!kTmaV) {
 #pragma unroll
-    for (int r = 0; r < 16; ++r) vraw[r] = P2::load(v + (row0 + (int64_t)(r0 + r) * H) * DV + d0);
+      for (int r = 0; r < 16; ++r) vraw[r] = P2::load(v + (row0 + (int64_t)(r0 + r) * H) * DV + d0);
+    }
     uint32_t p0[8], p1[8];
 #pragma unroll
     for (int r = 0; r < 16; r += 2) {
@@ -401,23 +423,25 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       *reinterpret_cast<uint4*>(sm + kAW + sw_off(d0 + 1, r0 + 8 * c, 128)) =
           make_uint4(p1[4 * c], p1[4 * c + 1], p1[4 * c + 2], p1[4 * c + 3]);
     }
+    if constexpr (!kTmaV) {
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const float bt = sBeta[r0 + r];
-      const float2 vv = P2::f2(vraw[r]);
-      wk[r] = make_float2(bt * vv.x, bt * vv.y);
-    }
+      for (int r = 0; r < 16; ++r) {
+        const float bt = sBeta[r0 + r];
+        const float2 vv = P2::f2(vraw[r]);
+        wk[r] = make_float2(bt * vv.x, bt * vv.y);
+      }
 #pragma unroll
-    for (int r = 0; r < 16; r += 2) {
-      p0[r / 2] = bf2(wk[r].x, wk[r + 1].x);
-      p1[r / 2] = bf2(wk[r].y, wk[r + 1].y);
-    }
+      for (int r = 0; r < 16; r += 2) {
+        p0[r / 2] = bf2(wk[r].x, wk[r + 1].x);
+        p1[r / 2] = bf2(wk[r].y, wk[r + 1].y);
+      }
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      *reinterpret_cast<uint4*>(sm + kAU + sw_off(d0, r0 + 8 * c, 128)) =
-          make_uint4(p0[4 * c], p0[4 * c + 1], p0[4 * c + 2], p0[4 * c + 3]);
-      *reinterpret_cast<uint4*>(sm + kAU + sw_off(d0 + 1, r0 + 8 * c, 128)) =
-          make_uint4(p1[4 * c], p1[4 * c + 1], p1[4 * c + 2], p1[4 * c + 3]);
+      for (int c = 0; c < 2; ++c) {
+        *reinterpret_cast<uint4*>(sm + kAU + sw_off(d0, r0 + 8 * c, 128)) =
+            make_uint4(p0[4 * c], p0[4 * c + 1], p0[4 * c + 2], p0[4 * c + 3]);
+        *reinterpret_cast<uint4*>(sm + kAU + sw_off(d0 + 1, r0 + 8 * c, 128)) =
+            make_uint4(p1[4 * c], p1[4 * c + 1], p1[4 * c + 2], p1[4 * c + 3]);
+      }
     }
   }
   if (tid < DK / 2)
@@ -607,7 +631,14 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     const int t = tid >> 2, c0 = 16 * (tid & 3);
     uint32_t pk[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pk[i] = bf2(sT[t * LT + c0 + 2 * i], sT[t * LT + c0 + 2 * i + 1]);
+    for (int i = 0; i < 8; ++i) {
+      float t0 = sT[t * LT + c0 + 2 * i], t1 = sT[t * LT + c0 + 2 * i + 1];
+      if constexpr (kTmaV) {  // T diag(beta)
+        t0 *= sBeta[c0 + 2 * i];
+        t1 *= sBeta[c0 + 2 * i + 1];
+      }
+      pk[i] = bf2(t0, t1);
+    }
     *reinterpret_cast<uint4*>(sm + kBT + sw_off(t, c0, 64)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     *reinterpret_cast<uint4*>(sm + kBT + sw_off(t, c0 + 8, 64)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
   }
@@ -621,10 +652,22 @@ kda_prep_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     for (int s = 0; s < C / 16; ++s)
       tc::mma_f16_ss(tmem, tc::desc_kmajor_sw128(sm + kAW) + 2u * s, tc::desc_kmajor_sw128(sm + kBT) + 2u * s,
                      idesc, s != 0);
+    if constexpr (kTmaV) {
+      // v [t][d] as the MN-major A operand: 16 rows of t per k-step, the two
+      // 64-column blocks of d 8 KB apart
+      constexpr uint32_t idesc_v = tc::idesc_f16(128, 64, true, true, false);
+      if (mbar_wait(&bar[2], 0, err, 0xB230000Cu)) {
 #pragma unroll
-    for (int s = 0; s < C / 16; ++s)
-      tc::mma_f16_ss(tmem + 64, tc::desc_kmajor_sw128(sm + kAU) + 2u * s, tc::desc_kmajor_sw128(sm + kBT) + 2u * s,
-                     idesc, s != 0);
+        for (int s = 0; s < C / 16; ++s)
+          tc::mma_f16_ss(tmem + 64, tc::smem_desc(sm + kAU + s * 16 * 128, C * 128, 1024, tc::kSwizzle128B),
+                         tc::desc_kmajor_sw128(sm + kBT) + 2u * s, idesc_v, s != 0);
+      }
+    } else {
+#pragma unroll
+      for (int s = 0; s < C / 16; ++s)
+        tc::mma_f16_ss(tmem + 64, tc::desc_kmajor_sw128(sm + kAU) + 2u * s, tc::desc_kmajor_sw128(sm + kBT) + 2u * s,
+                       idesc, s != 0);
+    }
     tc::commit(&bar[1]);
   }
   if (alive) alive = mbar_wait(&bar[1], 0, err, 0xB2300002u);
@@ -1128,12 +1171,23 @@ extern "C" int b2_kda_fwd(const void* q, const void* k, const void* v, const flo
   B2_CHECK_ARG(err, B2_ERR_LAUNCH, "kda_fwd: no device error word");
   const dim3 ga((unsigned)(T / chunk), (unsigned)H, (unsigned)B);
   const dim3 gb(2 * (kda::DV / kda::RV), (unsigned)H, (unsigned)B);  // clusters of 2 along x
+  CUtensorMap tmv;
+  memset(&tmv, 0, sizeof(tmv));
+  if (dtype == B2_BF16) {
+    // v [B, T, H, Dv] as {d, h, (b, t)}
+    const uint64_t dims[3] = {(uint64_t)Dv, (uint64_t)H, (uint64_t)(B * T)};
+    const uint64_t strides[2] = {(uint64_t)Dv * 2, (uint64_t)H * Dv * 2};
+    const uint32_t box[3] = {64, 1, (uint32_t)kda::C};
+    B2_CHECK_ARG(make_tmap_3d(&tmv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B),
+                 B2_ERR_INVALID, "kda_fwd: v tensor map: %s", b2_last_error());
+  }
 #define B2_KDA_LAUNCH(TY)                                                                                         \
   do {                                                                                                            \
     set_max_smem((const void*)kda::kda_prep_kernel<TY>, (int)kda::prep::kSmem);                                  \
     set_max_smem((const void*)kda::kda_recur_kernel<TY>, (int)kda::kRSmem);                                      \
     kda::kda_prep_kernel<TY><<<ga, kda::prep::kThreads, kda::prep::kSmem, st>>>(                                  \
-        (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale, err);   \
+        (const TY*)q, (const TY*)k, (const TY*)v, g, (const TY*)beta, ws, (int)B, (int)T, (int)H, scale, err, tmv); \
     kda::kda_recur_kernel<TY><<<gb, kda::kRThreads, kda::kRSmem, st>>>(                                         \
         ws, initial_state, final_state, (TY*)o, (int)B, (int)T, (int)H, err);                                    \
   } while (0)
