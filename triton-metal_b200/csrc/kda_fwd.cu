@@ -898,6 +898,10 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
       alive = __syncthreads_and(mbar_wait(&full0[sl], (uint32_t)(c / kNS0) & 1u, err, 0xB2300003u));
       if (!alive) break;
       B2_RPROF(1, c);
+      // this chunk's fragment slot in the output CTA (its previous hand-over,
+      // two chunks back, is long consumed)
+      const bool sent = mbar_wait_cluster(&dempty[ds * RW + warp], ((uint32_t)(c >> 1) & 1u) ^ 1u, err, 0xB230000Bu);
+      uint4* stg = slot_stage + ds * (kSlotBytes / 16);
       const __half* sW = reinterpret_cast<const __half*>(st + kBW);
       const __half* sKr = reinterpret_cast<const __half*>(st + kBKr);
       const float* sGl = reinterpret_cast<const float*>(st + kBGl);
@@ -927,6 +931,8 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
         vp[2 * p + 1][2] = -a3.x;
         vp[2 * p + 1][3] = -a3.y;
       }
+      // V' MMAs; in their issue gaps: S^T o e^{G_last} (the MMAs read the
+      // fp16 copy) and the staging of the S^T fragments for the output CTA
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
 #pragma unroll
@@ -938,6 +944,15 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
           mma_16816<B2_F16>(vp[2 * np], sa[kk], w0);
           mma_16816<B2_F16>(vp[2 * np + 1], sa[kk], w1);
         }
+#pragma unroll
+        for (int nt = 2 * kk; nt < 2 * kk + 2; ++nt) {
+          const float2 gl = *reinterpret_cast<const float2*>(sGl + 8 * nt + 2 * tq);
+          S[nt][0] *= gl.x;
+          S[nt][1] *= gl.y;
+          S[nt][2] *= gl.x;
+          S[nt][3] *= gl.y;
+        }
+        if (sent) stg[kk * 32] = make_uint4(sa[kk][0], sa[kk][1], sa[kk][2], sa[kk][3]);
       }
       // V'^T = -acc as fp16 A fragments over the chunk's 4 16-step blocks
       uint32_t va[4][4];
@@ -949,34 +964,7 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
         va[kk][3] = pack_h2(-vp[2 * kk + 1][2], -vp[2 * kk + 1][3]);
       }
       B2_RPROF(2, c);
-      // hand S^T and V'^T to the output warp of the same columns: asynchronous
-      // remote stores that complete the slot's mbarrier transaction there
-      bool sent = mbar_wait_cluster(&dempty[ds * RW + warp], ((uint32_t)(c >> 1) & 1u) ^ 1u, err, 0xB230000Bu);
-      B2_RPROF(3, c);
-      if (sent) {
-        // local staging slot (free: the output warp consumed its previous copy),
-        // then one bulk copy of the warp's 6 KB into the output CTA
-        uint4* stg = slot_stage + ds * (kSlotBytes / 16);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) stg[kk * 32] = make_uint4(sa[kk][0], sa[kk][1], sa[kk][2], sa[kk][3]);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) stg[(8 + kk) * 32] = make_uint4(va[kk][0], va[kk][1], va[kk][2], va[kk][3]);
-        tc::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0)
-          bulk_s2cluster(slot_remote + ds * kSlotBytes, smb + kSlots0 + ds * kSlotBytes + warp * kSlotWarp, kSlotWarp,
-                         dfull_remote + ds * RW * 8);
-      }
-      B2_RPROF(4, c);
-      // S^T = S^T o e^{G_last} (per dk column) + V'^T Kr
-#pragma unroll
-      for (int nt = 0; nt < 16; ++nt) {
-        const float2 gl = *reinterpret_cast<const float2*>(sGl + 8 * nt + 2 * tq);
-        S[nt][0] *= gl.x;
-        S[nt][1] *= gl.y;
-        S[nt][2] *= gl.x;
-        S[nt][3] *= gl.y;
-      }
+      // S^T = S^T o e^{G_last} + V'^T Kr, staging V'^T in the MMA gaps
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
@@ -987,6 +975,16 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
           mma_16816<B2_F16>(S[2 * np], va[kk], k0);
           mma_16816<B2_F16>(S[2 * np + 1], va[kk], k1);
         }
+        if (sent) stg[(8 + kk) * 32] = make_uint4(va[kk][0], va[kk][1], va[kk][2], va[kk][3]);
+      }
+      // hand the staged S^T / V'^T over: one bulk copy of the warp's 6 KB into
+      // the output CTA, completing the slot's mbarrier transaction there
+      if (sent) {
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0)
+          bulk_s2cluster(slot_remote + ds * kSlotBytes, smb + kSlots0 + ds * kSlotBytes + warp * kSlotWarp, kSlotWarp,
+                         dfull_remote + ds * RW * 8);
       }
       B2_RPROF(5, c);
       // every warp is done with stage sl (and agrees on the hand-over)
@@ -1052,12 +1050,11 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
         va[kk][2] = x.z;
         va[kk][3] = x.w;
       }
-      // the slot is free again: re-arm it for chunk c + 2, then tell the state warp
+      // the slot's contents are in registers: re-arm it for chunk c + 2 (the
+      // state warp is told after the MMAs, when the release-arrive no longer
+      // waits on outstanding memory operations)
       __syncwarp();
-      if (lane == 0) {
-        if (c + 2 < nc) mbar_arrive_expect_tx(&dfull[ds * RW + warp], kSlotWarp);
-        mbar_arrive_remote(dempty_remote + ds * RW * 8);
-      }
+      if (lane == 0 && c + 2 < nc) mbar_arrive_expect_tx(&dfull[ds * RW + warp], kSlotWarp);
       float oa[8][4];
 #pragma unroll
       for (int n = 0; n < 8; ++n)
@@ -1091,6 +1088,8 @@ kda_recur_kernel(const float* __restrict__ ws, const float* __restrict__ s0, flo
           mma_16816<B2_F16>(oa[2 * np + 1], va[kk], a1);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(dempty_remote + ds * RW * 8);  // the slot is free again
       // O^T -> staging tile [t][dv], then coalesced rows of o
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
