@@ -22,12 +22,13 @@
 //               accumulator (2 x 256 columns, double-buffered across tiles)
 //               and commits the stage back to the producer;
 //   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, (per-channel
-//               scale), bf16 convert, global store; frees the accumulator;
+//               scale), bf16 convert, 32 x 32 tile staged in shared memory
+//               and written by a TMA store; frees the accumulator;
 //   warps 6-21  (MODE 1/2) dequantisers: packed tile -> exact integers ->
 //               scaled bf16 written straight into the 128B-swizzled K-major
 //               B layout the MMA reads, then fence.proxy.async + arrive.
 // M and N may be ragged (multiples of 1 and 8): the TMA boxes past the edge
-// read zeros and the epilogue masks its stores.  All waits are bounded
+// read zeros and the TMA stores clip at M / N.  All waits are bounded
 // (error word + early exit).
 #include "tc_common.cuh"
 #include <stdlib.h>
@@ -43,6 +44,9 @@ constexpr int kTmemCols = 2 * kAccCols;
 constexpr int kDequantWarps = 16;
 // W8 with zeros: per-tile row sums of x, [2 k-halves][256 rows] fp32
 constexpr int kXsBytes = 2 * 2 * BM * 4;
+// epilogue: one 32 x 32 output tile (16-bit) per epilogue warp, stored by TMA
+constexpr int kEpiTile = 32 * 32 * 2;
+constexpr int kEpiBytes = 4 * kEpiTile;
 
 template <int MODE>
 struct Cfg {
@@ -66,8 +70,12 @@ struct Cfg {
   static constexpr int kThreads = kWarps * 32;
   static constexpr size_t kSmem = (size_t)kStages * kStageBytes + (SPLITB ? kBRegion : 0) + 1024 /*align*/ +
                                   256 /*barriers*/ +
-                                  (MODE == 1 ? kXsBytes : 0);
+                                  (MODE == 1 ? kXsBytes : 0) + kEpiBytes;
 };
+
+static_assert(Cfg<0>::kSmem <= 227 * 1024 && Cfg<1>::kSmem <= 227 * 1024 && Cfg<2>::kSmem <= 227 * 1024 &&
+                  Cfg<3>::kSmem <= 227 * 1024,
+              "shared memory per CTA");
 
 struct Params {
   int M, N, K, G;
@@ -210,7 +218,7 @@ __device__ __forceinline__ float sum8(uint4 v) {
 template <int MODE, int DT, bool ZP>
 __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
 wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  const Params p) {
+                  const __grid_constant__ CUtensorMap tmO, const Params p) {
   using C = Cfg<MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -229,6 +237,8 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* xsbuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // MODE 1 && ZP
+  // 128-byte aligned (full sits on a 1024-byte boundary)
+  uint8_t* sEpi = reinterpret_cast<uint8_t*>(full) + 256 + (MODE == 1 ? kXsBytes : 0);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kblocks = p.K / BK;
@@ -377,6 +387,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   } else if (warp < 6) {
     // ------------------------------ epilogue ----------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* const stg = sEpi + q * kEpiTile;
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * p.bn;
@@ -397,18 +408,17 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       }
 #pragma unroll 1
       for (int h = 0; h < (C::TWO ? 2 : 1); ++h) {
-        const int row = m0 + h * BM + q * 32 + lane;
         const uint32_t tcol = C::TWO ? h * kAccCols : acc * kAccCols;
-        uint16_t* orow = p.out + (size_t)row * p.N + n0;
+        const int row0 = m0 + h * BM + q * 32;  // first row of this warp's 32
 #pragma unroll 1
         for (int c = 0; c < p.bn / 32; ++c) {
           uint32_t r[32];
-          // warp-collective: every lane loads, rows / columns past the edge
-          // only skip their stores
+          // warp-collective: every lane loads; tiles past the edge skip their
+          // store, and the TMA store clips the rows / columns past M / N
           tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + tcol + c * 32, r);
           tc::tmem_ld_wait();
           const int nc = n0 + c * 32;
-          if (row >= p.M || nc >= p.N) continue;
+          if (row0 >= p.M || nc >= p.N) continue;
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -424,17 +434,19 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             }
             packed[j] = pack_pair<DT>(v0, v1);
           }
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-          if (nc + 32 <= p.N) {
+          // the previous chunk's store has read the staging tile
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          // row `lane` of the 32 x 32 tile (64 bytes, unswizzled)
+          uint4* srow = reinterpret_cast<uint4*>(stg + lane * 64);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-          } else {
-            // ragged N (multiple of 8): whole 16-byte pieces only
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              if (nc + 8 * j < p.N)
-                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          for (int j = 0; j < 4; ++j)
+            srow[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, stg, nc, row0);
+            bulk_commit();
           }
         }
         tc::fence_before_sync();
@@ -442,6 +454,8 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         if (lane == 0) mbar_arrive(&tempty[C::TWO ? h : acc]);
       }
     }
+    // the staging tiles stay valid until the last store has completed
+    if (lane == 0) bulk_wait_all();
   } else if constexpr (MODE != 0) {
     // ------------------------------ dequantisers ------------------------------
     const int d = (warp - 6) * 32 + lane;
@@ -601,7 +615,7 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   const CUtensorMapDataType adt = DT == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int grid = num_sms();
   const int bn = pick_bn((int)((M + C::BMC - 1) / C::BMC), N, grid);
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
   if (!make_tmap_2d(&ta, x, adt, K, M, K * 2, BK, C::BMC, CU_TENSOR_MAP_SWIZZLE_128B)) return B2_ERR_INVALID;
   bool okb;
   if (MODE == 0)
@@ -613,6 +627,8 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   else
     okb = make_tmap_2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, BK / 2, bn);
   if (!okb) return B2_ERR_INVALID;
+  // output [M, N] 16-bit, stored 32 x 32 per epilogue warp
+  if (!make_tmap_2d(&to, out, CU_TENSOR_MAP_DATA_TYPE_UINT16, N, M, N * 2, 32, 32)) return B2_ERR_INVALID;
   Params p;
   p.M = (int)M;
   p.N = (int)N;
@@ -630,7 +646,7 @@ static int launch_gemm(const void* x, const void* w, const void* scales, const v
   if (grid > ntiles) grid = ntiles;
   auto kern = wxa16_gemm_kernel<MODE, DT, ZP>;
   set_max_smem((const void*)kern, (int)C::kSmem);
-  kern<<<grid, C::kThreads, C::kSmem, st>>>(ta, tb, p);
+  kern<<<grid, C::kThreads, C::kSmem, st>>>(ta, tb, to, p);
   return launch_status("wxa16_gemm");
 }
 
