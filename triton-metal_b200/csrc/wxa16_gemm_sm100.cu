@@ -47,6 +47,9 @@ constexpr int kXsBytes = 2 * 2 * BM * 4;
 // epilogue: one 32 x 32 output tile (16-bit) per epilogue warp, stored by TMA
 constexpr int kEpiTile = 32 * 32 * 2;
 constexpr int kEpiBytes = 4 * kEpiTile;
+// W8: each epilogue warp's copy of the tile's per-channel scales and zeros
+// (16-bit, [2][BN])
+constexpr int kEpiSzBytes = 4 * 2 * BN * 2;
 
 template <int MODE>
 struct Cfg {
@@ -70,7 +73,7 @@ struct Cfg {
   static constexpr int kThreads = kWarps * 32;
   static constexpr size_t kSmem = (size_t)kStages * kStageBytes + (SPLITB ? kBRegion : 0) + 1024 /*align*/ +
                                   256 /*barriers*/ +
-                                  (MODE == 1 ? kXsBytes : 0) + kEpiBytes;
+                                  (MODE == 1 ? kXsBytes + kEpiSzBytes : 0) + kEpiBytes;
 };
 
 static_assert(Cfg<0>::kSmem <= 227 * 1024 && Cfg<1>::kSmem <= 227 * 1024 && Cfg<2>::kSmem <= 227 * 1024 &&
@@ -176,6 +179,22 @@ __device__ __forceinline__ uint32_t pack_pair(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+}
+template <int DT>
+__device__ __forceinline__ void unpack_pair(uint32_t w, float& lo, float& hi) {
+  if constexpr (DT == B2_BF16) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xffff0000u);
+  } else {
+    const __half2 h2 = *reinterpret_cast<const __half2*>(&w);
+    lo = __low2float(h2);
+    hi = __high2float(h2);
+  }
+}
+// 32-bit word j (0 .. 15) of four 16-byte vectors
+__device__ __forceinline__ uint32_t word_of(const uint4 (&v)[4], int j) {
+  const uint4& u = v[j >> 2];
+  return (j & 3) == 0 ? u.x : (j & 3) == 1 ? u.y : (j & 3) == 2 ? u.z : u.w;
 }
 template <int DT>
 __device__ __forceinline__ float ld_act(const uint16_t* p) {
@@ -388,11 +407,23 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     // ------------------------------ epilogue ----------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     uint8_t* const stg = sEpi + q * kEpiTile;
+    uint16_t* const wsz = reinterpret_cast<uint16_t*>(sEpi + kEpiBytes) + q * 2 * BN;  // MODE 1
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int m0 = (tile % p.tiles_m) * C::BMC, n0 = (tile / p.tiles_m) * p.bn;
       const int acc = C::TWO ? 0 : (it & 1);
       const uint32_t acc_phase = C::TWO ? (it & 1) : ((it >> 1) & 1);
+      if constexpr (MODE == 1) {
+        // this tile's scales (and zeros) in shared memory, read as vectors below
+        __syncwarp();  // every lane has read the previous tile's
+        for (int i = lane; i < BN; i += 32) {
+          const int n = n0 + i;
+          const bool in = i < p.bn && n < p.N;
+          wsz[i] = in ? p.scales[n] : (uint16_t)0;
+          if constexpr (ZP) wsz[BN + i] = in ? p.zeros[n] : (uint16_t)0;
+        }
+        __syncwarp();
+      }
       if (!wait_or_abort(&tfull[acc], acc_phase, p, 0xB2100005u, abort_flag)) break;
       tc::fence_after_sync();
       float xs2[2] = {0.f, 0.f};  // W8 with zeros: sum_k x[row, k] of both row halves
@@ -420,17 +451,28 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           const int nc = n0 + c * 32;
           if (row0 >= p.M || nc >= p.N) continue;
           uint32_t packed[16];
+          uint4 sv[4], zv[4];  // MODE 1: the chunk's 32 scales / zeros (16-bit pairs)
+          if constexpr (MODE == 1) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              sv[j] = reinterpret_cast<const uint4*>(wsz + c * 32)[j];
+              if constexpr (ZP) zv[j] = reinterpret_cast<const uint4*>(wsz + BN + c * 32)[j];
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
             if constexpr (MODE == 1) {
-              const int n = nc + 2 * j;
+              float s0, s1;
+              unpack_pair<DT>(word_of(sv, j), s0, s1);
               if constexpr (ZP) {
-                v0 -= (n < p.N ? ld_act<DT>(p.zeros + n) : 0.f) * xs2[h];
-                v1 -= (n + 1 < p.N ? ld_act<DT>(p.zeros + n + 1) : 0.f) * xs2[h];
+                float z0, z1;
+                unpack_pair<DT>(word_of(zv, j), z0, z1);
+                v0 -= z0 * xs2[h];
+                v1 -= z1 * xs2[h];
               }
-              v0 *= n < p.N ? ld_act<DT>(p.scales + n) : 0.f;
-              v1 *= n + 1 < p.N ? ld_act<DT>(p.scales + n + 1) : 0.f;
+              v0 *= s0;
+              v1 *= s1;
             }
             packed[j] = pack_pair<DT>(v0, v1);
           }
