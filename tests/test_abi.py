@@ -68,3 +68,38 @@ def test_caller_output_must_be_a_device_tensor_of_the_right_shape():
         _lib.check_out(torch.empty(2, 3), (2, 3), torch.float32, "op")  # host memory
     with pytest.raises(errors.B2ShapeError):
         _lib.check_out(torch.empty(2, 3, device="meta"), (2, 4), torch.float32, "op")
+
+
+def test_fast_binding_is_built_and_declines_host_tensors():
+    """_b2fast (the C++ argument handling of the per-layer int4 call) loads on
+    a machine without a GPU and hands every case it does not take (here:
+    host tensors) back to the Python operator by returning None."""
+    import torch
+    from b200kern import _lib
+    fast = _lib.fast()
+    assert fast is not None
+    x = torch.zeros(1, 64, dtype=torch.float16)
+    w = torch.zeros(8, 32, dtype=torch.int32)
+    s = torch.zeros(1, 32, dtype=torch.float16)
+    assert fast.int4_matmul(x, w, s, 64, None) is None
+    assert fast.int4_matmul(x.float(), w, s, 64) is None
+
+
+def test_fast_binding_status_raises_the_typed_error(monkeypatch):
+    """A nonzero b2 status from the binding raises the same typed error as the
+    ctypes path (status -> B2Error subclass)."""
+    import pytest
+    import torch
+    import b200kern as bk
+    from b200kern import _lib, errors
+
+    class _Fake:
+        @staticmethod
+        def int4_matmul(*args):
+            return errors.ERR_UNSUPPORTED
+
+    monkeypatch.setattr(_lib, "_fast", _Fake())
+    x = torch.zeros(1, 64, dtype=torch.float16)
+    with pytest.raises(errors.B2UnsupportedError):
+        bk.int4_matmul(x, torch.zeros(8, 32, dtype=torch.int32), torch.zeros(1, 32, dtype=torch.float16),
+                       group_size=64)

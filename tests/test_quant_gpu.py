@@ -309,3 +309,33 @@ def test_int8_fp32_reference_dtype(cuda, zeros, M, N, K):
     assert out.dtype == torch.float32
     ref = oq.int8_matmul(x.double().numpy(), w.numpy(), s.double().numpy(), None if z is None else z.double().numpy())
     _close_f32(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M", [1, 5, 16, 40])
+def test_int4_fast_binding_matches_the_ctypes_path(cuda, monkeypatch, dtype, M):
+    """The C++ binding (_b2fast) and the Python / ctypes path call the same
+    entry point: bit-identical outputs, into a fresh tensor, into a caller's
+    `out`, and (by copy) into an `out` of another dtype."""
+    import b200kern as bk
+    from b200kern import _lib
+    from b200kern.synthetic import w4_inputs
+    assert _lib.fast() is not None
+    N, K, G = 520, 1024, 128
+    d = w4_inputs(M, N, K, G, dtype=dtype, seed=M)
+    x, qw, s = d["x"].to(cuda), d["qweight"].to(cuda), d["scales"].to(cuda)
+    outs = {}
+    for name, fast in (("binding", _lib.fast()), ("ctypes", None)):
+        monkeypatch.setattr(_lib, "_fast", fast)
+        a = bk.int4_matmul(x, qw, s, group_size=G)
+        b = torch.empty(M, N, dtype=dtype, device=cuda)
+        rb = bk.int4_matmul(x, qw, s, group_size=G, out=b)
+        c = torch.empty(M, N, dtype=torch.float32, device=cuda)
+        rc = bk.int4_matmul(x, qw, s, group_size=G, out=c)
+        assert rb is b and rc is c
+        outs[name] = (a, b, c)
+    for u, v in zip(outs["binding"], outs["ctypes"]):
+        assert torch.equal(u, v)
+    ref = oq.int4_matmul(d["x"].double().numpy(), d["q"].numpy(), d["scales"].double().numpy(), None, G)
+    # the GEMM path (M > 16) rounds the dequantised operand: RMS-scaled bound
+    _close_rms(outs["binding"][0].double().cpu().numpy(), ref)

@@ -109,6 +109,26 @@ def strides_arg(t):
     return (ctypes.c_int64 * 3)(*t)
 
 
+_fast = False  # not looked up yet
+
+
+def fast():
+    """The _b2fast binding (C++ argument handling of the per-layer decode
+    call, built by csrc/build.py next to libb2.so and linked against it), or
+    None when it is not built or libb2.so was loaded from another path."""
+    global _fast
+    if _fast is False:
+        _fast = None
+        if os.path.dirname(os.path.abspath(LIB_PATH)) == _HERE:
+            load()
+            try:
+                from . import _b2fast
+                _fast = _b2fast
+            except ImportError:
+                pass
+    return _fast
+
+
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 

@@ -83,7 +83,16 @@ def int4_matmul(input, weight, scales, zeros=None, group_size=128, layout=LAYOUT
     """
     # Common decode / prefill case, straight to the kernel with no conversion
     # or copy.  A decode step issues one of these per layer and the kernel
-    # takes a few microseconds, so this path reads each tensor attribute once.
+    # takes a few microseconds, so the argument checks run in C++ (_b2fast)
+    # when it is built, else here reading each tensor attribute once.
+    if zeros is None and layout == LAYOUT_GPTQ:
+        fast = _lib.fast()
+        if fast is not None:
+            r = fast.int4_matmul(input, weight, scales, group_size, out)
+            if r is not None:
+                if r.__class__ is int:
+                    _lib.check(r, "b2_int4_matmul")
+                return r
     dti = input.dtype
     dt = _DT.get(dti)
     if (dt is not None and zeros is None and layout == LAYOUT_GPTQ and weight.dtype == torch.int32
