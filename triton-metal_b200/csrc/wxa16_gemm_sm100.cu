@@ -108,48 +108,21 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, co
   return false;
 }
 
-// int4 word (k = 8r..8r+7 in nibbles 0..7) -> nibble order 0,2,4,6,1,3,5,7 so
-// that (w >> 4j) & 0x000F000F holds the adjacent pair (k = 2j, 2j+1).
-__device__ __forceinline__ uint32_t unzip_nibbles(uint32_t w) {
-  uint32_t t = ((w >> 4) ^ w) & 0x00F000F0u;  // swap nibbles 1<->2 in each half
-  w ^= t ^ (t << 4);
-  return prmt(w, w, 0x3120);                 // bytes (q0q2)(q1q3)(q4q6)(q5q7) -> (q0q2)(q4q6)(q1q3)(q5q7)
-}
-
 // 8 k-values of one column -> 4 packed pairs (activation dtype) of
-// (q - 8) * s (symmetric) or (q - z) * s (asymmetric).  q is exact: OR-ing it
-// into the mantissa of 128.0 (bf16, ulp 1) or 1024.0 (fp16, ulp 1) gives
-// bias + q.  With zeros, z = zi + zf (zi = rint(z)): subtracting the exact
-// pair bz2 = bias + zi leaves q - zi exactly, and one fma adds the small
-// residual zr2 = -zf * s, so the result is rounded once (plus the rounding
-// of the |zf| <= 1/2 residual).
+// (q - 8) * s (symmetric) or (q - z) * s (asymmetric).  Both layouts hold the
+// pair (k = 2j, 2j + 1) in byte j of a 32-bit word (low nibble, high nibble):
+// a GPTQ int32 (k = 8r .. 8r + 7 in nibbles 0 .. 7) and four bytes of a
+// reference [N, K/2] row.  One PRMT puts byte j of w and of w >> 4 into the
+// two halves, one LOP3 keeps the nibbles and ORs in the bias (9 integer ops
+// per word; a nibble unzip followed by shifts took 12 and measured 1203 TF/s
+// at C2 against 1238).  q is exact: OR-ing it into the mantissa of 128.0
+// (bf16, ulp 1) or 1024.0 (fp16, ulp 1) gives bias + q.  With zeros,
+// z = zi + zf (zi = rint(z)): subtracting the exact pair bz2 = bias + zi
+// leaves q - zi exactly, and one fma adds the small residual zr2 = -zf * s,
+// so the result is rounded once (plus the rounding of the |zf| <= 1/2
+// residual).
 template <int DT, bool ZP>
 __device__ __forceinline__ uint4 dequant8_int4(uint32_t w, uint32_t s2, uint32_t bz2, uint32_t zr2) {
-  const uint32_t u = unzip_nibbles(w);
-  constexpr uint32_t kBias = DT == B2_BF16 ? 0x43004300u : 0x64006400u;
-  constexpr uint32_t kBias8 = DT == B2_BF16 ? 0x43084308u : 0x64086408u;
-  uint32_t r[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t biased = and_or(u >> (4 * j), 0x000F000Fu, kBias);
-    if constexpr (!ZP) {
-      const uint32_t v = sub2<DT>(biased, kBias8);  // q - 8, exact
-      if constexpr (DT == B2_BF16) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
-      else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[j]) : "r"(v), "r"(s2));
-    } else {
-      const uint32_t v = sub2<DT>(biased, bz2);     // q - zi, exact
-      if constexpr (DT == B2_BF16) asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
-      else asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r[j]) : "r"(v), "r"(s2), "r"(zr2));
-    }
-  }
-  return make_uint4(r[0], r[1], r[2], r[3]);
-}
-
-// Reference layout: byte j of w holds k = 2j (low nibble) and 2j + 1 (high
-// nibble), already a k-ordered pair: one PRMT puts byte j of w and of w >> 4
-// into the two halves, one LOP3 keeps the nibbles and ORs in the bias.
-template <int DT, bool ZP>
-__device__ __forceinline__ uint4 dequant8_int4_ref(uint32_t w, uint32_t s2, uint32_t bz2, uint32_t zr2) {
   constexpr uint32_t kBias = DT == B2_BF16 ? 0x43004300u : 0x64006400u;
   constexpr uint32_t kBias8 = DT == B2_BF16 ? 0x43084308u : 0x64086408u;
   const uint32_t w4 = w >> 4;
@@ -556,7 +529,7 @@ wxa16_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           const uint32_t wv[4] = {pv.x, pv.y, pv.z, pv.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const uint4 v = dequant8_int4_ref<DT, ZP>(wv[i], s2, bz2, zr2);
+            const uint4 v = dequant8_int4<DT, ZP>(wv[i], s2, bz2, zr2);
             *reinterpret_cast<uint4*>(brow + (((4 * h + i) ^ sw) << 4)) = v;
           }
         } else {
