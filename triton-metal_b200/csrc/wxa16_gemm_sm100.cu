@@ -181,13 +181,26 @@ __device__ __forceinline__ uint32_t splat(float v) {
 // 4 int8 -> 2 packed pairs (activation dtype), exact.
 template <int DT>
 __device__ __forceinline__ void int8x4_to_act(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7650)) - 8388736.f;
-  const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7651)) - 8388736.f;
-  const float f2 = __uint_as_float(prmt(u, 0x4B000000u, 0x7652)) - 8388736.f;
-  const float f3 = __uint_as_float(prmt(u, 0x4B000000u, 0x7653)) - 8388736.f;
-  lo = pack_pair<DT>(f0, f1);
-  hi = pack_pair<DT>(f2, f3);
+  // bytes (0, 1) and (2, 3) of w into the low bytes of the two 16-bit halves
+  const uint32_t p[2] = {prmt(w, 0u, 0x4140u), prmt(w, 0u, 0x4342u)};
+  uint32_t r[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    if constexpr (DT == B2_BF16) {
+      // bf16 holds 128 + m (m = the byte's low 7 bits) exactly; the byte's
+      // sign bit selects 128 (w >= 0: w = m) or 256 (w < 0: w = m - 128) to
+      // subtract, so the difference is the exact integer w
+      r[i] = sub2<DT>(and_or(p[i], 0x007F007Fu, 0x43004300u), and_or(p[i], 0x00800080u, 0x43004300u));
+    } else {
+      // fp16 holds 1024 + (w + 128) exactly: (byte ^ 0x80) | 0x6400, then
+      // subtract 1152
+      uint32_t t;
+      asm("lop3.b32 %0, %1, %2, %3, 0xBE;" : "=r"(t) : "r"(p[i]), "r"(0x00800080u), "r"(0x64006400u));
+      r[i] = sub2<DT>(t, 0x64806480u);
+    }
+  }
+  lo = r[0];
+  hi = r[1];
 }
 
 // fp32 sum of 8 packed activation values.
